@@ -1,0 +1,646 @@
+"""Benchmark of the B200 block-sparse attention path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload: block-sparse prefill forward+backward, bf16,
+B=1, 32 query heads / 8 KV heads (GQA), D=128, N=8192, route block 128 (64x64 block grid),
+tree routing of depth 6 with a per-head LCA threshold drawn from {1..6} (seeded), causal,
+sink block kept.  A step = build the block lists + forward + backward (Delta/transposed
+lists, dQ, dK/dV), each a C-ABI launch timed with CUDA events on the launching stream;
+L2 is flushed (a 256 MiB write) between steps, outside the events.  ``value`` is kept-block
+TFLOP/s: kept (query block, key block) pairs x (4 + 10) * RB^2 * D / step time.
+
+Also reported: ``e2e`` (same metric through the public ``block_list_attention`` autograd API
+with pinned host buffers, H2D of q/k/v/dO and D2H of out/dq/dk/dv inside the timed region),
+the 50 / 90 / 98.4 % sparsity sweep with dense SDPA beside it, the C3 routed paged decode
+(tok/s and GB/s of routed bytes), the roofline of the dominant kernel, sampled SM clocks,
+and the reference's CPU path (masked dense fp32 attention) timed on a bounded head sample.
+
+Multi-GPU (torchrun, one rank per GPU): each rank runs its own C2 head group and its own 64
+decode requests, no data-path collective (weak scaling); times are the max over ranks.
+``--impl reference`` times the reference's CPU path alone (rank 0; other ranks exit).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "sparse-ai_b200"))
+
+import torch  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# C2 configuration
+C2 = dict(Z=1, H=32, Hkv=8, N=8192, D=128, RB=128, TD=6)
+
+
+# ---------------------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------------------
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def tree_router(Z, H, NB, TD):
+    depth = max(1, math.ceil(math.log2(max(NB, 2))))
+    r = torch.zeros(Z, H, NB, TD, dtype=torch.int32)
+    for d in range(min(depth, TD)):
+        r[:, :, :, d] = (torch.arange(NB) >> (depth - 1 - d)) % 2
+    return r
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.samples = []
+        if self.proc is None:
+            return False
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+        return False
+
+    def summary(self):
+        if not getattr(self, "samples", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i] == "Active"})
+        loaded = [x for x in sm if x > 500] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------------------
+# the reference's CPU path (bounded sample), used by cpu_baseline and --impl reference
+# ---------------------------------------------------------------------------------------
+
+def c2_masks(t_heads, causal, sink):
+    from oracle import block_list_oracle as blo
+    H, NB, TD = C2["H"], C2["N"] // C2["RB"], C2["TD"]
+    router = tree_router(1, H, NB, TD).numpy()
+    return torch.from_numpy(blo.block_mask(router, t_heads, is_causal=causal, sink_block=sink))
+
+
+def c2_thresholds(seed=0):
+    g = torch.Generator().manual_seed(1000 + seed)
+    return torch.randint(1, 7, (C2["H"],), generator=g).tolist()
+
+
+def cpu_reference_sample(heads=(0, 1), causal=True, sink=True, seed=0, t_heads=None):
+    """Masked dense fp32 attention forward + autograd backward on the CPU for a head subset
+    of C2 (query-chunked, benchmarks/benchmark_block_list.py:106-123 of the reference).
+    Returns (seconds, n_heads)."""
+    from oracle import attention_oracle as ao
+    N, D, RB = C2["N"], C2["D"], C2["RB"]
+    t_heads = t_heads if t_heads is not None else c2_thresholds(seed)
+    bm = c2_masks(t_heads, causal, sink)
+    gen = torch.Generator().manual_seed(seed)
+    group = C2["H"] // C2["Hkv"]
+    kv_heads = sorted({h // group for h in heads})
+    q = torch.randn(1, len(heads), N, D, generator=gen).bfloat16().float().requires_grad_(True)
+    k = torch.randn(1, len(kv_heads), N, D, generator=gen).bfloat16().float().requires_grad_(True)
+    v = torch.randn(1, len(kv_heads), N, D, generator=gen).bfloat16().float().requires_grad_(True)
+    do = torch.randn(1, len(heads), N, D, generator=gen).bfloat16().float()
+    bm_sub = bm[:, list(heads)]
+    t0 = time.perf_counter()
+    outs = []
+    for hi, h in enumerate(heads):
+        kh = kv_heads.index(h // group)
+        o, _ = ao.masked_attention_chunked(q[:, hi:hi + 1], k[:, kh:kh + 1], v[:, kh:kh + 1],
+                                           bm_sub[:, hi:hi + 1], RB, causal, chunk=2048,
+                                           compute_dtype=torch.float32)
+        outs.append(o)
+    out = torch.cat(outs, dim=1)
+    out.backward(do)
+    t1 = time.perf_counter()
+    return t1 - t0, len(heads)
+
+
+def kept_flops_c2(t_heads, causal, sink, fwd=True, bwd=True):
+    bm = c2_masks(t_heads, causal, sink)
+    kept = int(bm.sum())
+    RB, D = C2["RB"], C2["D"]
+    per = (4 if fwd else 0) + (10 if bwd else 0)
+    return kept, kept * per * RB * RB * D
+
+
+def run_reference_arm(args):
+    world, rank, _ = dist_setup(args.gpus)
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    t_heads = c2_thresholds(0)
+    kept, flops = kept_flops_c2(t_heads, True, True)
+    heads = (0, 1)
+    for _ in range(args.warmup):
+        cpu_reference_sample(heads, t_heads=t_heads)
+    times = []
+    for _ in range(args.steps):
+        s, nh = cpu_reference_sample(heads, t_heads=t_heads)
+        times.append(s * C2["H"] / nh)
+    step = statistics.mean(times)
+    value = flops * args.gpus / step / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_c2(args.gpus, t_heads, kept),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"masked dense fp32 attention fwd+bwd (autograd) on {len(heads)} of "
+                                   f"{C2['H']} heads of C2, full N=8192, scaled x{C2['H'] // len(heads)}"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "sparse prefill fwd+bwd kept-block TFLOP/s (C2 bf16 N=8192 H=32/8 D=128)"
+
+
+def config_c2(n_gpus, t_heads, kept):
+    NB = C2["N"] // C2["RB"]
+    return {"workload": "C2 block-sparse prefill fwd+bwd, tree routes depth 6, per-head LCA "
+                        "threshold ~U{1..6}, causal + sink",
+            "batch_per_gpu": 1, "heads": C2["H"], "kv_heads": C2["Hkv"], "seq_len": C2["N"],
+            "head_dim": C2["D"], "route_block": C2["RB"], "thresholds": t_heads,
+            "kept_blocks": kept,
+            "sparsity_full_grid": 1 - kept / (C2["H"] * NB * NB),
+            "sparsity_causal": 1 - kept / (C2["H"] * NB * (NB + 1) / 2),
+            "parallelism": f"heads sharded, {n_gpus} x (32 q / 8 kv heads), no collective",
+            "l2": "flushed between steps (256 MiB write)",
+            "flops_per_kept_pair": "fwd 4*RB^2*D + bwd 10*RB^2*D"}
+
+
+# ---------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------
+
+class C2Problem:
+    """Device-resident C2 inputs and the direct C-ABI step (build, fwd, bwd phases)."""
+
+    def __init__(self, dev, seed, t_heads, causal=True, sink=True):
+        from ultrametric import _native as nat
+        self.nat = nat
+        self.dev = dev
+        Z, H, Hkv, N, D, RB, TD = (C2[k] for k in ("Z", "H", "Hkv", "N", "D", "RB", "TD"))
+        self.NB = N // RB
+        gen = torch.Generator().manual_seed(seed)
+        self.h_q = torch.randn(Z, H, N, D, generator=gen).bfloat16().pin_memory()
+        self.h_k = torch.randn(Z, Hkv, N, D, generator=gen).bfloat16().pin_memory()
+        self.h_v = torch.randn(Z, Hkv, N, D, generator=gen).bfloat16().pin_memory()
+        self.h_do = torch.randn(Z, H, N, D, generator=gen).bfloat16().pin_memory()
+        self.q, self.k, self.v, self.do = (t.to(dev) for t in (self.h_q, self.h_k, self.h_v, self.h_do))
+        self.router = tree_router(Z, H, self.NB, TD).to(dev)
+        self.t_heads = list(t_heads)
+        self.depth = torch.tensor(self.t_heads, dtype=torch.int32, device=dev)
+        self.causal, self.sink = causal, sink
+        self.scale = 1.0 / math.sqrt(D)
+        NB = self.NB
+        self.lists = torch.empty(Z, H, NB, NB, dtype=torch.int32, device=dev)
+        self.counts = torch.empty(Z, H, NB, dtype=torch.int32, device=dev)
+        self.out = torch.empty_like(self.q)
+        self.lse = torch.empty(Z, H, N, dtype=torch.float32, device=dev)
+        self.dq = torch.empty_like(self.q)
+        self.dk = torch.empty_like(self.k)
+        self.dv = torch.empty_like(self.v)
+        wsb = int(nat.lib().sa_block_list_attention_bwd_workspace_bytes(Z, H, N, RB))
+        self.ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        self.build()
+        torch.cuda.synchronize()
+        self.kept = int(self.counts.sum())
+        RB2D = RB * RB * D
+        self.flops = {"fwd": self.kept * 4 * RB2D, "dq": self.kept * 6 * RB2D,
+                      "dkdv": self.kept * 8 * RB2D}
+        self.flops_alg = self.kept * 14 * RB2D
+        # compulsory bytes of the forward: Q, O, LSE and each referenced K/V block once per KV head
+        NBK = NB
+        ref_kv = torch.zeros(Z, Hkv, NBK, dtype=torch.bool, device=dev)
+        group = H // Hkv
+        for h in range(H):
+            c = self.counts[0, h]
+            m = torch.arange(NB, device=dev).view(1, -1) < c.view(-1, 1)
+            ref_kv[0, h // group].index_put_((self.lists[0, h][m].long(),), torch.tensor(True, device=dev))
+        self.fwd_bytes = (2 * self.q.numel() * 2 + self.lse.numel() * 4 +
+                          int(ref_kv.sum()) * RB * D * 2 * 2)
+
+    def build(self):
+        nat, s = self.nat, torch.cuda.current_stream().cuda_stream
+        Z, H, NB = 1, C2["H"], self.NB
+        nat.check(nat.lib().sa_build_block_lists(
+            self.router.data_ptr(), nat.SA_I32, nat.strides(self.router), Z, H, NB, C2["TD"],
+            self.depth.data_ptr(), 2, 1, int(self.causal), int(self.sink), 0,
+            self.lists.data_ptr(), NB, self.counts.data_ptr(), s), "build")
+
+    def fwd(self):
+        nat, s = self.nat, torch.cuda.current_stream().cuda_stream
+        Z, H, Hkv, N, D, RB = (C2[k] for k in ("Z", "H", "Hkv", "N", "D", "RB"))
+        nat.check(nat.lib().sa_block_list_attention_fwd(
+            nat.SA_BF16, Z, H, Hkv, N, D, RB, self.q.data_ptr(), nat.strides(self.q),
+            self.k.data_ptr(), nat.strides(self.k), self.v.data_ptr(), nat.strides(self.v),
+            self.out.data_ptr(), nat.strides(self.out), self.lse.data_ptr(),
+            self.lists.data_ptr(), self.NB, self.counts.data_ptr(), None, 0, None,
+            int(self.causal), self.scale, s), "fwd")
+
+    def bwd(self, phase):
+        nat, s = self.nat, torch.cuda.current_stream().cuda_stream
+        Z, H, Hkv, N, D, RB = (C2[k] for k in ("Z", "H", "Hkv", "N", "D", "RB"))
+        nat.check(nat.lib().sa_block_list_attention_bwd_phase(
+            phase, nat.SA_BF16, Z, H, Hkv, N, D, RB, self.q.data_ptr(), nat.strides(self.q),
+            self.k.data_ptr(), nat.strides(self.k), self.v.data_ptr(), nat.strides(self.v),
+            self.out.data_ptr(), nat.strides(self.out), self.do.data_ptr(), nat.strides(self.do),
+            self.lse.data_ptr(), self.lists.data_ptr(), self.NB, self.counts.data_ptr(),
+            None, 0, None, int(self.causal), self.scale,
+            self.dq.data_ptr(), nat.strides(self.dq), self.dk.data_ptr(), nat.strides(self.dk),
+            self.dv.data_ptr(), nat.strides(self.dv), None, self.ws.data_ptr(), self.ws.numel(), s),
+            f"bwd phase {phase}")
+
+    PARTS = ("build", "fwd", "prep", "dq", "dkdv")
+    LAUNCHES = {"build": 1, "fwd": 1, "prep": 2, "dq": 1, "dkdv": 1}
+
+    def step(self, evs):
+        evs[0].record()
+        self.build()
+        evs[1].record()
+        self.fwd()
+        evs[2].record()
+        self.bwd(1)
+        evs[3].record()
+        self.bwd(2)
+        evs[4].record()
+        self.bwd(3)
+        evs[5].record()
+
+
+def flush_l2(buf):
+    buf.zero_()
+
+
+def time_c2(prob, steps, warmup, flush, barrier=None):
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
+    for _ in range(warmup):
+        flush_l2(flush)
+        prob.step([torch.cuda.Event(enable_timing=True) for _ in range(6)])
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        flush_l2(flush)
+        prob.step(evs[i])
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    torch.cuda.synchronize()
+    parts = {p: [] for p in C2Problem.PARTS}
+    totals = []
+    for e in evs:
+        for j, p in enumerate(C2Problem.PARTS):
+            parts[p].append(e[j].elapsed_time(e[j + 1]))
+        totals.append(e[0].elapsed_time(e[5]))
+    return sum(totals), {p: statistics.mean(v) for p, v in parts.items()}
+
+
+def time_e2e(prob, steps, warmup):
+    """Public API end to end: pinned host -> device, block_list_attention autograd fwd+bwd,
+    out/dq/dk/dv -> pinned host, per step."""
+    from ultrametric import block_list_attention, build_block_lists
+    dev = prob.dev
+    h_out = torch.empty_like(prob.h_q).pin_memory()
+    h_dq = torch.empty_like(prob.h_q).pin_memory()
+    h_dk = torch.empty_like(prob.h_k).pin_memory()
+    h_dv = torch.empty_like(prob.h_v).pin_memory()
+    h_router = prob.router.cpu().pin_memory()
+
+    def one():
+        q = prob.h_q.to(dev, non_blocking=True).requires_grad_(True)
+        k = prob.h_k.to(dev, non_blocking=True).requires_grad_(True)
+        v = prob.h_v.to(dev, non_blocking=True).requires_grad_(True)
+        do = prob.h_do.to(dev, non_blocking=True)
+        r = h_router.to(dev, non_blocking=True)
+        bl = build_block_lists(r, prob.t_heads, is_causal=prob.causal, sink_block=prob.sink, arity=2)
+        out = block_list_attention(q, k, v, bl, route_block=C2["RB"], is_causal=prob.causal)
+        out.backward(do)
+        h_out.copy_(out.detach(), non_blocking=True)
+        h_dq.copy_(q.grad, non_blocking=True)
+        h_dk.copy_(k.grad, non_blocking=True)
+        h_dv.copy_(v.grad, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        one()
+        e1.record()
+        e1.synchronize()
+        total += e0.elapsed_time(e1)
+    h2d = sum(t.numel() * t.element_size() for t in (prob.h_q, prob.h_k, prob.h_v, prob.h_do, h_router))
+    d2h = sum(t.numel() * t.element_size() for t in (h_out, h_dq, h_dk, h_dv))
+    return total / steps, h2d, d2h
+
+
+def time_sdpa(prob, causal, steps=5):
+    import torch.nn.functional as F
+    q = prob.q.detach().requires_grad_(True)
+    k = prob.k.detach().requires_grad_(True)
+    v = prob.v.detach().requires_grad_(True)
+
+    def fwd():
+        return F.scaled_dot_product_attention(q, k, v, is_causal=causal, enable_gqa=True)
+
+    res = {}
+    try:
+        for _ in range(2):
+            fwd()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            with torch.no_grad():
+                fwd()
+        e1.record()
+        e1.synchronize()
+        res["fwd_ms"] = e0.elapsed_time(e1) / steps
+        for _ in range(2):
+            fwd().backward(prob.do)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            fwd().backward(prob.do)
+        e1.record()
+        e1.synchronize()
+        res["fwd_bwd_ms"] = e0.elapsed_time(e1) / steps
+    except Exception as ex:  # pragma: no cover - depends on the torch build
+        res["error"] = f"{type(ex).__name__}: {str(ex)[:120]}"
+    return res
+
+
+def run_sweep(dev, flush, steps):
+    NB = C2["N"] // C2["RB"]
+    rows = []
+    for name, t, causal, sink in (("50%", 1, True, True), ("90%", 4, True, True),
+                                  ("98.4%", 6, False, False)):
+        prob = C2Problem(dev, 0, [t] * C2["H"], causal=causal, sink=sink)
+        total, parts = time_c2(prob, steps, 2, flush)
+        ms = total / steps
+        kept = prob.kept
+        fwd_tf = prob.flops["fwd"] / (parts["fwd"] * 1e-3) / 1e12
+        bwd_ms = parts["prep"] + parts["dq"] + parts["dkdv"]
+        sd = time_sdpa(prob, causal)
+        rows.append({
+            "target": name, "threshold": t, "causal": causal, "sink": sink, "kept_blocks": kept,
+            "sparsity_full_grid": round(1 - kept / (C2["H"] * NB * NB), 4),
+            "sparsity_causal": round(1 - kept / (C2["H"] * NB * (NB + 1) / 2), 4),
+            "step_ms": round(ms, 4), "fwd_ms": round(parts["fwd"], 4), "bwd_ms": round(bwd_ms, 4),
+            "build_ms": round(parts["build"], 4),
+            "fwd_kept_tflops": round(fwd_tf, 2),
+            "fwd_bwd_kept_tflops": round(prob.flops_alg / (ms * 1e-3) / 1e12, 2),
+            "dense_sdpa": sd,
+            "speedup_fwd_vs_sdpa": round(sd["fwd_ms"] / parts["fwd"], 2) if "fwd_ms" in sd else None,
+        })
+        del prob
+        torch.cuda.empty_cache()
+    return rows
+
+
+def run_decode(dev, seed, steps, warmup, flush, peaks):
+    """C3: 64 requests, H=32/8, D=128, page 64, ctx ~U[2048, 32768], shuffled pool,
+    tree routes on the logical page index (depth 9), random query leaf, req_depth 4,
+    sink + most recent page."""
+    from ultrametric import ultrametric_decode
+    B, H, Hkv, D, page, TD = 64, 32, 8, 128, 64, 9
+    gen = torch.Generator().manual_seed(10 + seed)
+    ctx = torch.randint(2048, 32769, (B,), generator=gen, dtype=torch.int32)
+    n_log = (ctx + page - 1) // page
+    maxL = int(n_log.max())
+    total = int(n_log.sum()) + 16
+    perm = torch.randperm(total, generator=gen).to(torch.int32)
+    bt = torch.zeros(B, maxL, dtype=torch.int32)
+    logical_of = torch.zeros(total, dtype=torch.int64)
+    off = 0
+    for b in range(B):
+        n = int(n_log[b])
+        bt[b, :n] = perm[off:off + n]
+        logical_of[perm[off:off + n].long()] = torch.arange(n)
+        off += n
+    bits = ((logical_of.view(-1, 1) >> torch.arange(TD - 1, -1, -1).view(1, -1)) & 1).to(torch.int32)
+    ri = bits.view(total, 1, TD).expand(total, H, TD).contiguous()
+    leaf = torch.randint(0, 1 << TD, (B,), generator=gen)
+    qbits = ((leaf.view(-1, 1) >> torch.arange(TD - 1, -1, -1).view(1, -1)) & 1).to(torch.int32)
+    qri = qbits.view(B, 1, TD).expand(B, H, TD).contiguous()
+    g = torch.Generator(device=dev).manual_seed(20 + seed)
+    kc = torch.randn(total, Hkv, page, D, generator=g, device=dev, dtype=torch.bfloat16)
+    vc = torch.randn(total, Hkv, page, D, generator=g, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(B, H, D, generator=g, device=dev, dtype=torch.bfloat16)
+    btd, ctxd, rid, qrid = bt.to(dev), ctx.to(dev), ri.to(dev), qri.to(dev)
+    # routed bytes (routes are shared by the heads of a group): selected pages x valid tokens
+    rd, local = 4, 1
+    sel_tokens = 0
+    sel_pages = 0
+    for b in range(B):
+        n = int(n_log[b])
+        lp = torch.arange(n)
+        match = (bits[lp][:, :rd] == qbits[b, :rd]).all(-1)
+        match[0] = True
+        match[max(0, n - local):] = True
+        valid = torch.clamp(int(ctx[b]) - lp * page, max=page)
+        sel_tokens += int(valid[match].sum())
+        sel_pages += int(match.sum())
+    kv_bytes = sel_tokens * Hkv * D * 2 * 2
+    qo_bytes = 2 * B * H * D * 2
+    routed_bytes = kv_bytes + qo_bytes
+
+    def one():
+        return ultrametric_decode(q, kc, vc, btd, ctxd, rid, qrid, rd, local_blocks=local, sink_block=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(steps):
+        flush_l2(flush)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        one()
+        e1.record()
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    ms = tot / steps
+    gbs = routed_bytes / (ms * 1e-3) / 1e9
+    dense_bytes = int(n_log.sum()) * page * Hkv * D * 2 * 2
+    return {
+        "config": "C3: 64 req x 1 token, H=32/8, D=128, page 64, ctx~U[2048,32768], req_depth 4, sink+last page",
+        "ms_per_step": round(ms, 4), "tok_per_s": round(B / (ms * 1e-3), 1),
+        "routed_gbs": round(gbs, 1), "routed_bytes": routed_bytes, "routed_pages": sel_pages,
+        "dense_equivalent_bytes": dense_bytes,
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
+        "gpu_launches_per_step": 2,
+    }
+
+
+def run_ours(args):
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    barrier = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+        def barrier():
+            dist.barrier()
+    peaks, peak_kind = load_peaks()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    t_heads = c2_thresholds(0)
+    prob = C2Problem(dev, seed=rank, t_heads=t_heads)
+    with ClockSampler(local) as clk:
+        total_ms, parts = time_c2(prob, args.steps, args.warmup, flush, barrier)
+    my = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(my, op=dist.ReduceOp.MAX)
+    total_ms = float(my.item())
+    ms_step = total_ms / args.steps
+    value = prob.flops_alg * world / (ms_step * 1e-3) / 1e12
+
+    # dominant kernel roofline (tensor-bound kernels of the step)
+    kern = max(("fwd", "dq", "dkdv"), key=lambda p: parts[p])
+    achieved = prob.flops[kern] / (parts[kern] * 1e-3) / 1e12
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as f:
+            traffic = json.load(f).get(kern)
+
+    e2e_ms, h2d, d2h = time_e2e(prob, max(3, args.steps // 2), 2)
+    e2e_value = prob.flops_alg * world / (e2e_ms * 1e-3) / 1e12
+
+    extras = {}
+    if not args.quick:
+        extras["sweep"] = run_sweep(dev, flush, steps=5)
+        extras["decode"] = run_decode(dev, rank, args.steps, args.warmup, flush, peaks)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        torch.set_num_threads(os.cpu_count() or 1)
+        s, nh = cpu_reference_sample((0, 1), t_heads=t_heads)
+        cpu_step = s * C2["H"] / nh
+        cpu = {"value": prob.flops_alg / cpu_step / 1e12, "unit": "TFLOP/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"masked dense fp32 attention fwd+bwd (autograd), 2 of 32 heads of C2 at "
+                         f"N=8192, {s:.2f} s, scaled x16 to {cpu_step:.1f} s per step"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": config_c2(world, t_heads, prob.kept),
+            "breakdown_ms": {p: round(v, 4) for p, v in parts.items()},
+            "roofline": {"bound": "tensor", "kernel": kern, "achieved": round(achieved, 2),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
+                         "peak_source": f"{peak_kind} bf16 burst",
+                         "flops_per_launch": prob.flops[kern],
+                         "fwd": {"ms": round(parts["fwd"], 4),
+                                 "tflops": round(prob.flops["fwd"] / (parts["fwd"] * 1e-3) / 1e12, 2),
+                                 "hbm_gbs": round(prob.fwd_bytes / (parts["fwd"] * 1e-3) / 1e9, 1),
+                                 "compulsory_bytes": prob.fwd_bytes}},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 3),
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "ultrametric.block_list_attention autograd (ctypes -> C ABI)"},
+            "clocks": clk.summary(),
+            "gpu_launches": sum(C2Problem.LAUNCHES.values()) * args.steps,
+            **extras,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--quick", action="store_true", help="headline only (no sweep / decode)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

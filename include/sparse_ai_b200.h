@@ -154,6 +154,34 @@ SA_API int sa_block_list_attention_bwd(int dtype, int64_t Z, int64_t H, int64_t 
                                 float* d_soft_bias,
                                 void* workspace, int64_t workspace_bytes, void* stream);
 
+/*
+ * The backward split at the reference's own launch boundaries, for callers that schedule
+ * or time the pieces separately (same arguments as sa_block_list_attention_bwd; the
+ * workspace must persist from phase 1 to phases 2 and 3):
+ *   phase 0  everything (== sa_block_list_attention_bwd)
+ *   phase 1  Delta = rowsum(dO * O) and the transposed lists with slots
+ *            (block_list.py:785 and :844-846), zeroes d_soft_bias
+ *   phase 2  dQ and d_soft_bias (the _block_list_bwd_dq_kernel launch, block_list.py:811-842)
+ *   phase 3  dK and dV (the _block_list_bwd_dkdv_kernel launch, block_list.py:844-876)
+ */
+SA_API int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H,
+                                      int64_t Hkv, int64_t N, int64_t D, int64_t route_block,
+                                      const void* q, const int64_t* q_strides,
+                                      const void* k, const int64_t* k_strides,
+                                      const void* v, const int64_t* v_strides,
+                                      const void* out, const int64_t* out_strides,
+                                      const void* dout, const int64_t* dout_strides,
+                                      const float* lse,
+                                      const int32_t* lists, int64_t list_stride,
+                                      const int32_t* counts,
+                                      const void* soft_bias, int sb_dtype, const int64_t* sb_strides,
+                                      int is_causal, float sm_scale,
+                                      void* dq, const int64_t* dq_strides,
+                                      void* dk, const int64_t* dk_strides,
+                                      void* dv, const int64_t* dv_strides,
+                                      float* d_soft_bias,
+                                      void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Bytes of workspace sa_ultrametric_decode needs for these sizes. */
 SA_API int64_t sa_ultrametric_decode_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t D,
                                               int64_t max_logical_pages);

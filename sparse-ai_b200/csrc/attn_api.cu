@@ -99,8 +99,8 @@ int64_t sa_block_list_attention_bwd_workspace_bytes(int64_t Z, int64_t H, int64_
   return (int64_t)b;
 }
 
-int sa_block_list_attention_bwd(int dtype, int64_t Z, int64_t H, int64_t Hkv, int64_t N,
-                                int64_t D, int64_t route_block, const void* q,
+int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H, int64_t Hkv,
+                                      int64_t N, int64_t D, int64_t route_block, const void* q,
                                 const int64_t* q_strides, const void* k, const int64_t* k_strides,
                                 const void* v, const int64_t* v_strides, const void* out,
                                 const int64_t* out_strides, const void* dout,
@@ -158,19 +158,43 @@ int sa_block_list_attention_bwd(int dtype, int64_t Z, int64_t H, int64_t Hkv, in
   p.k_slots = k_slots;
   p.q_counts = q_counts;
 
-  rc = launch_delta(p, s);
-  if (rc) return rc;
-  rc = launch_transpose_lists(lists, list_stride, counts, Z * H, NB, NB, k_lists, NB, q_counts,
-                              k_slots, 0, s);
-  if (rc) return rc;
-  if (d_soft_bias) {
-    if (cudaMemsetAsync(d_soft_bias, 0, (size_t)Z * H * NB * list_stride * sizeof(float), s) !=
-        cudaSuccess)
-      return check_launch("memset d_soft_bias");
+  if (phase < 0 || phase > 3) return fail(SA_EINVAL, "backward phase must be 0..3");
+  if (phase == 0 || phase == 1) {
+    rc = launch_delta(p, s);
+    if (rc) return rc;
+    rc = launch_transpose_lists(lists, list_stride, counts, Z * H, NB, NB, k_lists, NB, q_counts,
+                                k_slots, 0, s);
+    if (rc) return rc;
+    if (d_soft_bias) {
+      if (cudaMemsetAsync(d_soft_bias, 0, (size_t)Z * H * NB * list_stride * sizeof(float), s) !=
+          cudaSuccess)
+        return check_launch("memset d_soft_bias");
+    }
   }
-  rc = launch_bwd_sm100(p, s);
+  const int parts = phase == 0 ? (kBwdDq | kBwdDkDv) : phase == 2 ? kBwdDq : phase == 3 ? kBwdDkDv : 0;
+  if (!parts) return SA_OK;
+  rc = launch_bwd_sm100(p, s, parts);
   if (rc != SA_EUNSUPPORTED) return rc;
-  return launch_bwd_simt(p, s);
+  return launch_bwd_simt(p, s, parts);
+}
+
+int sa_block_list_attention_bwd(int dtype, int64_t Z, int64_t H, int64_t Hkv, int64_t N,
+                                int64_t D, int64_t route_block, const void* q,
+                                const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                const void* v, const int64_t* v_strides, const void* out,
+                                const int64_t* out_strides, const void* dout,
+                                const int64_t* dout_strides, const float* lse,
+                                const int32_t* lists, int64_t list_stride, const int32_t* counts,
+                                const void* soft_bias, int sb_dtype, const int64_t* sb_strides,
+                                int is_causal, float sm_scale, void* dq,
+                                const int64_t* dq_strides, void* dk, const int64_t* dk_strides,
+                                void* dv, const int64_t* dv_strides, float* d_soft_bias,
+                                void* workspace, int64_t workspace_bytes, void* stream) {
+  return sa_block_list_attention_bwd_phase(
+      0, dtype, Z, H, Hkv, N, D, route_block, q, q_strides, k, k_strides, v, v_strides, out,
+      out_strides, dout, dout_strides, lse, lists, list_stride, counts, soft_bias, sb_dtype,
+      sb_strides, is_causal, sm_scale, dq, dq_strides, dk, dk_strides, dv, dv_strides,
+      d_soft_bias, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -4,6 +4,6 @@
 
 namespace sa {
 
-int launch_bwd_sm100(const AttnParams&, cudaStream_t) { return SA_EUNSUPPORTED; }
+int launch_bwd_sm100(const AttnParams&, cudaStream_t, int) { return SA_EUNSUPPORTED; }
 
 }  // namespace sa

@@ -387,7 +387,9 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
   int rc = make_tmap_4d(&a.tm_q, p.q, p.dtype, p.Z, p.H, p.N, D, p.qs, 64, kT);
   if (!rc) rc = make_tmap_4d(&a.tm_k, p.k, p.dtype, p.Z, p.Hkv, p.N, D, p.ks, 64, kT);
   if (!rc) rc = make_tmap_4d(&a.tm_v, p.v, p.dtype, p.Z, p.Hkv, p.N, D, p.vs, 64, kT);
-  if (rc) return rc;
+  // The shape passed the eligibility checks: a failure here is an error, never a silent
+  // hand-off to the CUDA-core kernel.
+  if (rc) return fail(SA_ELAUNCH, std::string("forward tensor maps: ") + sa_last_error());
   a.Z = p.Z;
   a.H = p.H;
   a.Hkv = p.Hkv;

@@ -42,8 +42,11 @@ struct AttnParams {
   unsigned* status;
 };
 
+// backward parts (bitmask)
+constexpr int kBwdDq = 1, kBwdDkDv = 2;
+
 int launch_fwd_simt(const AttnParams& p, cudaStream_t stream);
-int launch_bwd_simt(const AttnParams& p, cudaStream_t stream);
+int launch_bwd_simt(const AttnParams& p, cudaStream_t stream, int parts);
 int launch_delta(const AttnParams& p, cudaStream_t stream);
 int launch_transpose_lists(const int32_t* lists, int64_t list_stride, const int32_t* counts,
                            int64_t ZH, int64_t NBQ, int64_t NBK, int32_t* k_lists,
@@ -51,6 +54,6 @@ int launch_transpose_lists(const int32_t* lists, int64_t list_stride, const int3
                            cudaStream_t stream);
 // tcgen05 kernels: return SA_EUNSUPPORTED (without launching) for shapes they do not take.
 int launch_fwd_sm100(const AttnParams& p, cudaStream_t stream);
-int launch_bwd_sm100(const AttnParams& p, cudaStream_t stream);
+int launch_bwd_sm100(const AttnParams& p, cudaStream_t stream, int parts);
 
 }  // namespace sa

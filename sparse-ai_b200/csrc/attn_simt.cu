@@ -352,8 +352,8 @@ int launch_fwd_t(const AttnParams& p, cudaStream_t s) {
 }
 
 template <typename T, int D>
-int launch_bwd_t(const AttnParams& p, cudaStream_t s) {
-  {
+int launch_bwd_t(const AttnParams& p, cudaStream_t s, int parts) {
+  if (parts & kBwdDq) {
     const size_t smem = (size_t)(2 * kBM * D + 2 * 32 * (D + 1)) * sizeof(float);
     auto kern = dq_simt_kernel<T, D>;
     if (smem > 48 * 1024)
@@ -363,7 +363,7 @@ int launch_bwd_t(const AttnParams& p, cudaStream_t s) {
     int rc = check_launch("dq_simt_kernel");
     if (rc) return rc;
   }
-  {
+  if (parts & kBwdDkDv) {
     const size_t smem = (size_t)(2 * kBMQ * (D + 1) + 2 * kBNK * D + 2 * kBMQ) * sizeof(float);
     auto kern = dkdv_simt_kernel<T, D>;
     if (smem > 48 * 1024)
@@ -372,6 +372,7 @@ int launch_bwd_t(const AttnParams& p, cudaStream_t s) {
     kern<<<grid, kThreads, smem, s>>>(p);
     return check_launch("dkdv_simt_kernel");
   }
+  return SA_OK;
 }
 
 template <typename T>
@@ -387,13 +388,13 @@ int dispatch_fwd(const AttnParams& p, cudaStream_t s) {
 }
 
 template <typename T>
-int dispatch_bwd(const AttnParams& p, cudaStream_t s) {
+int dispatch_bwd(const AttnParams& p, cudaStream_t s, int parts) {
   switch (p.D) {
-    case 16: return launch_bwd_t<T, 16>(p, s);
-    case 32: return launch_bwd_t<T, 32>(p, s);
-    case 64: return launch_bwd_t<T, 64>(p, s);
-    case 128: return launch_bwd_t<T, 128>(p, s);
-    case 256: return launch_bwd_t<T, 256>(p, s);
+    case 16: return launch_bwd_t<T, 16>(p, s, parts);
+    case 32: return launch_bwd_t<T, 32>(p, s, parts);
+    case 64: return launch_bwd_t<T, 64>(p, s, parts);
+    case 128: return launch_bwd_t<T, 128>(p, s, parts);
+    case 256: return launch_bwd_t<T, 256>(p, s, parts);
   }
   return fail(SA_EUNSUPPORTED, "head_dim " + std::to_string(p.D) + " not in {16,32,64,128,256}");
 }
@@ -410,12 +411,12 @@ int launch_fwd_simt(const AttnParams& p, cudaStream_t s) {
   return fail(SA_EUNSUPPORTED, "dtype");
 }
 
-int launch_bwd_simt(const AttnParams& p, cudaStream_t s) {
+int launch_bwd_simt(const AttnParams& p, cudaStream_t s, int parts) {
   if (p.N == 0 || p.Z * p.H == 0) return SA_OK;
   switch (p.dtype) {
-    case SA_F32: return dispatch_bwd<float>(p, s);
-    case SA_F16: return dispatch_bwd<__half>(p, s);
-    case SA_BF16: return dispatch_bwd<__nv_bfloat16>(p, s);
+    case SA_F32: return dispatch_bwd<float>(p, s, parts);
+    case SA_F16: return dispatch_bwd<__half>(p, s, parts);
+    case SA_BF16: return dispatch_bwd<__nv_bfloat16>(p, s, parts);
   }
   return fail(SA_EUNSUPPORTED, "dtype");
 }

@@ -44,6 +44,11 @@ _SIGNATURES = {
                                            _vp, _p64, _vp, _p64, _vp, _p64, _vp, _p64, _vp, _p64,
                                            _vp, _vp, _i64, _vp, _vp, _i32, _p64, _i32, _f32,
                                            _vp, _p64, _vp, _p64, _vp, _p64, _vp, _vp, _i64, _vp]),
+    "sa_block_list_attention_bwd_phase": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64, _i64, _i64,
+                                                 _vp, _p64, _vp, _p64, _vp, _p64, _vp, _p64, _vp,
+                                                 _p64, _vp, _vp, _i64, _vp, _vp, _i32, _p64, _i32,
+                                                 _f32, _vp, _p64, _vp, _p64, _vp, _p64, _vp, _vp,
+                                                 _i64, _vp]),
     "sa_ultrametric_decode_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64]),
     "sa_ultrametric_decode": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _i64,
                                      _vp, _p64, _vp, _p64, _vp, _p64, _vp, _p64, _i64, _vp,
