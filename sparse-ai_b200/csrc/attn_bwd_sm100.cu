@@ -1,9 +1,746 @@
-// Block-list attention backward on sm_100a (tcgen05).  Until the tensor-core backward lands,
-// every shape is routed to the CUDA-core kernels of attn_simt.cu.
+// Block-list attention backward on sm_100a: TMA + tcgen05 (TMEM accumulators).
+//
+// Same semantics as src/ultrametric/block_list.py:494-584 (dQ) and :586-681 (dK/dV) of
+// sparse-ai: P = exp2(s*scale*log2e + bias*log2e - lse*log2e) on the visible (row, key)
+// pairs, dS = P * (dP - Delta), dQ = scale * dS K, dK = scale * dS^T Q, dV = P^T dO,
+// d_soft_bias[z,h,qb,t] = sum of the unscaled dS of the block pair.
+//
+// Both kernels are persistent (one CTA per SM), 6 warps:
+//   warp 0      TMA producer
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer
+//   warps 2-5   elementwise warps: one TMEM lane (row) per thread
+//
+// dQ kernel:   work item = (128-row query tile, z, h); Q and dO tiles resident; the listed
+//              key blocks stream as 64-key sub-tiles (K and V) through a 3-stage ring.
+//                S[b]  = Q  K_j^T  (M=128, N=64, K=D)     b = j % 2 (TMEM double buffer)
+//                dP[b] = dO V_j^T  (M=128, N=64, K=D)
+//                dQ   += dS_j K_j  (M=128, N=D, K=64)     dS_j bf16/fp16 in smem (x2)
+// dK/dV kernel: work item = (128-key tile, z, KV head); K and V tiles resident; for every
+//              query head of the GQA group and every query block of its transposed list,
+//              64-row sub-tiles of Q and dO stream through a 3-stage ring.
+//                S^T[b]  = K Q_i^T  (M=128, N=64, K=D)
+//                dP^T[b] = V dO_i^T (M=128, N=64, K=D)
+//                dV     += P^T_i dO_i (M=128, N=D, K=64)
+//                dK     += dS^T_i Q_i (M=128, N=D, K=64)
+// The elementwise warps never rescale: the forward's LSE is final.
+#include <string>
+#include <type_traits>
+
 #include "attn_params.cuh"
 
 namespace sa {
+namespace {
 
-int launch_bwd_sm100(const AttnParams&, cudaStream_t, int) { return SA_EUNSUPPORTED; }
+constexpr int kRows = 128;  // resident tile rows (TMEM lanes)
+constexpr int kSub = 64;    // streamed sub-tile rows
+constexpr int kStages = 3;  // streamed ring depth
+constexpr int kBwdThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColP = 128, kColAcc = 256;  // S[2]: 0/64, dP[2]: 128/192
+
+struct BwdArgs {
+  CUtensorMap tm_q, tm_do, tm_k, tm_v;
+  int64_t Z, H, Hkv, N, RB, NB, tiles;
+  const int32_t* lists;
+  int64_t list_stride;
+  const int32_t* counts;
+  const int32_t* k_lists;  // (Z, H, NB, NB) transposed lists
+  const int32_t* k_slots;
+  const int32_t* q_counts;
+  const float* lse;
+  const float* delta;
+  const void* bias;
+  int bias_dtype;
+  int64_t bs[4];
+  float* dbias;
+  void* dq;
+  int64_t dqs[4];
+  void* dk;
+  int64_t dks[4];
+  void* dv;
+  int64_t dvs[4];
+  int causal;
+  float scale;
+  unsigned* status;
+};
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
+  uint32_t r;
+  if (bf16)
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  else
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// One 64-element (128-byte) row into a [rows][64] 128B-swizzled K-major chunk.
+__device__ __forceinline__ void st_row_sw128(unsigned char* chunk, int row, const uint32_t* pk) {
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const uint32_t off = row * 128 + ((u ^ (row & 7)) << 4);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + off)),
+                 "r"(pk[u * 4 + 0]), "r"(pk[u * 4 + 1]), "r"(pk[u * 4 + 2]), "r"(pk[u * 4 + 3])
+                 : "memory");
+  }
+}
+
+__device__ __forceinline__ float bias_log2(const BwdArgs& a, int64_t z, int64_t h, int64_t qb,
+                                           int64_t slot) {
+  if (!a.bias) return 0.f;
+  return load_any_f32(a.bias, a.bias_dtype, z * a.bs[0] + h * a.bs[1] + qb * a.bs[2] + slot * a.bs[3]) *
+         kLog2e;
+}
+
+template <int D>
+__device__ __forceinline__ void store_row(void* base, const int64_t* st, int64_t z, int64_t h,
+                                          int64_t row, uint32_t taddr, bool bf16, bool valid,
+                                          bool zero) {
+  using T = __nv_bfloat16;  // both half types are 2 bytes; pack2 picks the format
+  T* dst = static_cast<T*>(base) + z * st[0] + h * st[1] + row * st[2];
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    float o[32];
+    if (!zero) {
+      tmem_ld32(taddr + c * 32, o);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = 0.f;
+    }
+    if (valid) {
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        uint4 w;
+        w.x = pack2(o[v * 8 + 0], o[v * 8 + 1], bf16);
+        w.y = pack2(o[v * 8 + 2], o[v * 8 + 3], bf16);
+        w.z = pack2(o[v * 8 + 4], o[v * 8 + 5], bf16);
+        w.w = pack2(o[v * 8 + 6], o[v * 8 + 7], bf16);
+        *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void init_bars(uint64_t* bars, const uint32_t* counts, int n) {
+  for (int i = 0; i < n; ++i) mbar_init(&bars[i], counts[i]);
+  fence_mbar_init();
+}
+
+// =======================================================================================
+// dQ kernel
+// =======================================================================================
+template <int D>
+struct DqLayout {
+  static constexpr uint32_t kQ = 0;                          // [128][D]
+  static constexpr uint32_t kDO = kRows * D * 2;             // [128][D]
+  static constexpr uint32_t kKV = 2 * kRows * D * 2;         // stages x (K [64][D], V [64][D])
+  static constexpr uint32_t kStage = 2 * kSub * D * 2;
+  static constexpr uint32_t kDS = kKV + kStages * kStage;    // 2 x [128][64]
+  static constexpr uint32_t kBars = kDS + 2 * kRows * kSub * 2;
+  static constexpr uint32_t kAlloc = kBars + 256 + 1024;
+};
+
+enum { DQ_QFULL = 0, DQ_QEMPTY, DQ_KVFULL0, DQ_KVEMPTY0 = DQ_KVFULL0 + kStages,
+       DQ_SFULL0 = DQ_KVEMPTY0 + kStages, DQ_SEMPTY0 = DQ_SFULL0 + 2, DQ_DSFULL0 = DQ_SEMPTY0 + 2,
+       DQ_DSEMPTY0 = DQ_DSFULL0 + 2, DQ_DONE = DQ_DSEMPTY0 + 2, DQ_NUM };
+
+struct DqItem {
+  int64_t z, h, hk, q_start, qb, row_id;
+  int n_sub;  // 64-key sub-tiles
+};
+
+__device__ __forceinline__ DqItem dq_item(const BwdArgs& a, int64_t item) {
+  DqItem it;
+  const int64_t zh_total = a.Z * a.H;
+  const int64_t qt = a.tiles - 1 - item / zh_total;
+  const int64_t zh = item % zh_total;
+  it.z = zh / a.H;
+  it.h = zh % a.H;
+  it.hk = it.h / (a.H / a.Hkv);
+  it.q_start = qt * kRows;
+  it.qb = it.q_start / a.RB;
+  it.row_id = zh * a.NB + it.qb;
+  it.n_sub = a.counts[it.row_id] * (int)(a.RB / kSub);
+  return it;
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __grid_constant__ BwdArgs a) {
+  using L = DqLayout<D>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
+  __shared__ uint32_t s_tmem;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t items = a.Z * a.H * a.tiles;
+  const int spb = (int)(a.RB / kSub);
+
+  if (threadIdx.x == 0) {
+    uint32_t cnt[DQ_NUM];
+    for (int i = 0; i < DQ_NUM; ++i) cnt[i] = 1;
+    cnt[DQ_SEMPTY0] = cnt[DQ_SEMPTY0 + 1] = 128;
+    cnt[DQ_DSFULL0] = cnt[DQ_DSFULL0 + 1] = 128;
+    init_bars(bars, cnt, DQ_NUM);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&a.tm_q);
+      prefetch_tmap(&a.tm_do);
+      prefetch_tmap(&a.tm_k);
+      prefetch_tmap(&a.tm_v);
+      uint32_t kv = 0, jq = 0;
+      bool ok = true;
+      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const DqItem it = dq_item(a, item);
+        if (it.n_sub == 0) continue;
+        if (!(ok = mbar_wait(&bars[DQ_QEMPTY], (jq & 1) ^ 1, a.status))) break;
+        ++jq;
+        mbar_arrive_expect_tx(&bars[DQ_QFULL], 2 * kRows * D * 2);
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(sm + L::kQ + c * kRows * 128, &a.tm_q, &bars[DQ_QFULL], c * 64,
+                      (int)it.q_start, (int)it.h, (int)it.z);
+          tma_load_4d(sm + L::kDO + c * kRows * 128, &a.tm_do, &bars[DQ_QFULL], c * 64,
+                      (int)it.q_start, (int)it.h, (int)it.z);
+        }
+        const int32_t* lst = a.lists + it.row_id * a.list_stride;
+        for (int j = 0; j < it.n_sub && ok; ++j, ++kv) {
+          const int64_t k0 = (int64_t)lst[j / spb] * a.RB + (j % spb) * kSub;
+          const uint32_t st = kv % kStages, ph = (kv / kStages) & 1;
+          if (!(ok = mbar_wait(&bars[DQ_KVEMPTY0 + st], ph ^ 1, a.status))) break;
+          unsigned char* stage = sm + L::kKV + st * L::kStage;
+          mbar_arrive_expect_tx(&bars[DQ_KVFULL0 + st], L::kStage);
+          for (int c = 0; c < D / 64; ++c) {
+            tma_load_4d(stage + c * kSub * 128, &a.tm_k, &bars[DQ_KVFULL0 + st], c * 64, (int)k0,
+                        (int)it.hk, (int)it.z);
+            tma_load_4d(stage + kSub * D * 2 + c * kSub * 128, &a.tm_v, &bars[DQ_KVFULL0 + st],
+                        c * 64, (int)k0, (int)it.hk, (int)it.z);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_f16(kRows, kSub, BF16, false, false);
+      constexpr uint32_t id_dq = idesc_f16(kRows, D, BF16, false, true);
+      const uint32_t q_addr = smem_u32(sm + L::kQ), do_addr = smem_u32(sm + L::kDO);
+      uint32_t kv = 0, s_it = 0, ds_it = 0, jq = 0;
+      bool ok = true;
+      auto issue_dq = [&](uint32_t kv_u, bool first) -> bool {
+        const uint32_t db = ds_it & 1, dph = (ds_it >> 1) & 1;
+        if (!mbar_wait(&bars[DQ_DSFULL0 + db], dph, a.status)) return false;
+        tc_fence_after();
+        const uint32_t st = kv_u % kStages;
+        const uint32_t k_addr = smem_u32(sm + L::kKV + st * L::kStage);
+        const uint32_t ds_addr = smem_u32(sm + L::kDS + db * kRows * kSub * 2);
+#pragma unroll
+        for (int kk = 0; kk < kSub / 16; ++kk)
+          tc_mma_f16(tmem + kColAcc, smem_desc(ds_addr + kk * 32, 16, 1024),
+                     smem_desc(k_addr + kk * 16 * 128, kSub * 128, 1024), id_dq,
+                     (!first || kk > 0) ? 1u : 0u);
+        tc_commit(&bars[DQ_DSEMPTY0 + db]);
+        tc_commit(&bars[DQ_KVEMPTY0 + st]);
+        ++ds_it;
+        return true;
+      };
+      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const DqItem it = dq_item(a, item);
+        if (it.n_sub == 0) continue;
+        if (!(ok = mbar_wait(&bars[DQ_QFULL], jq & 1, a.status))) break;
+        ++jq;
+        const uint32_t kv0 = kv;
+        for (int j = 0; j < it.n_sub && ok; ++j, ++kv) {
+          const uint32_t st = kv % kStages, ph = (kv / kStages) & 1;
+          const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
+          ok = mbar_wait(&bars[DQ_KVFULL0 + st], ph, a.status) &&
+               mbar_wait(&bars[DQ_SEMPTY0 + sb], sph ^ 1, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sm + L::kKV + st * L::kStage);
+          const uint32_t v_addr = k_addr + kSub * D * 2;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t oa = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+            const uint32_t ob = (kk >> 2) * (kSub * 128) + (kk & 3) * 32;
+            tc_mma_f16(tmem + kColS + sb * kSub, smem_desc(q_addr + oa, 16, 1024),
+                       smem_desc(k_addr + ob, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+            tc_mma_f16(tmem + kColP + sb * kSub, smem_desc(do_addr + oa, 16, 1024),
+                       smem_desc(v_addr + ob, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&bars[DQ_SFULL0 + sb]);
+          if (j == it.n_sub - 1) tc_commit(&bars[DQ_QEMPTY]);
+          ++s_it;
+          if (j > 0) ok = issue_dq(kv0 + j - 1, j - 1 == 0);
+        }
+        if (ok) ok = issue_dq(kv0 + it.n_sub - 1, it.n_sub == 1);
+        if (ok) tc_commit(&bars[DQ_DONE]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int rl = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float scale2 = a.scale * kLog2e;
+    uint32_t s_it = 0, ds_it = 0, done_it = 0;
+    bool ok = true;
+    for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+      const DqItem it = dq_item(a, item);
+      const int64_t row = it.q_start + rl;
+      const int64_t zh = it.z * a.H + it.h;
+      float lse2 = 0.f, dl = 0.f;
+      if (row < a.N) {
+        const float lv = a.lse[zh * a.N + row];
+        lse2 = lv == -INFINITY ? 0.f : lv * kLog2e;
+        dl = a.delta[zh * a.N + row];
+      }
+      const int32_t* lst = a.lists + it.row_id * a.list_stride;
+      float db_acc = 0.f;
+      for (int j = 0; j < it.n_sub && ok; ++j) {
+        const int slot = j / spb;
+        const int64_t k0 = (int64_t)lst[slot] * a.RB + (j % spb) * kSub;
+        const float b2 = bias_log2(a, it.z, it.h, it.qb, slot);
+        const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
+        if (!(ok = mbar_wait(&bars[DQ_SFULL0 + sb], sph, a.status))) break;
+        tc_fence_after();
+        float s[kSub], dp[kSub];
+#pragma unroll
+        for (int c = 0; c < kSub / 32; ++c) {
+          float t0[32], t1[32];
+          tmem_ld32(lane_addr + kColS + sb * kSub + c * 32, t0);
+          tmem_ld32(lane_addr + kColP + sb * kSub + c * 32, t1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            s[c * 32 + i] = t0[i];
+            dp[c * 32 + i] = t1[i];
+          }
+        }
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[DQ_SEMPTY0 + sb]);
+        ++s_it;
+        int64_t lim = a.N - 1 - k0;
+        if (a.causal) lim = min(lim, row - k0);
+        if (row >= a.N) lim = -1;
+        uint32_t pk[kSub / 2];
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < kSub; c += 2) {
+          float d0 = 0.f, d1 = 0.f;
+          if (c <= lim) d0 = fast_exp2(fmaf(s[c], scale2, b2) - lse2) * (dp[c] - dl);
+          if (c + 1 <= lim) d1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - lse2) * (dp[c + 1] - dl);
+          rs += d0 + d1;
+          pk[c / 2] = pack2(d0 * a.scale, d1 * a.scale, BF16);
+        }
+        db_acc += rs;
+        const uint32_t db = ds_it & 1, dph = (ds_it >> 1) & 1;
+        if (!(ok = mbar_wait(&bars[DQ_DSEMPTY0 + db], dph ^ 1, a.status))) break;
+        st_row_sw128(sm + L::kDS + db * kRows * kSub * 2, rl, pk);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars[DQ_DSFULL0 + db]);
+        ++ds_it;
+        if (a.dbias && (j % spb == spb - 1)) {
+          float v = db_acc;
+#pragma unroll
+          for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0) atomicAdd(&a.dbias[it.row_id * a.list_stride + slot], v);
+          db_acc = 0.f;
+        }
+      }
+      if (!ok) break;
+      if (it.n_sub > 0) {
+        if (!(ok = mbar_wait(&bars[DQ_DONE], done_it & 1, a.status))) break;
+        ++done_it;
+        tc_fence_after();
+      }
+      store_row<D>(a.dq, a.dqs, it.z, it.h, row, lane_addr + kColAcc, BF16, row < a.N, it.n_sub == 0);
+      tc_fence_before();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// =======================================================================================
+// dK / dV kernel
+// =======================================================================================
+template <int D>
+struct DkvLayout {
+  static constexpr uint32_t kK = 0;                         // [128][D]
+  static constexpr uint32_t kV = kRows * D * 2;             // [128][D]
+  static constexpr uint32_t kQD = 2 * kRows * D * 2;        // stages x (Q [64][D], dO [64][D])
+  static constexpr uint32_t kStage = 2 * kSub * D * 2;
+  static constexpr uint32_t kPT = kQD + kStages * kStage;   // P^T [128][64]
+  static constexpr uint32_t kDST = kPT + kRows * kSub * 2;  // dS^T [128][64]
+  static constexpr uint32_t kLD = kDST + kRows * kSub * 2;  // 2 x (lse2[64], delta[64]) fp32
+  static constexpr uint32_t kBars = kLD + 2 * 2 * kSub * 4;
+  static constexpr uint32_t kAlloc = kBars + 256 + 1024;
+};
+
+enum { KV_KVFULL = 0, KV_KVEMPTY, KV_QFULL0, KV_QEMPTY0 = KV_QFULL0 + kStages,
+       KV_SFULL0 = KV_QEMPTY0 + kStages, KV_SEMPTY0 = KV_SFULL0 + 2, KV_PFULL = KV_SEMPTY0 + 2,
+       KV_PEMPTY, KV_DONE, KV_NUM };
+
+struct KvItem {
+  int64_t z, hk, k0, kb;
+};
+
+__device__ __forceinline__ KvItem kv_item(const BwdArgs& a, int64_t item) {
+  KvItem it;
+  const int64_t zg_total = a.Z * a.Hkv;
+  const int64_t kt = item / zg_total;
+  const int64_t zg = item % zg_total;
+  it.z = zg / a.Hkv;
+  it.hk = zg % a.Hkv;
+  it.k0 = kt * kRows;
+  it.kb = it.k0 / a.RB;
+  return it;
+}
+
+// Visit every streamed query sub-tile of a dK/dV work item in a fixed order:
+// query heads of the group, then the transposed list, then 64-row sub-tiles.
+template <typename F>
+__device__ __forceinline__ bool for_each_qtile(const BwdArgs& a, const KvItem& it, F&& f) {
+  const int64_t group = a.H / a.Hkv;
+  const int spb = (int)(a.RB / kSub);
+  for (int64_t h = it.hk * group; h < (it.hk + 1) * group; ++h) {
+    const int64_t krow = (it.z * a.H + h) * a.NB + it.kb;
+    const int qc = a.q_counts[krow];
+    for (int j = 0; j < qc; ++j) {
+      const int64_t qb = a.k_lists[krow * a.NB + j];
+      const int64_t slot = a.k_slots[krow * a.NB + j];
+      for (int s = 0; s < spb; ++s)
+        if (!f(h, qb, slot, qb * a.RB + s * kSub)) return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ int kv_item_tiles(const BwdArgs& a, const KvItem& it) {
+  const int64_t group = a.H / a.Hkv;
+  int n = 0;
+  for (int64_t h = it.hk * group; h < (it.hk + 1) * group; ++h)
+    n += a.q_counts[(it.z * a.H + h) * a.NB + it.kb];
+  return n * (int)(a.RB / kSub);
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __grid_constant__ BwdArgs a) {
+  using L = DkvLayout<D>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
+  __shared__ uint32_t s_tmem;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t items = a.Z * a.Hkv * a.tiles;
+
+  if (threadIdx.x == 0) {
+    uint32_t cnt[KV_NUM];
+    for (int i = 0; i < KV_NUM; ++i) cnt[i] = 1;
+    cnt[KV_SEMPTY0] = cnt[KV_SEMPTY0 + 1] = 128;
+    cnt[KV_PFULL] = 128;
+    init_bars(bars, cnt, KV_NUM);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&a.tm_q);
+      prefetch_tmap(&a.tm_do);
+      prefetch_tmap(&a.tm_k);
+      prefetch_tmap(&a.tm_v);
+      uint32_t qd = 0, jk = 0;
+      bool ok = true;
+      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const KvItem it = kv_item(a, item);
+        if (kv_item_tiles(a, it) == 0) continue;
+        if (!(ok = mbar_wait(&bars[KV_KVEMPTY], (jk & 1) ^ 1, a.status))) break;
+        ++jk;
+        mbar_arrive_expect_tx(&bars[KV_KVFULL], 2 * kRows * D * 2);
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(sm + L::kK + c * kRows * 128, &a.tm_k, &bars[KV_KVFULL], c * 64, (int)it.k0,
+                      (int)it.hk, (int)it.z);
+          tma_load_4d(sm + L::kV + c * kRows * 128, &a.tm_v, &bars[KV_KVFULL], c * 64, (int)it.k0,
+                      (int)it.hk, (int)it.z);
+        }
+        ok = for_each_qtile(a, it, [&](int64_t h, int64_t, int64_t, int64_t q0) -> bool {
+          const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
+          if (!mbar_wait(&bars[KV_QEMPTY0 + st], ph ^ 1, a.status)) return false;
+          unsigned char* stage = sm + L::kQD + st * L::kStage;
+          mbar_arrive_expect_tx(&bars[KV_QFULL0 + st], L::kStage);
+          for (int c = 0; c < D / 64; ++c) {
+            tma_load_4d(stage + c * kSub * 128, &a.tm_q, &bars[KV_QFULL0 + st], c * 64, (int)q0,
+                        (int)h, (int)it.z);
+            tma_load_4d(stage + kSub * D * 2 + c * kSub * 128, &a.tm_do, &bars[KV_QFULL0 + st],
+                        c * 64, (int)q0, (int)h, (int)it.z);
+          }
+          ++qd;
+          return true;
+        });
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_f16(kRows, kSub, BF16, false, false);
+      constexpr uint32_t id_acc = idesc_f16(kRows, D, BF16, false, true);
+      const uint32_t k_addr = smem_u32(sm + L::kK), v_addr = smem_u32(sm + L::kV);
+      const uint32_t pt_addr = smem_u32(sm + L::kPT), dst_addr = smem_u32(sm + L::kDST);
+      uint32_t qd = 0, s_it = 0, p_it = 0, jk = 0;
+      bool ok = true;
+      auto issue_acc = [&](uint32_t qd_u, bool first) -> bool {
+        if (!mbar_wait(&bars[KV_PFULL], p_it & 1, a.status)) return false;
+        tc_fence_after();
+        const uint32_t st = qd_u % kStages;
+        const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
+        const uint32_t do_addr = q_addr + kSub * D * 2;
+#pragma unroll
+        for (int kk = 0; kk < kSub / 16; ++kk) {
+          const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+          tc_mma_f16(tmem + kColAcc, smem_desc(pt_addr + kk * 32, 16, 1024),
+                     smem_desc(do_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
+          tc_mma_f16(tmem + kColAcc + D, smem_desc(dst_addr + kk * 32, 16, 1024),
+                     smem_desc(q_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
+        }
+        tc_commit(&bars[KV_PEMPTY]);
+        tc_commit(&bars[KV_QEMPTY0 + st]);
+        ++p_it;
+        return true;
+      };
+      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const KvItem it = kv_item(a, item);
+        const int n = kv_item_tiles(a, it);
+        if (n == 0) continue;
+        if (!(ok = mbar_wait(&bars[KV_KVFULL], jk & 1, a.status))) break;
+        ++jk;
+        const uint32_t qd0 = qd;
+        int i = 0;
+        ok = for_each_qtile(a, it, [&](int64_t, int64_t, int64_t, int64_t) -> bool {
+          const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
+          const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
+          if (!mbar_wait(&bars[KV_QFULL0 + st], ph, a.status)) return false;
+          if (!mbar_wait(&bars[KV_SEMPTY0 + sb], sph ^ 1, a.status)) return false;
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
+          const uint32_t do_addr = q_addr + kSub * D * 2;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t oa = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+            const uint32_t ob = (kk >> 2) * (kSub * 128) + (kk & 3) * 32;
+            tc_mma_f16(tmem + kColS + sb * kSub, smem_desc(k_addr + oa, 16, 1024),
+                       smem_desc(q_addr + ob, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+            tc_mma_f16(tmem + kColP + sb * kSub, smem_desc(v_addr + oa, 16, 1024),
+                       smem_desc(do_addr + ob, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&bars[KV_SFULL0 + sb]);
+          if (i == n - 1) tc_commit(&bars[KV_KVEMPTY]);
+          ++s_it;
+          if (i > 0 && !issue_acc(qd0 + i - 1, i - 1 == 0)) return false;
+          ++qd;
+          ++i;
+          return true;
+        });
+        if (ok) ok = issue_acc(qd0 + n - 1, n == 1);
+        if (ok) tc_commit(&bars[KV_DONE]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int rl = quarter * 32 + lane;  // key row within the tile
+    const int tid = threadIdx.x - 64;    // 0..127 among the elementwise warps
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float scale2 = a.scale * kLog2e;
+    float* s_ld = reinterpret_cast<float*>(sm + L::kLD);  // [2][2][64]
+    uint32_t s_it = 0, p_it = 0, done_it = 0, ld_it = 0;
+    bool ok = true;
+    for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+      const KvItem it = kv_item(a, item);
+      const int n = kv_item_tiles(a, it);
+      const int64_t key = it.k0 + rl;
+      ok = for_each_qtile(a, it, [&](int64_t h, int64_t qb, int64_t slot, int64_t q0) -> bool {
+        const int64_t zh = it.z * a.H + h;
+        // stage this sub-tile's lse*log2e and Delta in shared memory (double buffered)
+        float* buf = s_ld + (ld_it & 1) * 2 * kSub;
+        {
+          const int j = tid & (kSub - 1);
+          const int64_t r = q0 + j;
+          if (tid < kSub) {
+            const float lv = r < a.N ? a.lse[zh * a.N + r] : -INFINITY;
+            buf[j] = lv == -INFINITY ? 0.f : lv * kLog2e;  // block_list.py:553 (lse_safe)
+          } else {
+            buf[kSub + j] = r < a.N ? a.delta[zh * a.N + r] : 0.f;
+          }
+        }
+        named_bar_sync(1, 128);
+        ++ld_it;
+        const float b2 = bias_log2(a, it.z, h, qb, slot);
+        const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
+        if (!mbar_wait(&bars[KV_SFULL0 + sb], sph, a.status)) return false;
+        tc_fence_after();
+        float s[kSub], dp[kSub];
+#pragma unroll
+        for (int c = 0; c < kSub / 32; ++c) {
+          float t0[32], t1[32];
+          tmem_ld32(lane_addr + kColS + sb * kSub + c * 32, t0);
+          tmem_ld32(lane_addr + kColP + sb * kSub + c * 32, t1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            s[c * 32 + i] = t0[i];
+            dp[c * 32 + i] = t1[i];
+          }
+        }
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[KV_SEMPTY0 + sb]);
+        ++s_it;
+        // query q0 + c sees this key iff key < N, q0 + c < N and, when causal, key <= q0 + c
+        const bool key_ok = key < a.N;
+        const int64_t cmin = a.causal ? key - q0 : 0;  // first visible query offset
+        const int64_t cend = a.N - q0;                 // queries at offsets >= cend are padding
+        uint32_t pk[kSub / 2], dk[kSub / 2];
+#pragma unroll
+        for (int c = 0; c < kSub; c += 2) {
+          float p0 = 0.f, p1 = 0.f, d0 = 0.f, d1 = 0.f;
+          if (key_ok && c >= cmin && c < cend) {
+            p0 = fast_exp2(fmaf(s[c], scale2, b2) - buf[c]);
+            d0 = p0 * (dp[c] - buf[kSub + c]) * a.scale;
+          }
+          if (key_ok && c + 1 >= cmin && c + 1 < cend) {
+            p1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - buf[c + 1]);
+            d1 = p1 * (dp[c + 1] - buf[kSub + c + 1]) * a.scale;
+          }
+          pk[c / 2] = pack2(p0, p1, BF16);
+          dk[c / 2] = pack2(d0, d1, BF16);
+        }
+        if (!mbar_wait(&bars[KV_PEMPTY], (p_it & 1) ^ 1, a.status)) return false;
+        st_row_sw128(sm + L::kPT, rl, pk);
+        st_row_sw128(sm + L::kDST, rl, dk);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars[KV_PFULL]);
+        ++p_it;
+        return true;
+      });
+      if (!ok) break;
+      if (n > 0) {
+        if (!(ok = mbar_wait(&bars[KV_DONE], done_it & 1, a.status))) break;
+        ++done_it;
+        tc_fence_after();
+      }
+      store_row<D>(a.dv, a.dvs, it.z, it.hk, key, lane_addr + kColAcc, BF16, key < a.N, n == 0);
+      store_row<D>(a.dk, a.dks, it.z, it.hk, key, lane_addr + kColAcc + D, BF16, key < a.N, n == 0);
+      tc_fence_before();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int D, bool BF16>
+int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
+  BwdArgs a{};
+  a.Z = p.Z;
+  a.H = p.H;
+  a.Hkv = p.Hkv;
+  a.N = p.N;
+  a.RB = p.RB;
+  a.NB = p.NB;
+  a.lists = p.lists;
+  a.list_stride = p.list_stride;
+  a.counts = p.counts;
+  a.k_lists = p.k_lists;
+  a.k_slots = p.k_slots;
+  a.q_counts = p.q_counts;
+  a.lse = p.lse;
+  a.delta = p.delta;
+  a.bias = p.bias;
+  a.bias_dtype = p.bias_dtype;
+  for (int i = 0; i < 4; ++i) {
+    a.bs[i] = p.bs[i];
+    a.dqs[i] = p.dqs[i];
+    a.dks[i] = p.dks[i];
+    a.dvs[i] = p.dvs[i];
+  }
+  a.dbias = p.dbias;
+  a.dq = p.dq;
+  a.dk = p.dk;
+  a.dv = p.dv;
+  a.causal = p.causal;
+  a.scale = p.scale;
+  a.status = p.status;
+  const int sms = device_sm_count();
+  if (parts & kBwdDq) {
+    int rc = make_tmap_4d(&a.tm_q, p.q, p.dtype, p.Z, p.H, p.N, D, p.qs, 64, kRows);
+    if (!rc) rc = make_tmap_4d(&a.tm_do, p.dout, p.dtype, p.Z, p.H, p.N, D, p.dos, 64, kRows);
+    if (!rc) rc = make_tmap_4d(&a.tm_k, p.k, p.dtype, p.Z, p.Hkv, p.N, D, p.ks, 64, kSub);
+    if (!rc) rc = make_tmap_4d(&a.tm_v, p.v, p.dtype, p.Z, p.Hkv, p.N, D, p.vs, 64, kSub);
+    if (rc) return fail(SA_ELAUNCH, std::string("dQ tensor maps: ") + sa_last_error());
+    a.tiles = (p.N + kRows - 1) / kRows;
+    const int64_t items = a.Z * a.H * a.tiles;
+    auto kern = bwd_dq_sm100_kernel<D, BF16>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DqLayout<D>::kAlloc);
+    kern<<<(unsigned)std::min<int64_t>(items, sms), kBwdThreads, DqLayout<D>::kAlloc, stream>>>(a);
+    int e = check_launch("bwd_dq_sm100_kernel");
+    if (e) return e;
+  }
+  if (parts & kBwdDkDv) {
+    int rc = make_tmap_4d(&a.tm_q, p.q, p.dtype, p.Z, p.H, p.N, D, p.qs, 64, kSub);
+    if (!rc) rc = make_tmap_4d(&a.tm_do, p.dout, p.dtype, p.Z, p.H, p.N, D, p.dos, 64, kSub);
+    if (!rc) rc = make_tmap_4d(&a.tm_k, p.k, p.dtype, p.Z, p.Hkv, p.N, D, p.ks, 64, kRows);
+    if (!rc) rc = make_tmap_4d(&a.tm_v, p.v, p.dtype, p.Z, p.Hkv, p.N, D, p.vs, 64, kRows);
+    if (rc) return fail(SA_ELAUNCH, std::string("dK/dV tensor maps: ") + sa_last_error());
+    a.tiles = (p.N + kRows - 1) / kRows;
+    const int64_t items = a.Z * a.Hkv * a.tiles;
+    auto kern = bwd_dkdv_sm100_kernel<D, BF16>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DkvLayout<D>::kAlloc);
+    kern<<<(unsigned)std::min<int64_t>(items, sms), kBwdThreads, DkvLayout<D>::kAlloc, stream>>>(a);
+    int e = check_launch("bwd_dkdv_sm100_kernel");
+    if (e) return e;
+  }
+  return SA_OK;
+}
+
+}  // namespace
+
+int launch_bwd_sm100(const AttnParams& p, cudaStream_t stream, int parts) {
+  if (p.dtype != SA_BF16 && p.dtype != SA_F16) return SA_EUNSUPPORTED;
+  if (p.D != 64 && p.D != 128) return SA_EUNSUPPORTED;
+  if (p.RB % kRows) return SA_EUNSUPPORTED;
+  const void* ptrs[7] = {p.q, p.k, p.v, p.dout, p.dq, p.dk, p.dv};
+  for (auto ptr : ptrs)
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return SA_EUNSUPPORTED;
+  for (int i = 0; i < 3; ++i)
+    if (p.qs[i] % 8 || p.ks[i] % 8 || p.vs[i] % 8 || p.dos[i] % 8 || p.dqs[i] % 8 ||
+        p.dks[i] % 8 || p.dvs[i] % 8)
+      return SA_EUNSUPPORTED;
+  if (p.N > INT32_MAX) return SA_EUNSUPPORTED;
+  const bool bf = p.dtype == SA_BF16;
+  if (p.D == 64) return bf ? launch_t<64, true>(p, stream, parts) : launch_t<64, false>(p, stream, parts);
+  return bf ? launch_t<128, true>(p, stream, parts) : launch_t<128, false>(p, stream, parts);
+}
 
 }  // namespace sa
