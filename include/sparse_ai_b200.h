@@ -213,6 +213,29 @@ SA_API int sa_ultrametric_decode(int dtype, int64_t B, int64_t H, int64_t Hkv, i
                           void* out, const int64_t* out_strides,
                           void* workspace, int64_t workspace_bytes, void* stream);
 
+/*
+ * sa_ultrametric_decode without a caller workspace.  No counterpart in the reference: it is
+ * for callers that cannot allocate device memory when they decode (a serving loop whose
+ * memory is carved up front by its own pool and that binds only this C ABI, or a host that
+ * must not trigger cudaMalloc's implicit synchronisation mid-step).  Same arguments and
+ * results as sa_ultrametric_decode minus the workspace pair; the split-K workspace comes
+ * from a fixed 16 MiB device array inside the library (held by every GPU that loads it
+ * until exit).  Requests needing more than 16 MiB of workspace return SA_EWORKSPACE.  The
+ * first call on a device looks the array up (make it before any stream capture).  All
+ * calls share the array: calls that overlap on the GPU race.  Allocates nothing.
+ */
+SA_API int sa_ultrametric_decode_noalloc(int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t D,
+                          int64_t page_size, int64_t num_pages,
+                          const void* q, const int64_t* q_strides,
+                          const void* k_cache, const int64_t* k_strides,
+                          const void* v_cache, const int64_t* v_strides,
+                          const int32_t* block_tables, const int64_t* bt_strides,
+                          int64_t max_logical_pages, const int32_t* context_lens,
+                          const void* router, int router_dtype, const int64_t* router_strides,
+                          const void* q_router, int q_router_dtype, const int64_t* q_router_strides,
+                          int64_t TD, int64_t req_depth, int64_t local_blocks, int sink_block,
+                          void* out, const int64_t* out_strides, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

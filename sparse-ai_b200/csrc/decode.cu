@@ -480,3 +480,88 @@ int sa_ultrametric_decode(int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Decode without any allocation by the caller.
+//
+// Some callers cannot allocate device memory when they decode: a serving loop whose device
+// memory is carved up front by its own pool and that binds only this C ABI (it has no
+// allocator to call for the split-K workspace), or a host that must not trigger
+// cudaMalloc's implicit device synchronisation in the middle of a decode step.  This entry
+// point takes its split-K workspace from a fixed, file-scope device array instead.
+//
+//  * The array holds kNoAllocScratchBytes (16 MiB).  Every GPU that loads this library
+//    keeps it for the life of the process.
+//  * Its device address is looked up once per device (cudaGetSymbolAddress, with that
+//    device current) on the first call made on that device; make that first call before
+//    any stream capture.
+//  * Requests whose workspace would exceed the array are rejected with SA_EWORKSPACE.
+//  * All calls share the one array: calls that overlap on the GPU (different streams, or
+//    different host threads) race on it.  The decode kernel rewrites every slot it reads
+//    in the same launch, so nothing needs clearing between calls.
+// ---------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace sa {
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 16ll << 20;
+__device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+void* decode_scratch_ptr() {
+  constexpr int kMaxDev = 64;
+  static void* ptrs[kMaxDev] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess) {
+      set_error(std::string("decode scratch address: ") + cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+}  // namespace
+}  // namespace sa
+
+extern "C" {
+
+int sa_ultrametric_decode_noalloc(int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t D,
+                                  int64_t page_size, int64_t num_pages, const void* q,
+                                  const int64_t* q_strides, const void* k_cache,
+                                  const int64_t* k_strides, const void* v_cache,
+                                  const int64_t* v_strides, const int32_t* block_tables,
+                                  const int64_t* bt_strides, int64_t max_logical_pages,
+                                  const int32_t* context_lens, const void* router,
+                                  int router_dtype, const int64_t* router_strides,
+                                  const void* q_router, int q_router_dtype,
+                                  const int64_t* q_router_strides, int64_t TD, int64_t req_depth,
+                                  int64_t local_blocks, int sink_block, void* out,
+                                  const int64_t* out_strides, void* stream) {
+  using namespace sa;
+  if (H > 0 && Hkv > 0 && D > 0) {
+    const int64_t need = sa_ultrametric_decode_workspace_bytes(B, H, Hkv, D, max_logical_pages);
+    if (need > kNoAllocScratchBytes)
+      return fail(SA_EWORKSPACE, "decode_noalloc: this request needs " + std::to_string(need) +
+                                     " bytes of split-K workspace, above the fixed " +
+                                     std::to_string(kNoAllocScratchBytes) +
+                                     "-byte device array; use sa_ultrametric_decode with a "
+                                     "caller-provided workspace");
+  }
+  void* scratch = decode_scratch_ptr();
+  if (!scratch) return fail(SA_ELAUNCH, std::string("decode_noalloc: ") + sa_last_error());
+  return sa_ultrametric_decode(dtype, B, H, Hkv, D, page_size, num_pages, q, q_strides, k_cache,
+                               k_strides, v_cache, v_strides, block_tables, bt_strides,
+                               max_logical_pages, context_lens, router, router_dtype,
+                               router_strides, q_router, q_router_dtype, q_router_strides, TD,
+                               req_depth, local_blocks, sink_block, out, out_strides, scratch,
+                               kNoAllocScratchBytes, stream);
+}
+
+}  // extern "C"
