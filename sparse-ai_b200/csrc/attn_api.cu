@@ -96,6 +96,7 @@ int64_t sa_block_list_attention_bwd_workspace_bytes(int64_t Z, int64_t H, int64_
   size_t b = align256((size_t)Z * H * N * sizeof(float));            // delta
   b += 2 * align256((size_t)Z * H * NB * NB * sizeof(int32_t));       // k_lists, k_slots
   b += align256((size_t)Z * H * NB * sizeof(int32_t));                // q_counts
+  b += align256((size_t)Z * H * ((N + 63) / 64) * 128 * sizeof(float));  // row stats
   return (int64_t)b;
 }
 
@@ -154,6 +155,8 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
   int32_t* k_slots = reinterpret_cast<int32_t*>(w);
   w += align256((size_t)Z * H * NB * NB * sizeof(int32_t));
   int32_t* q_counts = reinterpret_cast<int32_t*>(w);
+  w += align256((size_t)Z * H * NB * sizeof(int32_t));
+  p.stats = reinterpret_cast<float*>(w);
   p.k_lists = k_lists;
   p.k_slots = k_slots;
   p.q_counts = q_counts;

@@ -8,7 +8,8 @@
 // Both kernels are persistent (one CTA per SM), 6 warps:
 //   warp 0      TMA producer
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
-//   warps 2-5   elementwise warps: one TMEM lane (row) per thread
+//   warps 2-9   elementwise warps: a thread owns one TMEM lane (row) and half of the
+//               64 columns of each streamed sub-tile (two warps per lane quarter)
 //
 // dQ kernel:   work item = (128-row query tile, z, h); Q and dO tiles resident; the listed
 //              key blocks stream as 64-key sub-tiles (K and V) through a 3-stage ring.
@@ -34,7 +35,9 @@ namespace {
 constexpr int kRows = 128;  // resident tile rows (TMEM lanes)
 constexpr int kSub = 64;    // streamed sub-tile rows
 constexpr int kStages = 3;  // streamed ring depth
-constexpr int kBwdThreads = 192;
+constexpr int kEw = 8;                      // elementwise warps: 2 per TMEM lane quarter
+constexpr int kEwThreads = kEw * 32;
+constexpr int kBwdThreads = 64 + kEwThreads;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 128, kColAcc = 256;  // S[2]: 0/64, dP[2]: 128/192
 
@@ -53,6 +56,7 @@ struct BwdArgs {
   int bias_dtype;
   int64_t bs[4];
   float* dbias;
+  const float* stats;  // (Z*H, ceil(N/64), {lse*log2e[64], delta[64]})
   void* dq;
   int64_t dqs[4];
   void* dk;
@@ -73,17 +77,6 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
   return r;
 }
 
-// One 64-element (128-byte) row into a [rows][64] 128B-swizzled K-major chunk.
-__device__ __forceinline__ void st_row_sw128(unsigned char* chunk, int row, const uint32_t* pk) {
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const uint32_t off = row * 128 + ((u ^ (row & 7)) << 4);
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + off)),
-                 "r"(pk[u * 4 + 0]), "r"(pk[u * 4 + 1]), "r"(pk[u * 4 + 2]), "r"(pk[u * 4 + 3])
-                 : "memory");
-  }
-}
-
 __device__ __forceinline__ float bias_log2(const BwdArgs& a, int64_t z, int64_t h, int64_t qb,
                                            int64_t slot) {
   if (!a.bias) return 0.f;
@@ -91,14 +84,16 @@ __device__ __forceinline__ float bias_log2(const BwdArgs& a, int64_t z, int64_t 
          kLog2e;
 }
 
-template <int D>
-__device__ __forceinline__ void store_row(void* base, const int64_t* st, int64_t z, int64_t h,
-                                          int64_t row, uint32_t taddr, bool bf16, bool valid,
-                                          bool zero) {
+// Store NC consecutive TMEM columns (starting at taddr) of one row, as bf16/fp16, to
+// base[z, h, row, c0 : c0 + NC].
+template <int NC>
+__device__ __forceinline__ void store_cols(void* base, const int64_t* st, int64_t z, int64_t h,
+                                           int64_t row, int c0, uint32_t taddr, bool bf16,
+                                           bool valid, bool zero) {
   using T = __nv_bfloat16;  // both half types are 2 bytes; pack2 picks the format
-  T* dst = static_cast<T*>(base) + z * st[0] + h * st[1] + row * st[2];
+  T* dst = static_cast<T*>(base) + z * st[0] + h * st[1] + row * st[2] + c0;
 #pragma unroll
-  for (int c = 0; c < D / 32; ++c) {
+  for (int c = 0; c < NC / 32; ++c) {
     float o[32];
     if (!zero) {
       tmem_ld32(taddr + c * 32, o);
@@ -118,6 +113,19 @@ __device__ __forceinline__ void store_row(void* base, const int64_t* st, int64_t
         *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
       }
     }
+  }
+}
+
+// Half a row (32 elements, four 16-byte units starting at unit u0) into a [rows][64]
+// 128B-swizzled K-major chunk.
+__device__ __forceinline__ void st_half_row_sw128(unsigned char* chunk, int row, int u0,
+                                                  const uint32_t* pk) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const uint32_t off = row * 128 + (((u0 + u) ^ (row & 7)) << 4);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + off)),
+                 "r"(pk[u * 4 + 0]), "r"(pk[u * 4 + 1]), "r"(pk[u * 4 + 2]), "r"(pk[u * 4 + 3])
+                 : "memory");
   }
 }
 
@@ -179,8 +187,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
   if (threadIdx.x == 0) {
     uint32_t cnt[DQ_NUM];
     for (int i = 0; i < DQ_NUM; ++i) cnt[i] = 1;
-    cnt[DQ_SEMPTY0] = cnt[DQ_SEMPTY0 + 1] = 128;
-    cnt[DQ_DSFULL0] = cnt[DQ_DSFULL0 + 1] = 128;
+    cnt[DQ_SEMPTY0] = cnt[DQ_SEMPTY0 + 1] = kEwThreads;
+    cnt[DQ_DSFULL0] = cnt[DQ_DSFULL0 + 1] = kEwThreads;
     init_bars(bars, cnt, DQ_NUM);
   }
   if (warp == 1) {
@@ -287,6 +295,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // which 32 of the 64 sub-tile columns
     const int rl = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const float scale2 = a.scale * kLog2e;
@@ -299,41 +308,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
       float lse2 = 0.f, dl = 0.f;
       if (row < a.N) {
         const float lv = a.lse[zh * a.N + row];
-        lse2 = lv == -INFINITY ? 0.f : lv * kLog2e;
+        lse2 = lv == -INFINITY ? 0.f : lv * kLog2e;  // block_list.py:553 (lse_safe)
         dl = a.delta[zh * a.N + row];
       }
       const int32_t* lst = a.lists + it.row_id * a.list_stride;
       float db_acc = 0.f;
       for (int j = 0; j < it.n_sub && ok; ++j) {
         const int slot = j / spb;
-        const int64_t k0 = (int64_t)lst[slot] * a.RB + (j % spb) * kSub;
+        const int64_t k0 = (int64_t)lst[slot] * a.RB + (j % spb) * kSub + half * 32;
         const float b2 = bias_log2(a, it.z, it.h, it.qb, slot);
         const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
         if (!(ok = mbar_wait(&bars[DQ_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
-        float s[kSub], dp[kSub];
-#pragma unroll
-        for (int c = 0; c < kSub / 32; ++c) {
-          float t0[32], t1[32];
-          tmem_ld32(lane_addr + kColS + sb * kSub + c * 32, t0);
-          tmem_ld32(lane_addr + kColP + sb * kSub + c * 32, t1);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            s[c * 32 + i] = t0[i];
-            dp[c * 32 + i] = t1[i];
-          }
-        }
+        float s[32], dp[32];
+        tmem_ld32(lane_addr + kColS + sb * kSub + half * 32, s);
+        tmem_ld32(lane_addr + kColP + sb * kSub + half * 32, dp);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars[DQ_SEMPTY0 + sb]);
         ++s_it;
-        int64_t lim = a.N - 1 - k0;
+        int64_t lim = a.N - 1 - k0;  // keys k0 + c with c <= lim are visible to this row
         if (a.causal) lim = min(lim, row - k0);
         if (row >= a.N) lim = -1;
-        uint32_t pk[kSub / 2];
+        uint32_t pk[16];
         float rs = 0.f;
 #pragma unroll
-        for (int c = 0; c < kSub; c += 2) {
+        for (int c = 0; c < 32; c += 2) {
           float d0 = 0.f, d1 = 0.f;
           if (c <= lim) d0 = fast_exp2(fmaf(s[c], scale2, b2) - lse2) * (dp[c] - dl);
           if (c + 1 <= lim) d1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - lse2) * (dp[c + 1] - dl);
@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         db_acc += rs;
         const uint32_t db = ds_it & 1, dph = (ds_it >> 1) & 1;
         if (!(ok = mbar_wait(&bars[DQ_DSEMPTY0 + db], dph ^ 1, a.status))) break;
-        st_row_sw128(sm + L::kDS + db * kRows * kSub * 2, rl, pk);
+        st_half_row_sw128(sm + L::kDS + db * kRows * kSub * 2, rl, half * 4, pk);
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&bars[DQ_DSFULL0 + db]);
@@ -362,7 +362,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         ++done_it;
         tc_fence_after();
       }
-      store_row<D>(a.dq, a.dqs, it.z, it.h, row, lane_addr + kColAcc, BF16, row < a.N, it.n_sub == 0);
+      store_cols<D / 2>(a.dq, a.dqs, it.z, it.h, row, half * (D / 2),
+                        lane_addr + kColAcc + half * (D / 2), BF16, row < a.N, it.n_sub == 0);
       tc_fence_before();
     }
   }
@@ -381,12 +382,12 @@ template <int D>
 struct DkvLayout {
   static constexpr uint32_t kK = 0;                         // [128][D]
   static constexpr uint32_t kV = kRows * D * 2;             // [128][D]
-  static constexpr uint32_t kQD = 2 * kRows * D * 2;        // stages x (Q [64][D], dO [64][D])
-  static constexpr uint32_t kStage = 2 * kSub * D * 2;
+  static constexpr uint32_t kQD = 2 * kRows * D * 2;        // stages x (Q, dO, stats)
+  static constexpr uint32_t kStats = 2 * kSub * D * 2;      // stage offset: lse2[64], delta[64]
+  static constexpr uint32_t kStage = kStats + 1024;         // keeps the tiles 1024-aligned
   static constexpr uint32_t kPT = kQD + kStages * kStage;   // P^T [128][64]
   static constexpr uint32_t kDST = kPT + kRows * kSub * 2;  // dS^T [128][64]
-  static constexpr uint32_t kLD = kDST + kRows * kSub * 2;  // 2 x (lse2[64], delta[64]) fp32
-  static constexpr uint32_t kBars = kLD + 2 * 2 * kSub * 4;
+  static constexpr uint32_t kBars = kDST + kRows * kSub * 2;
   static constexpr uint32_t kAlloc = kBars + 256 + 1024;
 };
 
@@ -451,8 +452,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
   if (threadIdx.x == 0) {
     uint32_t cnt[KV_NUM];
     for (int i = 0; i < KV_NUM; ++i) cnt[i] = 1;
-    cnt[KV_SEMPTY0] = cnt[KV_SEMPTY0 + 1] = 128;
-    cnt[KV_PFULL] = 128;
+    cnt[KV_SEMPTY0] = cnt[KV_SEMPTY0 + 1] = kEwThreads;
+    cnt[KV_PFULL] = kEwThreads;
     init_bars(bars, cnt, KV_NUM);
   }
   if (warp == 1) {
@@ -488,13 +489,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
           const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
           if (!mbar_wait(&bars[KV_QEMPTY0 + st], ph ^ 1, a.status)) return false;
           unsigned char* stage = sm + L::kQD + st * L::kStage;
-          mbar_arrive_expect_tx(&bars[KV_QFULL0 + st], L::kStage);
+          mbar_arrive_expect_tx(&bars[KV_QFULL0 + st], L::kStats + 2 * kSub * 4);
           for (int c = 0; c < D / 64; ++c) {
             tma_load_4d(stage + c * kSub * 128, &a.tm_q, &bars[KV_QFULL0 + st], c * 64, (int)q0,
                         (int)h, (int)it.z);
             tma_load_4d(stage + kSub * D * 2 + c * kSub * 128, &a.tm_do, &bars[KV_QFULL0 + st],
                         c * 64, (int)q0, (int)h, (int)it.z);
           }
+          const int64_t zh = it.z * a.H + h;
+          bulk_load(stage + L::kStats, a.stats + (zh * ((a.N + kSub - 1) / kSub) + q0 / kSub) * 2 * kSub,
+                    2 * kSub * 4, &bars[KV_QFULL0 + st]);
           ++qd;
           return true;
         });
@@ -566,75 +570,58 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;    // which 32 of the 64 query columns
     const int rl = quarter * 32 + lane;  // key row within the tile
-    const int tid = threadIdx.x - 64;    // 0..127 among the elementwise warps
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const float scale2 = a.scale * kLog2e;
-    float* s_ld = reinterpret_cast<float*>(sm + L::kLD);  // [2][2][64]
-    uint32_t s_it = 0, p_it = 0, done_it = 0, ld_it = 0;
+    uint32_t s_it = 0, p_it = 0, done_it = 0, qd = 0;
     bool ok = true;
     for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
       const KvItem it = kv_item(a, item);
       const int n = kv_item_tiles(a, it);
       const int64_t key = it.k0 + rl;
       ok = for_each_qtile(a, it, [&](int64_t h, int64_t qb, int64_t slot, int64_t q0) -> bool {
-        const int64_t zh = it.z * a.H + h;
-        // stage this sub-tile's lse*log2e and Delta in shared memory (double buffered)
-        float* buf = s_ld + (ld_it & 1) * 2 * kSub;
-        {
-          const int j = tid & (kSub - 1);
-          const int64_t r = q0 + j;
-          if (tid < kSub) {
-            const float lv = r < a.N ? a.lse[zh * a.N + r] : -INFINITY;
-            buf[j] = lv == -INFINITY ? 0.f : lv * kLog2e;  // block_list.py:553 (lse_safe)
-          } else {
-            buf[kSub + j] = r < a.N ? a.delta[zh * a.N + r] : 0.f;
-          }
-        }
-        named_bar_sync(1, 128);
-        ++ld_it;
+        // the stage's TMA writes (Q, dO, row stats) are visible once its phase completed
+        const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
+        ++qd;
+        if (!mbar_wait(&bars[KV_QFULL0 + st], ph, a.status)) return false;
+        const float* stats = reinterpret_cast<const float*>(sm + L::kQD + st * L::kStage + L::kStats);
         const float b2 = bias_log2(a, it.z, h, qb, slot);
         const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
         if (!mbar_wait(&bars[KV_SFULL0 + sb], sph, a.status)) return false;
         tc_fence_after();
-        float s[kSub], dp[kSub];
-#pragma unroll
-        for (int c = 0; c < kSub / 32; ++c) {
-          float t0[32], t1[32];
-          tmem_ld32(lane_addr + kColS + sb * kSub + c * 32, t0);
-          tmem_ld32(lane_addr + kColP + sb * kSub + c * 32, t1);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            s[c * 32 + i] = t0[i];
-            dp[c * 32 + i] = t1[i];
-          }
-        }
+        float s[32], dp[32];
+        tmem_ld32(lane_addr + kColS + sb * kSub + half * 32, s);
+        tmem_ld32(lane_addr + kColP + sb * kSub + half * 32, dp);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars[KV_SEMPTY0 + sb]);
         ++s_it;
         // query q0 + c sees this key iff key < N, q0 + c < N and, when causal, key <= q0 + c
+        const int64_t qh = q0 + half * 32;
         const bool key_ok = key < a.N;
-        const int64_t cmin = a.causal ? key - q0 : 0;  // first visible query offset
-        const int64_t cend = a.N - q0;                 // queries at offsets >= cend are padding
-        uint32_t pk[kSub / 2], dk[kSub / 2];
+        const int64_t cmin = a.causal ? key - qh : 0;  // first visible query offset
+        const int64_t cend = a.N - qh;                 // offsets >= cend are padding rows
+        const float* l2 = stats + half * 32;
+        const float* dl = stats + kSub + half * 32;
+        uint32_t pk[16], dk[16];
 #pragma unroll
-        for (int c = 0; c < kSub; c += 2) {
+        for (int c = 0; c < 32; c += 2) {
           float p0 = 0.f, p1 = 0.f, d0 = 0.f, d1 = 0.f;
           if (key_ok && c >= cmin && c < cend) {
-            p0 = fast_exp2(fmaf(s[c], scale2, b2) - buf[c]);
-            d0 = p0 * (dp[c] - buf[kSub + c]) * a.scale;
+            p0 = fast_exp2(fmaf(s[c], scale2, b2) - l2[c]);
+            d0 = p0 * (dp[c] - dl[c]) * a.scale;
           }
           if (key_ok && c + 1 >= cmin && c + 1 < cend) {
-            p1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - buf[c + 1]);
-            d1 = p1 * (dp[c + 1] - buf[kSub + c + 1]) * a.scale;
+            p1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - l2[c + 1]);
+            d1 = p1 * (dp[c + 1] - dl[c + 1]) * a.scale;
           }
           pk[c / 2] = pack2(p0, p1, BF16);
           dk[c / 2] = pack2(d0, d1, BF16);
         }
         if (!mbar_wait(&bars[KV_PEMPTY], (p_it & 1) ^ 1, a.status)) return false;
-        st_row_sw128(sm + L::kPT, rl, pk);
-        st_row_sw128(sm + L::kDST, rl, dk);
+        st_half_row_sw128(sm + L::kPT, rl, half * 4, pk);
+        st_half_row_sw128(sm + L::kDST, rl, half * 4, dk);
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&bars[KV_PFULL]);
@@ -647,8 +634,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         ++done_it;
         tc_fence_after();
       }
-      store_row<D>(a.dv, a.dvs, it.z, it.hk, key, lane_addr + kColAcc, BF16, key < a.N, n == 0);
-      store_row<D>(a.dk, a.dks, it.z, it.hk, key, lane_addr + kColAcc + D, BF16, key < a.N, n == 0);
+      const int c0 = half * (D / 2);
+      store_cols<D / 2>(a.dv, a.dvs, it.z, it.hk, key, c0, lane_addr + kColAcc + c0, BF16,
+                        key < a.N, n == 0);
+      store_cols<D / 2>(a.dk, a.dks, it.z, it.hk, key, c0, lane_addr + kColAcc + D + c0, BF16,
+                        key < a.N, n == 0);
       tc_fence_before();
     }
   }
@@ -686,6 +676,7 @@ int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
     a.dvs[i] = p.dvs[i];
   }
   a.dbias = p.dbias;
+  a.stats = p.stats;
   a.dq = p.dq;
   a.dk = p.dk;
   a.dv = p.dv;

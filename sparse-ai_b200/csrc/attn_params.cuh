@@ -29,6 +29,7 @@ struct AttnParams {
   const void* dout;
   int64_t dos[4];
   float* delta;  // (Z, H, N) fp32 workspace
+  float* stats;  // (Z*H, ceil(N/64), {lse*log2e[64], delta[64]}) fp32 workspace
   const int32_t* k_lists;  // transposed lists (Z, H, NB, NB) + slots
   const int32_t* k_slots;
   const int32_t* q_counts;

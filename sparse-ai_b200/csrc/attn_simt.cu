@@ -122,20 +122,36 @@ __global__ void __launch_bounds__(kThreads) fwd_simt_kernel(AttnParams p) {
   }
 }
 
-// Delta_i = sum_d dO_i,d * O_i,d in fp32 (block_list.py:785).  One warp per row.
+// Delta_i = sum_d dO_i,d * O_i,d in fp32 (block_list.py:785).  One warp per row; the grid
+// covers the rows padded to a multiple of 64 so the row-stats array is fully written:
+// stats[zh][row / 64] = {lse*log2e (0 for -inf rows, as lse_safe in block_list.py:553),
+// Delta}, 64 + 64 floats per 64-row block, zeros for the padding rows.  The tcgen05 dK/dV
+// kernel bulk-copies one 512-byte block per 64-row query sub-tile.
 template <typename T>
 __global__ void delta_kernel(AttnParams p) {
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (gw >= p.Z * p.H * p.N) return;
-  const int64_t row = gw % p.N, zh = gw / p.N, z = zh / p.H, h = zh % p.H;
-  const T* o = static_cast<const T*>(p.out) + z * p.os[0] + h * p.os[1] + row * p.os[2];
-  const T* g = static_cast<const T*>(p.dout) + z * p.dos[0] + h * p.dos[1] + row * p.dos[2];
-  float a = 0.f;
-  for (int64_t d = lane; d < p.D; d += 32) a = fmaf(to_f32<T>(o[d]), to_f32<T>(g[d]), a);
+  const int64_t npad = (p.N + 63) / 64 * 64;
+  if (gw >= p.Z * p.H * npad) return;
+  const int64_t row = gw % npad, zh = gw / npad, z = zh / p.H, h = zh % p.H;
+  float a = 0.f, l2 = 0.f;
+  if (row < p.N) {
+    const T* o = static_cast<const T*>(p.out) + z * p.os[0] + h * p.os[1] + row * p.os[2];
+    const T* g = static_cast<const T*>(p.dout) + z * p.dos[0] + h * p.dos[1] + row * p.dos[2];
+    for (int64_t d = lane; d < p.D; d += 32) a = fmaf(to_f32<T>(o[d]), to_f32<T>(g[d]), a);
 #pragma unroll
-  for (int off = 16; off; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
-  if (lane == 0) p.delta[zh * p.N + row] = a;
+    for (int off = 16; off; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+    const float lv = p.lse[zh * p.N + row];
+    l2 = lv == -INFINITY ? 0.f : lv * kLog2e;
+  }
+  if (lane == 0) {
+    if (row < p.N) p.delta[zh * p.N + row] = a;
+    if (p.stats) {
+      float* st = p.stats + (zh * (npad / 64) + row / 64) * 128;
+      st[row % 64] = l2;
+      st[64 + row % 64] = a;
+    }
+  }
 }
 
 // dQ over the forward lists (+ soft-bias gradient).  grid (ceil(N / kBM), Z*H).
@@ -422,7 +438,7 @@ int launch_bwd_simt(const AttnParams& p, cudaStream_t s, int parts) {
 }
 
 int launch_delta(const AttnParams& p, cudaStream_t s) {
-  const int64_t rows = p.Z * p.H * p.N;
+  const int64_t rows = p.Z * p.H * ((p.N + 63) / 64 * 64);
   if (rows == 0) return SA_OK;
   const int threads = 256;
   const int64_t blocks = (rows * 32 + threads - 1) / threads;
