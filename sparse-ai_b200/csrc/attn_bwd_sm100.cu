@@ -129,6 +129,15 @@ __device__ __forceinline__ void st_half_row_sw128(unsigned char* chunk, int row,
   }
 }
 
+// Per streamed stage: what the producer read from the lists, handed to the elementwise
+// warps through shared memory (released by the stage's full mbarrier), so that no consumer
+// reads the lists from global memory on its critical path.
+struct StageMeta {
+  int64_t start;  // first key (dQ kernel) or first query (dK/dV kernel) of the sub-tile
+  float b2;       // soft-bias * log2(e) of the block pair
+  int pad;
+};
+
 __device__ __forceinline__ void init_bars(uint64_t* bars, const uint32_t* counts, int n) {
   for (int i = 0; i < n; ++i) mbar_init(&bars[i], counts[i]);
   fence_mbar_init();
@@ -145,7 +154,8 @@ struct DqLayout {
   static constexpr uint32_t kStage = 2 * kSub * D * 2;
   static constexpr uint32_t kDS = kKV + kStages * kStage;    // 2 x [128][64]
   static constexpr uint32_t kBars = kDS + 2 * kRows * kSub * 2;
-  static constexpr uint32_t kAlloc = kBars + 256 + 1024;
+  static constexpr uint32_t kMeta = kBars + 256;  // StageMeta[kStages]
+  static constexpr uint32_t kAlloc = kMeta + 256 + 1024;
 };
 
 enum { DQ_QFULL = 0, DQ_QEMPTY, DQ_KVFULL0, DQ_KVEMPTY0 = DQ_KVFULL0 + kStages,
@@ -179,6 +189,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
+  StageMeta* meta = reinterpret_cast<StageMeta*>(sm + L::kMeta);
   __shared__ uint32_t s_tmem;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t items = a.Z * a.H * a.tiles;
@@ -226,6 +237,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
           const uint32_t st = kv % kStages, ph = (kv / kStages) & 1;
           if (!(ok = mbar_wait(&bars[DQ_KVEMPTY0 + st], ph ^ 1, a.status))) break;
           unsigned char* stage = sm + L::kKV + st * L::kStage;
+          meta[st].start = k0;
+          meta[st].b2 = bias_log2(a, it.z, it.h, it.qb, j / spb);
           mbar_arrive_expect_tx(&bars[DQ_KVFULL0 + st], L::kStage);
           for (int c = 0; c < D / 64; ++c) {
             tma_load_4d(stage + c * kSub * 128, &a.tm_k, &bars[DQ_KVFULL0 + st], c * 64, (int)k0,
@@ -299,7 +312,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
     const int rl = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const float scale2 = a.scale * kLog2e;
-    uint32_t s_it = 0, ds_it = 0, done_it = 0;
+    uint32_t s_it = 0, ds_it = 0, done_it = 0, kv = 0;
     bool ok = true;
     for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
       const DqItem it = dq_item(a, item);
@@ -311,12 +324,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         lse2 = lv == -INFINITY ? 0.f : lv * kLog2e;  // block_list.py:553 (lse_safe)
         dl = a.delta[zh * a.N + row];
       }
-      const int32_t* lst = a.lists + it.row_id * a.list_stride;
       float db_acc = 0.f;
-      for (int j = 0; j < it.n_sub && ok; ++j) {
+      for (int j = 0; j < it.n_sub && ok; ++j, ++kv) {
         const int slot = j / spb;
-        const int64_t k0 = (int64_t)lst[slot] * a.RB + (j % spb) * kSub + half * 32;
-        const float b2 = bias_log2(a, it.z, it.h, it.qb, slot);
+        // this stage's K/V stay resident until the dQ MMA of sub-tile j, which waits for us
+        const uint32_t st = kv % kStages;
+        if (!(ok = mbar_wait(&bars[DQ_KVFULL0 + st], (kv / kStages) & 1, a.status))) break;
+        const int64_t k0 = meta[st].start + half * 32;
+        const float b2 = meta[st].b2;
         const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
         if (!(ok = mbar_wait(&bars[DQ_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
@@ -388,7 +403,8 @@ struct DkvLayout {
   static constexpr uint32_t kPT = kQD + kStages * kStage;   // P^T [128][64]
   static constexpr uint32_t kDST = kPT + kRows * kSub * 2;  // dS^T [128][64]
   static constexpr uint32_t kBars = kDST + kRows * kSub * 2;
-  static constexpr uint32_t kAlloc = kBars + 256 + 1024;
+  static constexpr uint32_t kMeta = kBars + 256;  // StageMeta[kStages]
+  static constexpr uint32_t kAlloc = kMeta + 256 + 1024;
 };
 
 enum { KV_KVFULL = 0, KV_KVEMPTY, KV_QFULL0, KV_QEMPTY0 = KV_QFULL0 + kStages,
@@ -445,6 +461,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
+  StageMeta* meta = reinterpret_cast<StageMeta*>(sm + L::kMeta);
   __shared__ uint32_t s_tmem;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t items = a.Z * a.Hkv * a.tiles;
@@ -485,10 +502,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
           tma_load_4d(sm + L::kV + c * kRows * 128, &a.tm_v, &bars[KV_KVFULL], c * 64, (int)it.k0,
                       (int)it.hk, (int)it.z);
         }
-        ok = for_each_qtile(a, it, [&](int64_t h, int64_t, int64_t, int64_t q0) -> bool {
+        ok = for_each_qtile(a, it, [&](int64_t h, int64_t qb, int64_t slot, int64_t q0) -> bool {
           const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
           if (!mbar_wait(&bars[KV_QEMPTY0 + st], ph ^ 1, a.status)) return false;
           unsigned char* stage = sm + L::kQD + st * L::kStage;
+          meta[st].start = q0;
+          meta[st].b2 = bias_log2(a, it.z, h, qb, slot);
           mbar_arrive_expect_tx(&bars[KV_QFULL0 + st], L::kStats + 2 * kSub * 4);
           for (int c = 0; c < D / 64; ++c) {
             tma_load_4d(stage + c * kSub * 128, &a.tm_q, &bars[KV_QFULL0 + st], c * 64, (int)q0,
@@ -538,12 +557,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         if (!(ok = mbar_wait(&bars[KV_KVFULL], jk & 1, a.status))) break;
         ++jk;
         const uint32_t qd0 = qd;
-        int i = 0;
-        ok = for_each_qtile(a, it, [&](int64_t, int64_t, int64_t, int64_t) -> bool {
+        for (int i = 0; i < n && ok; ++i) {
           const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
           const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
-          if (!mbar_wait(&bars[KV_QFULL0 + st], ph, a.status)) return false;
-          if (!mbar_wait(&bars[KV_SEMPTY0 + sb], sph ^ 1, a.status)) return false;
+          if (!(ok = mbar_wait(&bars[KV_QFULL0 + st], ph, a.status))) break;
+          if (!(ok = mbar_wait(&bars[KV_SEMPTY0 + sb], sph ^ 1, a.status))) break;
           tc_fence_after();
           const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
           const uint32_t do_addr = q_addr + kSub * D * 2;
@@ -559,11 +577,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
           tc_commit(&bars[KV_SFULL0 + sb]);
           if (i == n - 1) tc_commit(&bars[KV_KVEMPTY]);
           ++s_it;
-          if (i > 0 && !issue_acc(qd0 + i - 1, i - 1 == 0)) return false;
+          if (i > 0) ok = issue_acc(qd0 + i - 1, i - 1 == 0);
           ++qd;
-          ++i;
-          return true;
-        });
+        }
         if (ok) ok = issue_acc(qd0 + n - 1, n == 1);
         if (ok) tc_commit(&bars[KV_DONE]);
       }
@@ -580,15 +596,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
       const KvItem it = kv_item(a, item);
       const int n = kv_item_tiles(a, it);
       const int64_t key = it.k0 + rl;
-      ok = for_each_qtile(a, it, [&](int64_t h, int64_t qb, int64_t slot, int64_t q0) -> bool {
-        // the stage's TMA writes (Q, dO, row stats) are visible once its phase completed
+      for (int i = 0; i < n && ok; ++i) {
+        // the stage's TMA writes (Q, dO, row stats) and its meta are visible once its phase
+        // completed; the stage stays resident until the dV/dK MMAs of this sub-tile
         const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
         ++qd;
-        if (!mbar_wait(&bars[KV_QFULL0 + st], ph, a.status)) return false;
+        if (!(ok = mbar_wait(&bars[KV_QFULL0 + st], ph, a.status))) break;
         const float* stats = reinterpret_cast<const float*>(sm + L::kQD + st * L::kStage + L::kStats);
-        const float b2 = bias_log2(a, it.z, h, qb, slot);
+        const int64_t q0 = meta[st].start;
+        const float b2 = meta[st].b2;
         const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
-        if (!mbar_wait(&bars[KV_SFULL0 + sb], sph, a.status)) return false;
+        if (!(ok = mbar_wait(&bars[KV_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
         float s[32], dp[32];
         tmem_ld32(lane_addr + kColS + sb * kSub + half * 32, s);
@@ -619,15 +637,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
           pk[c / 2] = pack2(p0, p1, BF16);
           dk[c / 2] = pack2(d0, d1, BF16);
         }
-        if (!mbar_wait(&bars[KV_PEMPTY], (p_it & 1) ^ 1, a.status)) return false;
+        if (!(ok = mbar_wait(&bars[KV_PEMPTY], (p_it & 1) ^ 1, a.status))) break;
         st_half_row_sw128(sm + L::kPT, rl, half * 4, pk);
         st_half_row_sw128(sm + L::kDST, rl, half * 4, dk);
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&bars[KV_PFULL]);
         ++p_it;
-        return true;
-      });
+      }
       if (!ok) break;
       if (n > 0) {
         if (!(ok = mbar_wait(&bars[KV_DONE], done_it & 1, a.status))) break;

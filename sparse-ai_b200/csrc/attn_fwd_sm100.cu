@@ -64,6 +64,15 @@ struct FwdLayout {
 enum { B_QFULL = 0, B_QEMPTY, B_KFULL0, B_KFULL1, B_KEMPTY0, B_KEMPTY1, B_VFULL0, B_VFULL1,
        B_VEMPTY0, B_VEMPTY1, B_SFULL0, B_SFULL1, B_SEMPTY0, B_SEMPTY1, B_PFULL, B_ODONE, B_NUM };
 
+// Per K/V stage: what the producer learned from the lists, handed to the softmax warps
+// through shared memory (released by the stage's V mbarrier) so that no consumer reads
+// the lists from global memory on its critical path.
+struct TileMeta {
+  int64_t key_start;
+  float b2;  // soft-bias * log2(e) of the block pair
+  int pad;
+};
+
 struct ItemInfo {
   int64_t z, h, hk, q_start, qb, row_id;
   int count, n_sub;
@@ -107,6 +116,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
+  TileMeta* meta = reinterpret_cast<TileMeta*>(sm + L::kBars + 128);  // [2], one per K/V stage
   __shared__ uint32_t s_tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -165,6 +175,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
                         &bars[B_KFULL0 + st], c * 64, (int)ks, (int)it.hk, (int)it.z);
           ok = mbar_wait(&bars[B_VEMPTY0 + st], ph ^ 1, a.status);
           if (!ok) break;
+          meta[st].key_start = ks;
+          meta[st].b2 = a.bias ? load_any_f32(a.bias, a.bias_dtype,
+                                              it.z * a.bs[0] + it.h * a.bs[1] + it.qb * a.bs[2] +
+                                                  (t / (int)(a.RB / kT)) * a.bs[3]) *
+                                     kLog2e
+                               : 0.f;
           mbar_arrive_expect_tx(&bars[B_VFULL0 + st], L::kTileBytes);
           for (int c = 0; c < D / 64; ++c)
             tma_load_4d(sm + L::kV0 + st * L::kTileBytes + c * kT * 128, &a.tm_v,
@@ -235,13 +251,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const float scale2 = a.scale * kLog2e;
     unsigned char* p_tile = sm + L::kP;
-    uint32_t s_it = 0, od = 0;
+    uint32_t s_it = 0, od = 0, kv = 0;
     bool ok = true;
     for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
       const ItemInfo it = item_info(a, item);
       const int64_t row = it.q_start + rl;
       float m_used = -INFINITY, l_sum = 0.f;
-      for (int t = 0; t < it.n_sub && ok; ++t) {
+      for (int t = 0; t < it.n_sub && ok; ++t, ++kv) {
         const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
         if (!mbar_wait(&bars[B_SFULL0 + sb], sph, a.status)) { ok = false; break; }
         tc_fence_after();
@@ -258,14 +274,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         mbar_arrive(&bars[B_SEMPTY0 + sb]);
         ++s_it;
 
-        const int64_t ks = key_start_of(a, it, t);
-        float b2 = 0.f;
-        if (a.bias) {
-          const int spb = (int)(a.RB / kT);
-          b2 = load_any_f32(a.bias, a.bias_dtype,
-                            it.z * a.bs[0] + it.h * a.bs[1] + it.qb * a.bs[2] + (t / spb) * a.bs[3]) *
-               kLog2e;
-        }
+        // the V stage of this tile stays resident until PV(t), which waits for this warp
+        if (!mbar_wait(&bars[B_VFULL0 + (kv & 1)], (kv >> 1) & 1, a.status)) { ok = false; break; }
+        const int64_t ks = meta[kv & 1].key_start;
+        const float b2 = meta[kv & 1].b2;
         // keys key_start + c are visible for c <= lim
         int64_t lim = a.N - 1 - ks;
         if (a.causal) lim = min(lim, row - ks);
