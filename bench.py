@@ -260,8 +260,10 @@ class C2Problem:
         self.dq = torch.empty_like(self.q)
         self.dk = torch.empty_like(self.k)
         self.dv = torch.empty_like(self.v)
-        wsb = int(nat.lib().sa_block_list_attention_bwd_workspace_bytes(Z, H, N, RB))
+        wsb = int(nat.lib().sa_block_list_attention_bwd_workspace_bytes(Z, H, Hkv, N, D, RB))
         self.ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        fwb = int(nat.lib().sa_block_list_attention_fwd_workspace_bytes(Z, H, N, D, RB))
+        self.fws = torch.empty(max(fwb, 256), dtype=torch.uint8, device=dev)
         self.build()
         torch.cuda.synchronize()
         self.kept = int(self.counts.sum())
@@ -296,7 +298,7 @@ class C2Problem:
             self.k.data_ptr(), nat.strides(self.k), self.v.data_ptr(), nat.strides(self.v),
             self.out.data_ptr(), nat.strides(self.out), self.lse.data_ptr(),
             self.lists.data_ptr(), self.NB, self.counts.data_ptr(), None, 0, None,
-            int(self.causal), self.scale, s), "fwd")
+            int(self.causal), self.scale, self.fws.data_ptr(), self.fws.numel(), s), "fwd")
 
     def bwd(self, phase):
         nat, s = self.nat, torch.cuda.current_stream().cuda_stream
@@ -312,7 +314,8 @@ class C2Problem:
             f"bwd phase {phase}")
 
     PARTS = ("build", "fwd", "prep", "dq", "dkdv")
-    LAUNCHES = {"build": 1, "fwd": 1, "prep": 2, "dq": 1, "dkdv": 1}
+    # fwd: planner + kernel; prep: delta, transposed lists, 2 planners; dkdv: kernel + split reduce
+    LAUNCHES = {"build": 1, "fwd": 2, "prep": 4, "dq": 1, "dkdv": 2}
 
     def step(self, evs):
         evs[0].record()

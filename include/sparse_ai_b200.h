@@ -110,6 +110,9 @@ SA_API int sa_build_transposed_block_lists(const int32_t* lists, int64_t list_st
  * lists/counts  int32 (Z, H, NB, list_stride) contiguous / (Z, H, NB), NB = ceil(N/route_block).
  * soft_bias     optional (Z, H, NB, list_stride) of sb_dtype with sb_strides, or NULL.
  * lse           optional fp32 (Z, H, N) contiguous, or NULL.
+ * workspace     optional, >= sa_block_list_attention_fwd_workspace_bytes() bytes, 256-aligned:
+ *               the tcgen05 kernel then schedules its work items heaviest-first from a queue
+ *               (NULL: static round-robin; same results either way).
  */
 SA_API int sa_block_list_attention_fwd(int dtype, int64_t Z, int64_t H, int64_t Hkv, int64_t N,
                                 int64_t D, int64_t route_block,
@@ -119,11 +122,16 @@ SA_API int sa_block_list_attention_fwd(int dtype, int64_t Z, int64_t H, int64_t 
                                 void* out, const int64_t* out_strides, float* lse,
                                 const int32_t* lists, int64_t list_stride, const int32_t* counts,
                                 const void* soft_bias, int sb_dtype, const int64_t* sb_strides,
-                                int is_causal, float sm_scale, void* stream);
+                                int is_causal, float sm_scale,
+                                void* workspace, int64_t workspace_bytes, void* stream);
 
-/* Bytes of workspace sa_block_list_attention_bwd needs for these sizes. */
-SA_API int64_t sa_block_list_attention_bwd_workspace_bytes(int64_t Z, int64_t H, int64_t N,
-                                                    int64_t route_block);
+/* Bytes of (optional) workspace for sa_block_list_attention_fwd, on the current device. */
+SA_API int64_t sa_block_list_attention_fwd_workspace_bytes(int64_t Z, int64_t H, int64_t N,
+                                                    int64_t D, int64_t route_block);
+
+/* Bytes of workspace sa_block_list_attention_bwd needs for these sizes, on the current device. */
+SA_API int64_t sa_block_list_attention_bwd_workspace_bytes(int64_t Z, int64_t H, int64_t Hkv,
+                                                    int64_t N, int64_t D, int64_t route_block);
 
 /*
  * Block-list attention backward.

@@ -3,7 +3,7 @@
 // route_block a multiple of 128) or to the CUDA-core kernels (everything else, fp32).
 #include <string>
 
-#include "attn_params.cuh"
+#include "attn_plan.cuh"
 
 namespace sa {
 namespace {
@@ -68,7 +68,8 @@ int sa_block_list_attention_fwd(int dtype, int64_t Z, int64_t H, int64_t Hkv, in
                                 const int64_t* out_strides, float* lse, const int32_t* lists,
                                 int64_t list_stride, const int32_t* counts, const void* soft_bias,
                                 int sb_dtype, const int64_t* sb_strides, int is_causal,
-                                float sm_scale, void* stream) {
+                                float sm_scale, void* workspace, int64_t workspace_bytes,
+                                void* stream) {
   using namespace sa;
   AttnParams p{};
   int rc = fill_common(p, dtype, Z, H, Hkv, N, D, route_block, q, q_strides, k, k_strides, v,
@@ -82,21 +83,36 @@ int sa_block_list_attention_fwd(int dtype, int64_t Z, int64_t H, int64_t Hkv, in
   p.lse = lse;
   if (Z * H * N == 0) return SA_OK;
   if (!q || !k || !v || !out || !lists || !counts) return fail(SA_EINVAL, "null pointer argument");
+  if (workspace) {
+    if (reinterpret_cast<uintptr_t>(workspace) % 256)
+      return fail(SA_EINVAL, "workspace must be 256-byte aligned");
+    if (workspace_bytes < fwd_plan_bytes(Z, H, N, D))
+      return fail(SA_EWORKSPACE, "forward workspace too small");
+    p.plan_fwd = workspace;
+  }
   cudaStream_t s = (cudaStream_t)stream;
   rc = launch_fwd_sm100(p, s);
   if (rc != SA_EUNSUPPORTED) return rc;
   return launch_fwd_simt(p, s);
 }
 
-int64_t sa_block_list_attention_bwd_workspace_bytes(int64_t Z, int64_t H, int64_t N,
+int64_t sa_block_list_attention_fwd_workspace_bytes(int64_t Z, int64_t H, int64_t N, int64_t D,
                                                     int64_t route_block) {
+  if (Z <= 0 || H <= 0 || N <= 0 || D <= 0 || route_block <= 0) return 0;
+  return sa::fwd_plan_bytes(Z, H, N, D);
+}
+
+int64_t sa_block_list_attention_bwd_workspace_bytes(int64_t Z, int64_t H, int64_t Hkv, int64_t N,
+                                                    int64_t D, int64_t route_block) {
   using sa::align256;
-  if (Z <= 0 || H <= 0 || N <= 0 || route_block <= 0) return 0;
+  if (Z <= 0 || H <= 0 || Hkv <= 0 || N <= 0 || D <= 0 || route_block <= 0) return 0;
   const int64_t NB = (N + route_block - 1) / route_block;
   size_t b = align256((size_t)Z * H * N * sizeof(float));            // delta
   b += 2 * align256((size_t)Z * H * NB * NB * sizeof(int32_t));       // k_lists, k_slots
   b += align256((size_t)Z * H * NB * sizeof(int32_t));                // q_counts
   b += align256((size_t)Z * H * ((N + 63) / 64) * 128 * sizeof(float));  // row stats
+  b += align256((size_t)sa::bwd_plan_bytes(sa::kPlanDq, Z, H, Hkv, N, D));
+  b += align256((size_t)sa::bwd_plan_bytes(sa::kPlanDkdv, Z, H, Hkv, N, D));
   return (int64_t)b;
 }
 
@@ -139,7 +155,7 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
   if (Z * H * N == 0) return SA_OK;
   if (!q || !k || !v || !out || !dout || !lse || !lists || !counts || !dq || !dk || !dv)
     return fail(SA_EINVAL, "null pointer argument");
-  const int64_t need = sa_block_list_attention_bwd_workspace_bytes(Z, H, N, route_block);
+  const int64_t need = sa_block_list_attention_bwd_workspace_bytes(Z, H, Hkv, N, D, route_block);
   if (!workspace || workspace_bytes < need)
     return fail(SA_EWORKSPACE, "backward workspace too small (" + std::to_string(workspace_bytes) +
                                    " < " + std::to_string(need) + ")");
@@ -157,6 +173,10 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
   int32_t* q_counts = reinterpret_cast<int32_t*>(w);
   w += align256((size_t)Z * H * NB * sizeof(int32_t));
   p.stats = reinterpret_cast<float*>(w);
+  w += align256((size_t)Z * H * ((N + 63) / 64) * 128 * sizeof(float));
+  p.plan_dq = w;
+  w += align256((size_t)bwd_plan_bytes(kPlanDq, Z, H, Hkv, N, D));
+  p.plan_dkdv = w;
   p.k_lists = k_lists;
   p.k_slots = k_slots;
   p.q_counts = q_counts;
@@ -167,6 +187,8 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
     if (rc) return rc;
     rc = launch_transpose_lists(lists, list_stride, counts, Z * H, NB, NB, k_lists, NB, q_counts,
                                 k_slots, 0, s);
+    if (rc) return rc;
+    rc = plan_bwd_sm100(p, s);  // work queues of the tcgen05 dQ and dK/dV kernels
     if (rc) return rc;
     if (d_soft_bias) {
       if (cudaMemsetAsync(d_soft_bias, 0, (size_t)Z * H * NB * list_stride * sizeof(float), s) !=

@@ -27,7 +27,7 @@
 #include <string>
 #include <type_traits>
 
-#include "attn_params.cuh"
+#include "sched.cuh"
 
 namespace sa {
 namespace {
@@ -66,6 +66,8 @@ struct BwdArgs {
   int causal;
   float scale;
   unsigned* status;
+  SchedArgs sched;
+  float* partials;  // dK/dV: fp32 [slot][128][dV D | dK D] for split chunks
 };
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
@@ -155,16 +157,17 @@ struct DqLayout {
   static constexpr uint32_t kDS = kKV + kStages * kStage;    // 2 x [128][64]
   static constexpr uint32_t kBars = kDS + 2 * kRows * kSub * 2;
   static constexpr uint32_t kMeta = kBars + 256;  // StageMeta[kStages]
-  static constexpr uint32_t kAlloc = kMeta + 256 + 1024;
+  static constexpr uint32_t kRingOff = kMeta + 128;  // WorkEntry[kRing]
+  static constexpr uint32_t kAlloc = kRingOff + 128 + 1024;
 };
 
 enum { DQ_QFULL = 0, DQ_QEMPTY, DQ_KVFULL0, DQ_KVEMPTY0 = DQ_KVFULL0 + kStages,
        DQ_SFULL0 = DQ_KVEMPTY0 + kStages, DQ_SEMPTY0 = DQ_SFULL0 + 2, DQ_DSFULL0 = DQ_SEMPTY0 + 2,
-       DQ_DSEMPTY0 = DQ_DSFULL0 + 2, DQ_DONE = DQ_DSEMPTY0 + 2, DQ_NUM };
+       DQ_DSEMPTY0 = DQ_DSFULL0 + 2, DQ_DONE = DQ_DSEMPTY0 + 2, DQ_WFULL0,
+       DQ_WEMPTY0 = DQ_WFULL0 + kRing, DQ_NUM = DQ_WEMPTY0 + kRing };
 
 struct DqItem {
   int64_t z, h, hk, q_start, qb, row_id;
-  int n_sub;  // 64-key sub-tiles
 };
 
 __device__ __forceinline__ DqItem dq_item(const BwdArgs& a, int64_t item) {
@@ -178,8 +181,12 @@ __device__ __forceinline__ DqItem dq_item(const BwdArgs& a, int64_t item) {
   it.q_start = qt * kRows;
   it.qb = it.q_start / a.RB;
   it.row_id = zh * a.NB + it.qb;
-  it.n_sub = a.counts[it.row_id] * (int)(a.RB / kSub);
   return it;
+}
+
+// 64-key sub-tiles of a dQ item: the static-schedule weight.
+__device__ __forceinline__ int dq_item_tiles(const BwdArgs& a, int64_t item) {
+  return a.counts[dq_item(a, item).row_id] * (int)(a.RB / kSub);
 }
 
 template <int D, bool BF16>
@@ -190,9 +197,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
   StageMeta* meta = reinterpret_cast<StageMeta*>(sm + L::kMeta);
+  WorkEntry* ring = reinterpret_cast<WorkEntry*>(sm + L::kRingOff);
   __shared__ uint32_t s_tmem;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t items = a.Z * a.H * a.tiles;
   const int spb = (int)(a.RB / kSub);
 
   if (threadIdx.x == 0) {
@@ -200,6 +207,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
     for (int i = 0; i < DQ_NUM; ++i) cnt[i] = 1;
     cnt[DQ_SEMPTY0] = cnt[DQ_SEMPTY0 + 1] = kEwThreads;
     cnt[DQ_DSFULL0] = cnt[DQ_DSFULL0 + 1] = kEwThreads;
+    for (int i = 0; i < kRing; ++i) cnt[DQ_WEMPTY0 + i] = 1 + kEwThreads;
     init_bars(bars, cnt, DQ_NUM);
   }
   if (warp == 1) {
@@ -219,9 +227,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
       prefetch_tmap(&a.tm_v);
       uint32_t kv = 0, jq = 0;
       bool ok = true;
-      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const DqItem it = dq_item(a, item);
-        if (it.n_sub == 0) continue;
+      const int n_entries = a.sched.header ? a.sched.header->n_entries : 0;
+      for (uint32_t w = 0; ok; ++w) {
+        const WorkEntry e =
+            sched_fetch(a.sched, n_entries, w, [&](int64_t i) { return dq_item_tiles(a, i); });
+        if (!(ok = ring_put(ring, &bars[DQ_WFULL0], &bars[DQ_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const DqItem it = dq_item(a, e.item);
+        if (e.end == e.begin) continue;
         if (!(ok = mbar_wait(&bars[DQ_QEMPTY], (jq & 1) ^ 1, a.status))) break;
         ++jq;
         mbar_arrive_expect_tx(&bars[DQ_QFULL], 2 * kRows * D * 2);
@@ -232,7 +245,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
                       (int)it.q_start, (int)it.h, (int)it.z);
         }
         const int32_t* lst = a.lists + it.row_id * a.list_stride;
-        for (int j = 0; j < it.n_sub && ok; ++j, ++kv) {
+        for (int j = e.begin; j < e.end && ok; ++j, ++kv) {
           const int64_t k0 = (int64_t)lst[j / spb] * a.RB + (j % spb) * kSub;
           const uint32_t st = kv % kStages, ph = (kv / kStages) & 1;
           if (!(ok = mbar_wait(&bars[DQ_KVEMPTY0 + st], ph ^ 1, a.status))) break;
@@ -273,13 +286,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         ++ds_it;
         return true;
       };
-      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const DqItem it = dq_item(a, item);
-        if (it.n_sub == 0) continue;
+      for (uint32_t w = 0; ok; ++w) {
+        WorkEntry e;
+        if (!(ok = ring_get(ring, &bars[DQ_WFULL0], &bars[DQ_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const int n_sub = e.end - e.begin;
+        if (n_sub == 0) continue;
         if (!(ok = mbar_wait(&bars[DQ_QFULL], jq & 1, a.status))) break;
         ++jq;
         const uint32_t kv0 = kv;
-        for (int j = 0; j < it.n_sub && ok; ++j, ++kv) {
+        for (int j = 0; j < n_sub && ok; ++j, ++kv) {
           const uint32_t st = kv % kStages, ph = (kv / kStages) & 1;
           const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
           ok = mbar_wait(&bars[DQ_KVFULL0 + st], ph, a.status) &&
@@ -298,11 +314,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
                        smem_desc(v_addr + ob, 16, 1024), id_s, kk > 0 ? 1u : 0u);
           }
           tc_commit(&bars[DQ_SFULL0 + sb]);
-          if (j == it.n_sub - 1) tc_commit(&bars[DQ_QEMPTY]);
+          if (j == n_sub - 1) tc_commit(&bars[DQ_QEMPTY]);
           ++s_it;
           if (j > 0) ok = issue_dq(kv0 + j - 1, j - 1 == 0);
         }
-        if (ok) ok = issue_dq(kv0 + it.n_sub - 1, it.n_sub == 1);
+        if (ok) ok = issue_dq(kv0 + n_sub - 1, n_sub == 1);
         if (ok) tc_commit(&bars[DQ_DONE]);
       }
     }
@@ -314,8 +330,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
     const float scale2 = a.scale * kLog2e;
     uint32_t s_it = 0, ds_it = 0, done_it = 0, kv = 0;
     bool ok = true;
-    for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
-      const DqItem it = dq_item(a, item);
+    for (uint32_t w = 0; ok; ++w) {
+      WorkEntry e;
+      if (!(ok = ring_get(ring, &bars[DQ_WFULL0], &bars[DQ_WEMPTY0], w, e, a.status))) break;
+      if (e.item < 0) break;
+      const DqItem it = dq_item(a, e.item);
+      const int n_sub = e.end - e.begin;
       const int64_t row = it.q_start + rl;
       const int64_t zh = it.z * a.H + it.h;
       float lse2 = 0.f, dl = 0.f;
@@ -325,7 +345,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         dl = a.delta[zh * a.N + row];
       }
       float db_acc = 0.f;
-      for (int j = 0; j < it.n_sub && ok; ++j, ++kv) {
+      for (int j = e.begin; j < e.end && ok; ++j, ++kv) {
         const int slot = j / spb;
         // this stage's K/V stay resident until the dQ MMA of sub-tile j, which waits for us
         const uint32_t st = kv % kStages;
@@ -372,13 +392,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         }
       }
       if (!ok) break;
-      if (it.n_sub > 0) {
+      if (n_sub > 0) {
         if (!(ok = mbar_wait(&bars[DQ_DONE], done_it & 1, a.status))) break;
         ++done_it;
         tc_fence_after();
       }
       store_cols<D / 2>(a.dq, a.dqs, it.z, it.h, row, half * (D / 2),
-                        lane_addr + kColAcc + half * (D / 2), BF16, row < a.N, it.n_sub == 0);
+                        lane_addr + kColAcc + half * (D / 2), BF16, row < a.N, n_sub == 0);
       tc_fence_before();
     }
   }
@@ -404,12 +424,14 @@ struct DkvLayout {
   static constexpr uint32_t kDST = kPT + kRows * kSub * 2;  // dS^T [128][64]
   static constexpr uint32_t kBars = kDST + kRows * kSub * 2;
   static constexpr uint32_t kMeta = kBars + 256;  // StageMeta[kStages]
-  static constexpr uint32_t kAlloc = kMeta + 256 + 1024;
+  static constexpr uint32_t kRingOff = kMeta + 128;  // WorkEntry[kRing]
+  static constexpr uint32_t kAlloc = kRingOff + 128 + 1024;
 };
 
 enum { KV_KVFULL = 0, KV_KVEMPTY, KV_QFULL0, KV_QEMPTY0 = KV_QFULL0 + kStages,
        KV_SFULL0 = KV_QEMPTY0 + kStages, KV_SEMPTY0 = KV_SFULL0 + 2, KV_PFULL = KV_SEMPTY0 + 2,
-       KV_PEMPTY, KV_DONE, KV_NUM };
+       KV_PEMPTY, KV_DONE, KV_WFULL0, KV_WEMPTY0 = KV_WFULL0 + kRing,
+       KV_NUM = KV_WEMPTY0 + kRing };
 
 struct KvItem {
   int64_t z, hk, k0, kb;
@@ -427,21 +449,28 @@ __device__ __forceinline__ KvItem kv_item(const BwdArgs& a, int64_t item) {
   return it;
 }
 
-// Visit every streamed query sub-tile of a dK/dV work item in a fixed order:
-// query heads of the group, then the transposed list, then 64-row sub-tiles.
+// Visit the streamed query sub-tiles [begin, end) of a dK/dV work item, in the item's fixed
+// order: query heads of the group, then the head's transposed list, then 64-row sub-tiles.
 template <typename F>
-__device__ __forceinline__ bool for_each_qtile(const BwdArgs& a, const KvItem& it, F&& f) {
+__device__ __forceinline__ bool for_each_qtile(const BwdArgs& a, const KvItem& it, int begin,
+                                               int end, F&& f) {
   const int64_t group = a.H / a.Hkv;
   const int spb = (int)(a.RB / kSub);
-  for (int64_t h = it.hk * group; h < (it.hk + 1) * group; ++h) {
+  int pos = 0;
+  for (int64_t h = it.hk * group; h < (it.hk + 1) * group && pos < end; ++h) {
     const int64_t krow = (it.z * a.H + h) * a.NB + it.kb;
-    const int qc = a.q_counts[krow];
-    for (int j = 0; j < qc; ++j) {
+    const int n_h = a.q_counts[krow] * spb;
+    if (pos + n_h <= begin) {
+      pos += n_h;
+      continue;
+    }
+    for (int t = max(0, begin - pos); t < n_h && pos + t < end; ++t) {
+      const int j = t / spb, sub = t % spb;
       const int64_t qb = a.k_lists[krow * a.NB + j];
       const int64_t slot = a.k_slots[krow * a.NB + j];
-      for (int s = 0; s < spb; ++s)
-        if (!f(h, qb, slot, qb * a.RB + s * kSub)) return false;
+      if (!f(h, qb, slot, qb * a.RB + sub * kSub)) return false;
     }
+    pos += n_h;
   }
   return true;
 }
@@ -462,15 +491,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
   StageMeta* meta = reinterpret_cast<StageMeta*>(sm + L::kMeta);
+  WorkEntry* ring = reinterpret_cast<WorkEntry*>(sm + L::kRingOff);
   __shared__ uint32_t s_tmem;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t items = a.Z * a.Hkv * a.tiles;
 
   if (threadIdx.x == 0) {
     uint32_t cnt[KV_NUM];
     for (int i = 0; i < KV_NUM; ++i) cnt[i] = 1;
     cnt[KV_SEMPTY0] = cnt[KV_SEMPTY0 + 1] = kEwThreads;
     cnt[KV_PFULL] = kEwThreads;
+    for (int i = 0; i < kRing; ++i) cnt[KV_WEMPTY0 + i] = 1 + kEwThreads;
     init_bars(bars, cnt, KV_NUM);
   }
   if (warp == 1) {
@@ -490,9 +520,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
       prefetch_tmap(&a.tm_v);
       uint32_t qd = 0, jk = 0;
       bool ok = true;
-      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const KvItem it = kv_item(a, item);
-        if (kv_item_tiles(a, it) == 0) continue;
+      const int n_entries = a.sched.header ? a.sched.header->n_entries : 0;
+      for (uint32_t w = 0; ok; ++w) {
+        const WorkEntry e = sched_fetch(a.sched, n_entries, w,
+                                        [&](int64_t i) { return kv_item_tiles(a, kv_item(a, i)); });
+        if (!(ok = ring_put(ring, &bars[KV_WFULL0], &bars[KV_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const KvItem it = kv_item(a, e.item);
+        if (e.end == e.begin) continue;
         if (!(ok = mbar_wait(&bars[KV_KVEMPTY], (jk & 1) ^ 1, a.status))) break;
         ++jk;
         mbar_arrive_expect_tx(&bars[KV_KVFULL], 2 * kRows * D * 2);
@@ -502,7 +537,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
           tma_load_4d(sm + L::kV + c * kRows * 128, &a.tm_v, &bars[KV_KVFULL], c * 64, (int)it.k0,
                       (int)it.hk, (int)it.z);
         }
-        ok = for_each_qtile(a, it, [&](int64_t h, int64_t qb, int64_t slot, int64_t q0) -> bool {
+        ok = for_each_qtile(a, it, e.begin, e.end,
+                            [&](int64_t h, int64_t qb, int64_t slot, int64_t q0) -> bool {
           const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
           if (!mbar_wait(&bars[KV_QEMPTY0 + st], ph ^ 1, a.status)) return false;
           unsigned char* stage = sm + L::kQD + st * L::kStage;
@@ -550,9 +586,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         ++p_it;
         return true;
       };
-      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const KvItem it = kv_item(a, item);
-        const int n = kv_item_tiles(a, it);
+      for (uint32_t w = 0; ok; ++w) {
+        WorkEntry e;
+        if (!(ok = ring_get(ring, &bars[KV_WFULL0], &bars[KV_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const int n = e.end - e.begin;
         if (n == 0) continue;
         if (!(ok = mbar_wait(&bars[KV_KVFULL], jk & 1, a.status))) break;
         ++jk;
@@ -592,9 +630,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
     const float scale2 = a.scale * kLog2e;
     uint32_t s_it = 0, p_it = 0, done_it = 0, qd = 0;
     bool ok = true;
-    for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
-      const KvItem it = kv_item(a, item);
-      const int n = kv_item_tiles(a, it);
+    for (uint32_t w = 0; ok; ++w) {
+      WorkEntry e;
+      if (!(ok = ring_get(ring, &bars[KV_WFULL0], &bars[KV_WEMPTY0], w, e, a.status))) break;
+      if (e.item < 0) break;
+      const KvItem it = kv_item(a, e.item);
+      const int n = e.end - e.begin;
       const int64_t key = it.k0 + rl;
       for (int i = 0; i < n && ok; ++i) {
         // the stage's TMA writes (Q, dO, row stats) and its meta are visible once its phase
@@ -652,10 +693,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         tc_fence_after();
       }
       const int c0 = half * (D / 2);
-      store_cols<D / 2>(a.dv, a.dvs, it.z, it.hk, key, c0, lane_addr + kColAcc + c0, BF16,
-                        key < a.N, n == 0);
-      store_cols<D / 2>(a.dk, a.dks, it.z, it.hk, key, c0, lane_addr + kColAcc + D + c0, BF16,
-                        key < a.N, n == 0);
+      if (e.slot < 0) {
+        store_cols<D / 2>(a.dv, a.dvs, it.z, it.hk, key, c0, lane_addr + kColAcc + c0, BF16,
+                          key < a.N, n == 0);
+        store_cols<D / 2>(a.dk, a.dks, it.z, it.hk, key, c0, lane_addr + kColAcc + D + c0, BF16,
+                          key < a.N, n == 0);
+      } else {
+        // a chunk of a split item: fp32 partial row [dV | dK] into its slot
+        float* prow = a.partials + ((int64_t)e.slot * kRows + rl) * (2 * D);
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+#pragma unroll
+          for (int c = 0; c < D / 2; c += 32) {
+            float o[32];
+            if (n > 0) {
+              tmem_ld32(lane_addr + kColAcc + part * D + c0 + c, o);
+              tmem_wait_ld();
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(prow + part * D + c0 + c + i) =
+                  make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+          }
+        }
+      }
       tc_fence_before();
     }
   }
@@ -709,9 +773,15 @@ int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
     if (rc) return fail(SA_ELAUNCH, std::string("dQ tensor maps: ") + sa_last_error());
     a.tiles = (p.N + kRows - 1) / kRows;
     const int64_t items = a.Z * a.H * a.tiles;
+    const int ctas = (int)std::min<int64_t>(items, sms);
+    a.sched = SchedArgs{nullptr, nullptr, items};
+    if (p.plan_dq) {
+      const PlanPtrs pp = plan_carve(p.plan_dq, kPlanDq, items, ctas, D);
+      a.sched = SchedArgs{pp.header, pp.queue, items};
+    }
     auto kern = bwd_dq_sm100_kernel<D, BF16>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DqLayout<D>::kAlloc);
-    kern<<<(unsigned)std::min<int64_t>(items, sms), kBwdThreads, DqLayout<D>::kAlloc, stream>>>(a);
+    kern<<<(unsigned)ctas, kBwdThreads, DqLayout<D>::kAlloc, stream>>>(a);
     int e = check_launch("bwd_dq_sm100_kernel");
     if (e) return e;
   }
@@ -723,18 +793,77 @@ int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
     if (rc) return fail(SA_ELAUNCH, std::string("dK/dV tensor maps: ") + sa_last_error());
     a.tiles = (p.N + kRows - 1) / kRows;
     const int64_t items = a.Z * a.Hkv * a.tiles;
+    const int ctas = (int)std::min<int64_t>(items, sms);
+    a.sched = SchedArgs{nullptr, nullptr, items};
+    PlanPtrs pp{};
+    if (p.plan_dkdv) {
+      pp = plan_carve(p.plan_dkdv, kPlanDkdv, items, ctas, D);
+      a.sched = SchedArgs{pp.header, pp.queue, items};
+      a.partials = pp.partials;
+    }
     auto kern = bwd_dkdv_sm100_kernel<D, BF16>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DkvLayout<D>::kAlloc);
-    kern<<<(unsigned)std::min<int64_t>(items, sms), kBwdThreads, DkvLayout<D>::kAlloc, stream>>>(a);
+    kern<<<(unsigned)ctas, kBwdThreads, DkvLayout<D>::kAlloc, stream>>>(a);
     int e = check_launch("bwd_dkdv_sm100_kernel");
     if (e) return e;
+    if (p.plan_dkdv) {
+      e = launch_dkdv_reduce(p, pp, ctas, stream);
+      if (e) return e;
+    }
   }
   return SA_OK;
 }
 
 }  // namespace
 
+bool bwd_sm100_eligible(const AttnParams& p) {
+  if (p.dtype != SA_BF16 && p.dtype != SA_F16) return false;
+  if (p.D != 64 && p.D != 128) return false;
+  if (p.RB % kRows) return false;
+  const void* ptrs[7] = {p.q, p.k, p.v, p.dout, p.dq, p.dk, p.dv};
+  for (auto ptr : ptrs)
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;
+  for (int i = 0; i < 3; ++i)
+    if (p.qs[i] % 8 || p.ks[i] % 8 || p.vs[i] % 8 || p.dos[i] % 8 || p.dqs[i] % 8 ||
+        p.dks[i] % 8 || p.dvs[i] % 8)
+      return false;
+  return p.N <= INT32_MAX;
+}
+
+int64_t bwd_plan_bytes(int which, int64_t Z, int64_t H, int64_t Hkv, int64_t N, int64_t D) {
+  const int64_t tiles = (N + kRows - 1) / kRows;
+  const int sms = device_sm_count();
+  if (which == kPlanDq) {
+    const int64_t items = Z * H * tiles;
+    return plan_workspace_bytes(kPlanDq, items, (int)std::min<int64_t>(items, sms), D);
+  }
+  const int64_t items = Z * Hkv * tiles;
+  return plan_workspace_bytes(kPlanDkdv, items, (int)std::min<int64_t>(items, sms), D);
+}
+
+int plan_bwd_sm100(const AttnParams& p, cudaStream_t stream) {
+  if (!bwd_sm100_eligible(p)) return SA_OK;
+  const int64_t tiles = (p.N + kRows - 1) / kRows;
+  const int sms = device_sm_count();
+  if (p.plan_dq) {
+    const int64_t items = p.Z * p.H * tiles;
+    const int ctas = (int)std::min<int64_t>(items, sms);
+    const int rc = launch_plan(kPlanDq, p, items, ctas, plan_carve(p.plan_dq, kPlanDq, items, ctas, p.D),
+                               stream);
+    if (rc) return rc;
+  }
+  if (p.plan_dkdv) {
+    const int64_t items = p.Z * p.Hkv * tiles;
+    const int ctas = (int)std::min<int64_t>(items, sms);
+    const int rc = launch_plan(kPlanDkdv, p, items, ctas,
+                               plan_carve(p.plan_dkdv, kPlanDkdv, items, ctas, p.D), stream);
+    if (rc) return rc;
+  }
+  return SA_OK;
+}
+
 int launch_bwd_sm100(const AttnParams& p, cudaStream_t stream, int parts) {
+  if (!bwd_sm100_eligible(p)) return SA_EUNSUPPORTED;
   if (p.dtype != SA_BF16 && p.dtype != SA_F16) return SA_EUNSUPPORTED;
   if (p.D != 64 && p.D != 128) return SA_EUNSUPPORTED;
   if (p.RB % kRows) return SA_EUNSUPPORTED;

@@ -20,7 +20,7 @@
 #include <string>
 #include <type_traits>
 
-#include "attn_params.cuh"
+#include "sched.cuh"
 
 namespace sa {
 namespace {
@@ -46,6 +46,7 @@ struct FwdArgs {
   int causal;
   float scale;
   unsigned* status;
+  SchedArgs sched;
 };
 
 template <int D>
@@ -56,13 +57,16 @@ struct FwdLayout {
   static constexpr uint32_t kV0 = kK0 + 2 * kTileBytes;
   static constexpr uint32_t kP = kV0 + 2 * kTileBytes;
   static constexpr uint32_t kBars = kP + kT * kT * 2;
-  static constexpr uint32_t kBytes = kBars + 256;
+  static constexpr uint32_t kMeta = kBars + 256;  // TileMeta[2]
+  static constexpr uint32_t kRingOff = kMeta + 64;  // WorkEntry[kRing]
+  static constexpr uint32_t kBytes = kRingOff + 128;
   static constexpr uint32_t kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
 // barrier slots
 enum { B_QFULL = 0, B_QEMPTY, B_KFULL0, B_KFULL1, B_KEMPTY0, B_KEMPTY1, B_VFULL0, B_VFULL1,
-       B_VEMPTY0, B_VEMPTY1, B_SFULL0, B_SFULL1, B_SEMPTY0, B_SEMPTY1, B_PFULL, B_ODONE, B_NUM };
+       B_VEMPTY0, B_VEMPTY1, B_SFULL0, B_SFULL1, B_SEMPTY0, B_SEMPTY1, B_PFULL, B_ODONE,
+       B_WFULL0, B_WEMPTY0 = B_WFULL0 + kRing, B_NUM = B_WEMPTY0 + kRing };
 
 // Per K/V stage: what the producer learned from the lists, handed to the softmax warps
 // through shared memory (released by the stage's V mbarrier) so that no consumer reads
@@ -75,7 +79,6 @@ struct TileMeta {
 
 struct ItemInfo {
   int64_t z, h, hk, q_start, qb, row_id;
-  int count, n_sub;
 };
 
 __device__ __forceinline__ ItemInfo item_info(const FwdArgs& a, int64_t item) {
@@ -89,9 +92,13 @@ __device__ __forceinline__ ItemInfo item_info(const FwdArgs& a, int64_t item) {
   it.q_start = qt * kT;
   it.qb = it.q_start / a.RB;
   it.row_id = zh * a.NB + it.qb;
-  it.count = a.counts[it.row_id];
-  it.n_sub = it.count * (int)(a.RB / kT);
   return it;
+}
+
+// 128-key tiles of an item (its whole list): the static-schedule weight.
+__device__ __forceinline__ int item_tiles(const FwdArgs& a, int64_t item) {
+  const ItemInfo it = item_info(a, item);
+  return a.counts[it.row_id] * (int)(a.RB / kT);
 }
 
 __device__ __forceinline__ int64_t key_start_of(const FwdArgs& a, const ItemInfo& it, int t) {
@@ -116,11 +123,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
-  TileMeta* meta = reinterpret_cast<TileMeta*>(sm + L::kBars + 128);  // [2], one per K/V stage
+  TileMeta* meta = reinterpret_cast<TileMeta*>(sm + L::kMeta);  // [2], one per K/V stage
+  WorkEntry* ring = reinterpret_cast<WorkEntry*>(sm + L::kRingOff);
   __shared__ uint32_t s_tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t items = a.Z * a.H * a.QT;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars[B_QFULL], 1);
@@ -135,6 +142,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     }
     mbar_init(&bars[B_PFULL], 128);
     mbar_init(&bars[B_ODONE], 1);
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&bars[B_WFULL0 + i], 1);
+      mbar_init(&bars[B_WEMPTY0 + i], 1 + 128);  // the MMA thread and the softmax threads
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -154,9 +165,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       prefetch_tmap(&a.tm_v);
       uint32_t kv = 0, jq = 0;
       bool ok = true;
-      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const ItemInfo it = item_info(a, item);
-        if (it.n_sub == 0) continue;
+      const int n_entries = a.sched.header ? a.sched.header->n_entries : 0;
+      for (uint32_t w = 0; ok; ++w) {
+        const WorkEntry e = sched_fetch(a.sched, n_entries, w, [&](int64_t i) { return item_tiles(a, i); });
+        if (!(ok = ring_put(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const ItemInfo it = item_info(a, e.item);
+        if (e.end == e.begin) continue;
         ok = mbar_wait(&bars[B_QEMPTY], (jq & 1) ^ 1, a.status);
         if (!ok) break;
         mbar_arrive_expect_tx(&bars[B_QFULL], L::kTileBytes);
@@ -164,7 +179,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           tma_load_4d(sm + L::kQ + c * kT * 128, &a.tm_q, &bars[B_QFULL], c * 64,
                       (int)it.q_start, (int)it.h, (int)it.z);
         ++jq;
-        for (int t = 0; t < it.n_sub && ok; ++t, ++kv) {
+        for (int t = e.begin; t < e.end && ok; ++t, ++kv) {
           const int64_t ks = key_start_of(a, it, t);
           const uint32_t st = kv & 1, ph = (kv >> 1) & 1;
           ok = mbar_wait(&bars[B_KEMPTY0 + st], ph ^ 1, a.status);
@@ -214,14 +229,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         ++pv;
         return true;
       };
-      for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const ItemInfo it = item_info(a, item);
-        if (it.n_sub == 0) continue;
+      for (uint32_t w = 0; ok; ++w) {
+        WorkEntry e;
+        if (!(ok = ring_get(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const int n_sub = e.end - e.begin;
+        if (n_sub == 0) continue;
         ok = mbar_wait(&bars[B_QFULL], jq & 1, a.status);
         ++jq;
         if (!ok) break;
         const uint32_t kv0 = kv;
-        for (int t = 0; t < it.n_sub && ok; ++t, ++kv) {
+        for (int t = 0; t < n_sub && ok; ++t, ++kv) {
           const uint32_t st = kv & 1, ph = (kv >> 1) & 1;
           const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
           ok = mbar_wait(&bars[B_KFULL0 + st], ph, a.status) &&
@@ -237,11 +255,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           }
           tc_commit(&bars[B_SFULL0 + sb]);
           tc_commit(&bars[B_KEMPTY0 + st]);
-          if (t == it.n_sub - 1) tc_commit(&bars[B_QEMPTY]);
+          if (t == n_sub - 1) tc_commit(&bars[B_QEMPTY]);
           ++s_it;
           if (t > 0) ok = issue_pv(kv0 + t - 1, t - 1 == 0);
         }
-        if (ok) ok = issue_pv(kv0 + it.n_sub - 1, it.n_sub == 1);
+        if (ok) ok = issue_pv(kv0 + n_sub - 1, n_sub == 1);
       }
     }
   } else {
@@ -253,11 +271,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     unsigned char* p_tile = sm + L::kP;
     uint32_t s_it = 0, od = 0, kv = 0;
     bool ok = true;
-    for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
-      const ItemInfo it = item_info(a, item);
+    for (uint32_t w = 0; ok; ++w) {
+      WorkEntry e;
+      if (!(ok = ring_get(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
+      if (e.item < 0) break;
+      const ItemInfo it = item_info(a, e.item);
+      const int n_sub = e.end - e.begin;
       const int64_t row = it.q_start + rl;
       float m_used = -INFINITY, l_sum = 0.f;
-      for (int t = 0; t < it.n_sub && ok; ++t, ++kv) {
+      for (int t = 0; t < n_sub && ok; ++t, ++kv) {
         const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
         if (!mbar_wait(&bars[B_SFULL0 + sb], sph, a.status)) { ok = false; break; }
         tc_fence_after();
@@ -348,7 +370,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       if (!ok) break;
       // ---------------------------------------------------------------- epilogue
       float inv = 0.f;
-      if (it.n_sub > 0) {
+      if (n_sub > 0) {
         if (!mbar_wait(&bars[B_ODONE], od & 1, a.status)) { ok = false; break; }
         ++od;
         tc_fence_after();
@@ -359,7 +381,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float o[32];
-        if (it.n_sub > 0) {
+        if (n_sub > 0) {
           tmem_ld32(lane_addr + kColO + c * 32, o);
           tmem_wait_ld();
         } else {
@@ -381,7 +403,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       tc_fence_before();
       if (a.lse && row < a.N)
         a.lse[(it.z * a.H + it.h) * a.N + row] =
-            it.n_sub > 0 ? (m_used + log2f(l_sum)) * kLn2 : -INFINITY;
+            n_sub > 0 ? (m_used + log2f(l_sum)) * kLn2 : -INFINITY;
     }
   }
 
@@ -425,6 +447,13 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
   a.status = p.status;
   const int64_t items = a.Z * a.H * a.QT;
   const int grid = (int)std::min<int64_t>(items, device_sm_count());
+  a.sched = SchedArgs{nullptr, nullptr, items};
+  if (p.plan_fwd) {
+    const PlanPtrs pp = plan_carve(p.plan_fwd, kPlanFwd, items, grid, D);
+    rc = launch_plan(kPlanFwd, p, items, grid, pp, stream);
+    if (rc) return rc;
+    a.sched = SchedArgs{pp.header, pp.queue, items};
+  }
   auto kern = fwd_sm100_kernel<D, BF16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdLayout<D>::kAlloc);
   kern<<<grid, kFwdThreads, FwdLayout<D>::kAlloc, stream>>>(a);
@@ -432,6 +461,11 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
 }
 
 }  // namespace
+
+int64_t fwd_plan_bytes(int64_t Z, int64_t H, int64_t N, int64_t D) {
+  const int64_t items = Z * H * ((N + kT - 1) / kT);
+  return plan_workspace_bytes(kPlanFwd, items, (int)std::min<int64_t>(items, device_sm_count()), D);
+}
 
 int launch_fwd_sm100(const AttnParams& p, cudaStream_t stream) {
   if (p.dtype != SA_BF16 && p.dtype != SA_F16) return SA_EUNSUPPORTED;

@@ -41,6 +41,10 @@ struct AttnParams {
   int64_t dvs[4];
   float* dbias;  // (Z, H, NB, list_stride) contiguous fp32, or null
   unsigned* status;
+  // planner workspaces of the tcgen05 kernels (null: static round-robin scheduling)
+  void* plan_fwd;
+  void* plan_dq;
+  void* plan_dkdv;
 };
 
 // backward parts (bitmask)
@@ -56,5 +60,10 @@ int launch_transpose_lists(const int32_t* lists, int64_t list_stride, const int3
 // tcgen05 kernels: return SA_EUNSUPPORTED (without launching) for shapes they do not take.
 int launch_fwd_sm100(const AttnParams& p, cudaStream_t stream);
 int launch_bwd_sm100(const AttnParams& p, cudaStream_t stream, int parts);
+// Planner workspaces (bytes) of the tcgen05 kernels for these sizes on the current device,
+// and the plan launches of the backward (run after the transposed lists exist).
+int64_t fwd_plan_bytes(int64_t Z, int64_t H, int64_t N, int64_t D);
+int64_t bwd_plan_bytes(int which, int64_t Z, int64_t H, int64_t Hkv, int64_t N, int64_t D);
+int plan_bwd_sm100(const AttnParams& p, cudaStream_t stream);
 
 }  // namespace sa

@@ -38,8 +38,10 @@ _SIGNATURES = {
                                                _vp, _vp]),
     "sa_block_list_attention_fwd": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _i64,
                                            _vp, _p64, _vp, _p64, _vp, _p64, _vp, _p64, _vp,
-                                           _vp, _i64, _vp, _vp, _i32, _p64, _i32, _f32, _vp]),
-    "sa_block_list_attention_bwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
+                                           _vp, _i64, _vp, _vp, _i32, _p64, _i32, _f32,
+                                           _vp, _i64, _vp]),
+    "sa_block_list_attention_fwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64]),
+    "sa_block_list_attention_bwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64, _i64]),
     "sa_block_list_attention_bwd": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _i64,
                                            _vp, _p64, _vp, _p64, _vp, _p64, _vp, _p64, _vp, _p64,
                                            _vp, _vp, _i64, _vp, _vp, _i32, _p64, _i32, _f32,

@@ -199,6 +199,8 @@ def _fwd(q, k, v, lists, counts, route_block, is_causal, scale, store_lse, soft_
     out = torch.empty_like(q)
     lse = torch.empty((Z, H, N), dtype=torch.float32, device=q.device) if store_lse else None
     sb = soft_block_bias
+    ws_bytes = int(nat.lib().sa_block_list_attention_fwd_workspace_bytes(Z, H, N, D, route_block))
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)
     nat.check(nat.lib().sa_block_list_attention_fwd(
         nat.float_code(q.dtype), Z, H, k.shape[1], N, D, route_block,
         q.data_ptr(), nat.strides(q), k.data_ptr(), nat.strides(k), v.data_ptr(), nat.strides(v),
@@ -206,7 +208,8 @@ def _fwd(q, k, v, lists, counts, route_block, is_causal, scale, store_lse, soft_
         lists.data_ptr(), lists.shape[-1], counts.data_ptr(),
         nat.ptr(sb), nat.float_code(sb.dtype) if sb is not None else 0,
         nat.strides(sb) if sb is not None else None,
-        int(bool(is_causal)), float(scale), nat.stream_of(q)), "block_list_attention forward")
+        int(bool(is_causal)), float(scale), ws.data_ptr(), ws.numel(), nat.stream_of(q)),
+        "block_list_attention forward")
     return out, lse
 
 
@@ -220,7 +223,8 @@ def _bwd(do, q, k, v, out, lse, lists, counts, route_block, is_causal, scale, so
     nb = -(-N // route_block)
     d_sb = (torch.empty((Z, H, nb, lists.shape[-1]), dtype=torch.float32, device=q.device)
             if sb is not None else None)
-    ws_bytes = int(nat.lib().sa_block_list_attention_bwd_workspace_bytes(Z, H, N, route_block))
+    ws_bytes = int(nat.lib().sa_block_list_attention_bwd_workspace_bytes(Z, H, k.shape[1], N, D,
+                                                                          route_block))
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)
     nat.check(nat.lib().sa_block_list_attention_bwd(
         nat.float_code(q.dtype), Z, H, k.shape[1], N, D, route_block,

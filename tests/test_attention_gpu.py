@@ -259,3 +259,25 @@ def test_backward_half_vs_oracle(Z, H, Hkv, N, D, RB, depth, causal, sink, local
         ref_db = res["d_bias"]
         err = (raw.grad.cpu().double() - ref_db).abs().max().item()
         assert err <= 2e-2 * max(1.0, ref_db.abs().max().item()), f"d_bias err {err}"
+
+
+def test_backward_split_heavy_sink_column():
+    """Causal + sink lists at N=2048 with 4 query heads per KV head: the sink key block is
+    listed by every query block of the group, so the dK/dV planner splits that item into
+    chunks whose fp32 partials are reduced separately; gradients must still match."""
+    Z, H, Hkv, N, D, RB = 1, 4, 1, 2048, 128, 128
+    gen = torch.Generator().manual_seed(31)
+    q = randn((Z, H, N, D), gen).bfloat16()
+    k = randn((Z, Hkv, N, D), gen).bfloat16()
+    v = randn((Z, Hkv, N, D), gen).bfloat16()
+    do = randn((Z, H, N, D), gen).bfloat16()
+    router = tree_router(Z, H, N // RB, 4).to(DEV)
+    bl = build_block_lists(router, [1, 1, 2, 1], is_causal=True, sink_block=True, arity=2)
+    qq, kk, vv = (t.to(DEV).requires_grad_(True) for t in (q, k, v))
+    out = block_list_attention(qq, kk, vv, bl, route_block=RB, is_causal=True)
+    out.backward(do.to(DEV))
+    mask = ao.token_mask(block_mask_from_lists(bl.lists, bl.counts), RB, N, True)
+    res = ao.masked_attention_grads(q.float(), k.float(), v.float(), mask, do.float())
+    assert_half_close(out, res["out"], "out")
+    for name, t in (("dq", qq), ("dk", kk), ("dv", vv)):
+        assert_half_close(t.grad, res[name], name)

@@ -35,8 +35,9 @@ def test_header_symbols_exported():
 
 def test_abi_version_and_workspace_sizes():
     lib = nat.lib()
-    assert lib.sa_abi_version() == 1
-    ws = lib.sa_block_list_attention_bwd_workspace_bytes(1, 32, 8192, 128)
+    assert lib.sa_abi_version() == 2
+    ws = lib.sa_block_list_attention_bwd_workspace_bytes(1, 32, 8, 8192, 128, 128)
+    assert lib.sa_block_list_attention_fwd_workspace_bytes(1, 32, 8192, 128, 128) > 0
     NB = 64
     assert ws >= 32 * 8192 * 4 + 2 * 32 * NB * NB * 4
     assert lib.sa_ultrametric_decode_workspace_bytes(64, 32, 8, 128, 512) > 0
@@ -52,11 +53,11 @@ def test_library_rejects_bad_arguments_without_launch():
     assert b"null" in lib.sa_last_error()
     rc = lib.sa_block_list_attention_fwd(nat.SA_BF16, 1, 3, 2, 128, 64, 128, None, st, None, st,
                                          None, st, None, st, None, None, 0, None, None, 0, None, 0,
-                                         1.0, None)
+                                         1.0, None, 0, None)
     assert rc == nat.SA_EINVAL and b"multiple" in lib.sa_last_error()
     rc = lib.sa_block_list_attention_fwd(nat.SA_BF16, 1, 2, 2, 128, 48, 128, None, st, None, st,
                                          None, st, None, st, None, None, 0, None, None, 0, None, 0,
-                                         1.0, None)
+                                         1.0, None, 0, None)
     assert rc == nat.SA_EINVAL and b"power of two" in lib.sa_last_error()
 
 
