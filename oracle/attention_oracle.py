@@ -142,3 +142,32 @@ def _token_bias_differentiable(bf, lists, counts, route_block, seq_len):
     full = torch.gather(padded, -1, idx)
     tb = full.repeat_interleave(route_block, dim=-2).repeat_interleave(route_block, dim=-1)
     return tb[..., :seq_len, :seq_len]
+
+
+def block_list_backward_lowp(q, k, v, out, dout, lse, mask, sm_scale=None, io_dtype=torch.bfloat16):
+    """Backward of the masked attention with the reference kernels' rounding points
+    (src/ultrametric/block_list.py:565-580 dQ and :652-680 dK/dV): P and the scaled dS are
+    rounded to the input dtype before their products, Delta uses the input-dtype output O
+    (block_list.py:785); everything else in fp64.  GQA: dK/dV summed over each KV group."""
+    H, D = q.shape[1], q.shape[-1]
+    scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(D)
+    f = torch.float64
+    qf, kf, vf = q.to(f), _expand_kv(k, H).to(f), _expand_kv(v, H).to(f)
+    dof = dout.to(f)
+    s = torch.matmul(qf, kf.transpose(-2, -1)) * scale
+    lse_safe = torch.where(torch.isinf(lse), torch.zeros_like(lse), lse).to(f)
+    p = torch.where(mask, torch.exp(s - lse_safe[..., None]), torch.zeros_like(s))
+    p_lp = p.to(io_dtype).to(f)
+    dp = torch.matmul(dof, vf.transpose(-2, -1))
+    delta = (dof * out.to(io_dtype).to(f)).sum(-1, keepdim=True)
+    ds = torch.where(mask, p * (dp - delta), torch.zeros_like(p))
+    ds_lp = (ds * scale).to(io_dtype).to(f)
+    dq = torch.matmul(ds_lp, kf)
+    dk = torch.matmul(ds_lp.transpose(-2, -1), qf)
+    dv = torch.matmul(p_lp.transpose(-2, -1), dof)
+    g = H // k.shape[1]
+    if g > 1:
+        Z, _, N, _ = dk.shape
+        dk = dk.view(Z, k.shape[1], g, N, D).sum(2)
+        dv = dv.view(Z, k.shape[1], g, N, D).sum(2)
+    return {"dq": dq, "dk": dk, "dv": dv}

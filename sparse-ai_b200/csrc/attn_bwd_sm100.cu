@@ -227,10 +227,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
       prefetch_tmap(&a.tm_v);
       uint32_t kv = 0, jq = 0;
       bool ok = true;
-      const int n_entries = a.sched.header ? a.sched.header->n_entries : 0;
+      auto weight = [&](int64_t i) { return dq_item_tiles(a, i); };
+      WorkFetcher fetch;
+      fetch.init(&a.sched, weight);
       for (uint32_t w = 0; ok; ++w) {
-        const WorkEntry e =
-            sched_fetch(a.sched, n_entries, w, [&](int64_t i) { return dq_item_tiles(a, i); });
+        const WorkEntry e = fetch.next(weight);
         if (!(ok = ring_put(ring, &bars[DQ_WFULL0], &bars[DQ_WEMPTY0], w, e, a.status))) break;
         if (e.item < 0) break;
         const DqItem it = dq_item(a, e.item);
@@ -520,10 +521,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
       prefetch_tmap(&a.tm_v);
       uint32_t qd = 0, jk = 0;
       bool ok = true;
-      const int n_entries = a.sched.header ? a.sched.header->n_entries : 0;
+      auto weight = [&](int64_t i) { return kv_item_tiles(a, kv_item(a, i)); };
+      WorkFetcher fetch;
+      fetch.init(&a.sched, weight);
       for (uint32_t w = 0; ok; ++w) {
-        const WorkEntry e = sched_fetch(a.sched, n_entries, w,
-                                        [&](int64_t i) { return kv_item_tiles(a, kv_item(a, i)); });
+        const WorkEntry e = fetch.next(weight);
         if (!(ok = ring_put(ring, &bars[KV_WFULL0], &bars[KV_WEMPTY0], w, e, a.status))) break;
         if (e.item < 0) break;
         const KvItem it = kv_item(a, e.item);

@@ -165,9 +165,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       prefetch_tmap(&a.tm_v);
       uint32_t kv = 0, jq = 0;
       bool ok = true;
-      const int n_entries = a.sched.header ? a.sched.header->n_entries : 0;
+      auto weight = [&](int64_t i) { return item_tiles(a, i); };
+      WorkFetcher fetch;
+      fetch.init(&a.sched, weight);
       for (uint32_t w = 0; ok; ++w) {
-        const WorkEntry e = sched_fetch(a.sched, n_entries, w, [&](int64_t i) { return item_tiles(a, i); });
+        const WorkEntry e = fetch.next(weight);
         if (!(ok = ring_put(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
         if (e.item < 0) break;
         const ItemInfo it = item_info(a, e.item);

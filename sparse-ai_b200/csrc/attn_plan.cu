@@ -49,6 +49,27 @@ __device__ __forceinline__ int weight_bin(int w) {
   return kBins - 1 - key;
 }
 
+// atomicAdd(&ctr[bin], n) aggregated over the lanes of a warp that share `bin`; returns this
+// lane's base (lanes of a group get consecutive ranges in lane order).  Avoids serialising
+// hundreds of shared-memory atomics on one address when most items share a bin.
+__device__ __forceinline__ int warp_bin_add(int* ctr, int bin, int n) {
+  const unsigned peers = __match_any_sync(__activemask(), bin);
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(peers) - 1;
+  int incl = n;  // inclusive prefix of n over the lower lanes of the group
+  int total = 0;
+  for (unsigned m = peers; m; m &= m - 1) {
+    const int l = __ffs(m) - 1;
+    const int v = __shfl_sync(peers, n, l);
+    total += v;
+    if (l < lane) incl += v;
+  }
+  int base = 0;
+  if (lane == leader) base = atomicAdd(&ctr[bin], total);
+  base = __shfl_sync(peers, base, leader);
+  return base + incl - n;
+}
+
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
   __shared__ int s_hist[kBins];
   __shared__ int s_cursor[kBins];
@@ -69,19 +90,24 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     a.weights[i] = w;
     tot += (unsigned long long)w;
   }
-  atomicAdd(&s_total, tot);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  if ((tid & 31) == 0) atomicAdd(&s_total, tot);
   __syncthreads();
   int T = 0x7fffffff;
   if (a.kind == kPlanDkdv) {
     const unsigned long long t = (s_total + a.ctas - 1) / (unsigned long long)a.ctas;
     T = (int)max((unsigned long long)kMinSplit, t);
   }
-  // histogram of entries by chunk weight
-  for (int64_t i = tid; i < a.items; i += blockDim.x) {
-    const int w = a.weights[i];
-    const int chunks = w > T ? (w + T - 1) / T : 1;
-    const int wc = (w + chunks - 1) / chunks;
-    atomicAdd(&s_hist[weight_bin(wc)], chunks);
+  // histogram of entries by chunk weight (warp-uniform trip count for the warp atomics)
+  for (int64_t i0 = 0; i0 < a.items; i0 += blockDim.x) {
+    const int64_t i = i0 + tid;
+    if (i < a.items) {
+      const int w = a.weights[i];
+      const int chunks = w > T ? (w + T - 1) / T : 1;
+      const int wc = (w + chunks - 1) / chunks;
+      warp_bin_add(s_hist, weight_bin(wc), chunks);
+    }
   }
   __syncthreads();
   if (tid == 0) {
@@ -93,21 +119,23 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     s_entries = run;
   }
   __syncthreads();
-  for (int64_t i = tid; i < a.items; i += blockDim.x) {
+  for (int64_t i0 = 0; i0 < a.items; i0 += blockDim.x) {
+    const int64_t i = i0 + tid;
+    if (i >= a.items) continue;
     const int w = a.weights[i];
     const int chunks = w > T ? (w + T - 1) / T : 1;
     const int wc = (w + chunks - 1) / chunks;
     const int bin = weight_bin(wc);
     int slot_base = -1;
-    if (chunks > 1) {
+    if (chunks > 1) {  // rare: at most one split item per CTA of the kernel
       slot_base = atomicAdd(&s_slots, chunks);
       const int k = atomicAdd(&s_nsplit, 1);
       a.plan.splits[k] = SplitItem{(int)i, slot_base, chunks, 0};
     }
+    const int pos0 = warp_bin_add(s_cursor, bin, chunks);
     for (int c = 0; c < chunks; ++c) {
-      const int pos = atomicAdd(&s_cursor[bin], 1);
       const int b0 = (int)((int64_t)w * c / chunks), b1 = (int)((int64_t)w * (c + 1) / chunks);
-      a.plan.queue[pos] = WorkEntry{(int)i, b0, b1, slot_base < 0 ? -1 : slot_base + c};
+      a.plan.queue[pos0 + c] = WorkEntry{(int)i, b0, b1, slot_base < 0 ? -1 : slot_base + c};
     }
   }
   __syncthreads();

@@ -274,10 +274,15 @@ def test_backward_split_heavy_sink_column():
     router = tree_router(Z, H, N // RB, 4).to(DEV)
     bl = build_block_lists(router, [1, 1, 2, 1], is_causal=True, sink_block=True, arity=2)
     qq, kk, vv = (t.to(DEV).requires_grad_(True) for t in (q, k, v))
-    out = block_list_attention(qq, kk, vv, bl, route_block=RB, is_causal=True)
+    out, lse = block_list_attention(qq, kk, vv, bl, route_block=RB, is_causal=True, return_lse=True)
     out.backward(do.to(DEV))
     mask = ao.token_mask(block_mask_from_lists(bl.lists, bl.counts), RB, N, True)
     res = ao.masked_attention_grads(q.float(), k.float(), v.float(), mask, do.float())
     assert_half_close(out, res["out"], "out")
+    # The sink keys' dK/dV sum 8192 terms whose P / dS the reference kernels round to bf16
+    # before the products (block_list.py:571-580, 666-680): compare with an oracle that
+    # rounds at the same points, and with exact math at 2x the tolerance.
+    lowp = ao.block_list_backward_lowp(q, k, v, out.detach().cpu(), do, lse.detach().cpu(), mask)
     for name, t in (("dq", qq), ("dk", kk), ("dv", vv)):
-        assert_half_close(t.grad, res[name], name)
+        assert_half_close(t.grad, lowp[name], name + " vs reference rounding")
+        assert_half_close(t.grad, res[name], name + " vs exact", abs_tol=4e-2, rel_tol=2e-2)
