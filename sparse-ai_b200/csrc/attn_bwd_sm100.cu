@@ -235,7 +235,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         if (!(ok = ring_put(ring, &bars[DQ_WFULL0], &bars[DQ_WEMPTY0], w, e, a.status))) break;
         if (e.item < 0) break;
         const DqItem it = dq_item(a, e.item);
-        if (e.end == e.begin) continue;
+        if (e.end == e.begin) {
+          fetch.reserve(weight);
+          continue;
+        }
         if (!(ok = mbar_wait(&bars[DQ_QEMPTY], (jq & 1) ^ 1, a.status))) break;
         ++jq;
         mbar_arrive_expect_tx(&bars[DQ_QFULL], 2 * kRows * D * 2);
@@ -260,6 +263,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
             tma_load_4d(stage + kSub * D * 2 + c * kSub * 128, &a.tm_v, &bars[DQ_KVFULL0 + st],
                         c * 64, (int)k0, (int)it.hk, (int)it.z);
           }
+          if (j == e.end - 1) fetch.reserve(weight);
         }
       }
     }
@@ -529,7 +533,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         if (!(ok = ring_put(ring, &bars[KV_WFULL0], &bars[KV_WEMPTY0], w, e, a.status))) break;
         if (e.item < 0) break;
         const KvItem it = kv_item(a, e.item);
-        if (e.end == e.begin) continue;
+        if (e.end == e.begin) {
+          fetch.reserve(weight);
+          continue;
+        }
         if (!(ok = mbar_wait(&bars[KV_KVEMPTY], (jk & 1) ^ 1, a.status))) break;
         ++jk;
         mbar_arrive_expect_tx(&bars[KV_KVFULL], 2 * kRows * D * 2);
@@ -539,6 +546,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
           tma_load_4d(sm + L::kV + c * kRows * 128, &a.tm_v, &bars[KV_KVFULL], c * 64, (int)it.k0,
                       (int)it.hk, (int)it.z);
         }
+        uint32_t done = 0;
         ok = for_each_qtile(a, it, e.begin, e.end,
                             [&](int64_t h, int64_t qb, int64_t slot, int64_t q0) -> bool {
           const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
@@ -557,6 +565,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
           bulk_load(stage + L::kStats, a.stats + (zh * ((a.N + kSub - 1) / kSub) + q0 / kSub) * 2 * kSub,
                     2 * kSub * 4, &bars[KV_QFULL0 + st]);
           ++qd;
+          if ((int)++done == e.end - e.begin) fetch.reserve(weight);
           return true;
         });
       }

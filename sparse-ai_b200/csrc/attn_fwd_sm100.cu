@@ -173,7 +173,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         if (!(ok = ring_put(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
         if (e.item < 0) break;
         const ItemInfo it = item_info(a, e.item);
-        if (e.end == e.begin) continue;
+        if (e.end == e.begin) {
+          fetch.reserve(weight);
+          continue;
+        }
         ok = mbar_wait(&bars[B_QEMPTY], (jq & 1) ^ 1, a.status);
         if (!ok) break;
         mbar_arrive_expect_tx(&bars[B_QFULL], L::kTileBytes);
@@ -202,6 +205,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           for (int c = 0; c < D / 64; ++c)
             tma_load_4d(sm + L::kV0 + st * L::kTileBytes + c * kT * 128, &a.tm_v,
                         &bars[B_VFULL0 + st], c * 64, (int)ks, (int)it.hk, (int)it.z);
+          if (t == e.end - 1) fetch.reserve(weight);
         }
       }
     }

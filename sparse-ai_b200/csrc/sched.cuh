@@ -21,56 +21,45 @@ struct SchedArgs {
 
 __device__ __forceinline__ WorkEntry no_work() { return WorkEntry{-1, 0, 0, -1}; }
 
-// Producer side: yields this CTA's entries in order.  Dynamic mode keeps the queue walk two
-// entries ahead -- the atomic for entry w+2 and the queue load for entry w+1 are in flight
-// while entry w is being produced -- so the fetch latency stays off the critical path.
-// `weight(i)` gives an item's sub-tile count in the static round-robin mode.
+// Producer side: yields this CTA's entries in order.  An entry is reserved (dynamic mode:
+// atomic on the queue counter, then the queue load) only when the producer issues the last
+// tile of the current entry -- late enough that a CTA never sits on queued work while other
+// CTAs go idle, early enough (the producer runs a few stages ahead of the MMA) to hide the
+// fetch latency.  `weight(i)` gives an item's sub-tile count in the static round-robin mode.
 struct WorkFetcher {
   const SchedArgs* s;
-  int n_entries;
-  int idx_next;      // queue index of the entry after `e_next`
-  WorkEntry e_next;  // the entry next() returns
+  WorkEntry e_next;
   uint32_t w;
-
-  __device__ __forceinline__ WorkEntry load(int idx) const {
-    return idx < n_entries ? s->queue[idx] : no_work();
-  }
+  bool reserved;
 
   template <typename WeightFn>
-  __device__ __forceinline__ WorkEntry statik(uint32_t k, WeightFn&& weight) const {
-    const int64_t idx = (int64_t)blockIdx.x + (int64_t)k * gridDim.x;
-    return idx < s->items ? WorkEntry{(int)idx, 0, weight(idx), -1} : no_work();
+  __device__ __forceinline__ void reserve(WeightFn&& weight) {
+    if (reserved) return;
+    reserved = true;
+    if (s->header) {
+      const int idx = atomicAdd(&s->header->counter, 1);
+      e_next = idx < s->header->n_entries ? s->queue[idx] : no_work();
+    } else {
+      const int64_t idx = (int64_t)blockIdx.x + (int64_t)w * gridDim.x;
+      e_next = idx < s->items ? WorkEntry{(int)idx, 0, weight(idx), -1} : no_work();
+    }
   }
 
   template <typename WeightFn>
   __device__ __forceinline__ void init(const SchedArgs* args, WeightFn&& weight) {
     s = args;
     w = 0;
-    if (s->header) {
-      n_entries = s->header->n_entries;
-      const int i0 = atomicAdd(&s->header->counter, 1);
-      idx_next = atomicAdd(&s->header->counter, 1);
-      e_next = load(i0);
-    } else {
-      n_entries = 0;
-      idx_next = 0;
-      e_next = statik(0, weight);
-    }
+    reserved = false;
+    reserve(weight);
   }
 
+  // The reserved entry; the caller reserves the following one with reserve().
   template <typename WeightFn>
   __device__ __forceinline__ WorkEntry next(WeightFn&& weight) {
-    const WorkEntry e = e_next;
+    reserve(weight);
+    reserved = false;
     ++w;
-    if (e.item >= 0) {
-      if (s->header) {
-        e_next = load(idx_next);  // consumed at the next call
-        idx_next = atomicAdd(&s->header->counter, 1);
-      } else {
-        e_next = statik(w, weight);
-      }
-    }
-    return e;
+    return e_next;
   }
 };
 
