@@ -557,7 +557,7 @@ def run_ours(args):
     peaks, peak_kind = load_peaks()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
-    t_heads = c2_thresholds(0)
+    t_heads = c2_thresholds(0) if args.threshold is None else [args.threshold] * C2["H"]
     prob = C2Problem(dev, seed=rank, t_heads=t_heads)
     with ClockSampler(local) as clk:
         total_ms, parts = time_c2(prob, args.steps, args.warmup, flush, barrier)
@@ -637,6 +637,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--quick", action="store_true", help="headline only (no sweep / decode)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--threshold", type=int, default=None,
+                    help="profiling aid: every head uses this LCA threshold instead of the seeded mix")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
