@@ -34,7 +34,8 @@ namespace {
 
 constexpr int kRows = 128;  // resident tile rows (TMEM lanes)
 constexpr int kSub = 64;    // streamed sub-tile rows
-constexpr int kStages = 3;  // streamed ring depth
+constexpr int kStages = 3;    // streamed ring depth (dQ kernel)
+constexpr int kKvStages = 2;  // streamed ring depth (dK/dV kernel: P^T/dS^T are double-buffered)
 constexpr int kEw = 8;                      // elementwise warps: 2 per TMEM lane quarter
 constexpr int kEwThreads = kEw * 32;
 constexpr int kBwdThreads = 64 + kEwThreads;
@@ -205,8 +206,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
   if (threadIdx.x == 0) {
     uint32_t cnt[DQ_NUM];
     for (int i = 0; i < DQ_NUM; ++i) cnt[i] = 1;
-    cnt[DQ_SEMPTY0] = cnt[DQ_SEMPTY0 + 1] = kEwThreads;
-    cnt[DQ_DSFULL0] = cnt[DQ_DSFULL0 + 1] = kEwThreads;
+    cnt[DQ_SEMPTY0] = cnt[DQ_SEMPTY0 + 1] = kEwThreads / 2;  // one group per buffer
+    cnt[DQ_DSFULL0] = cnt[DQ_DSFULL0 + 1] = kEwThreads / 2;
     for (int i = 0; i < kRing; ++i) cnt[DQ_WEMPTY0 + i] = 1 + kEwThreads;
     init_bars(bars, cnt, DQ_NUM);
   }
@@ -329,11 +330,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
     }
   } else {
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;  // which 32 of the 64 sub-tile columns
+    // Two groups of 4 warps ping-pong over the sub-tiles: group g takes the sub-tiles with
+    // s_it % 2 == g, i.e. TMEM S/dP buffer g and dS buffer g, so two sub-tiles are in
+    // flight and one group's latency overlaps the other's work.  Each thread owns a full
+    // 64-column row of its group's sub-tiles.
+    const int grp = (warp - 2) >> 2;
     const int rl = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const float scale2 = a.scale * kLog2e;
-    uint32_t s_it = 0, ds_it = 0, done_it = 0, kv = 0;
+    uint32_t s_it = 0, done_it = 0, kv = 0;
     bool ok = true;
     for (uint32_t w = 0; ok; ++w) {
       WorkEntry e;
@@ -349,51 +354,50 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         lse2 = lv == -INFINITY ? 0.f : lv * kLog2e;  // block_list.py:553 (lse_safe)
         dl = a.delta[zh * a.N + row];
       }
-      float db_acc = 0.f;
-      for (int j = e.begin; j < e.end && ok; ++j, ++kv) {
+      for (int j = e.begin; j < e.end && ok; ++j, ++kv, ++s_it) {
+        const uint32_t sb = s_it & 1;
+        if ((int)sb != grp) continue;  // the other group's sub-tile
         const int slot = j / spb;
         // this stage's K/V stay resident until the dQ MMA of sub-tile j, which waits for us
         const uint32_t st = kv % kStages;
         if (!(ok = mbar_wait(&bars[DQ_KVFULL0 + st], (kv / kStages) & 1, a.status))) break;
-        const int64_t k0 = meta[st].start + half * 32;
+        const int64_t k0 = meta[st].start;
         const float b2 = meta[st].b2;
-        const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
+        const uint32_t sph = (s_it >> 1) & 1;
         if (!(ok = mbar_wait(&bars[DQ_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
-        float s[32], dp[32];
-        tmem_ld32(lane_addr + kColS + sb * kSub + half * 32, s);
-        tmem_ld32(lane_addr + kColP + sb * kSub + half * 32, dp);
+        float s[kSub], dp[kSub];
+        tmem_ld32(lane_addr + kColS + sb * kSub, *reinterpret_cast<float(*)[32]>(s));
+        tmem_ld32(lane_addr + kColS + sb * kSub + 32, *reinterpret_cast<float(*)[32]>(s + 32));
+        tmem_ld32(lane_addr + kColP + sb * kSub, *reinterpret_cast<float(*)[32]>(dp));
+        tmem_ld32(lane_addr + kColP + sb * kSub + 32, *reinterpret_cast<float(*)[32]>(dp + 32));
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars[DQ_SEMPTY0 + sb]);
-        ++s_it;
         int64_t lim = a.N - 1 - k0;  // keys k0 + c with c <= lim are visible to this row
         if (a.causal) lim = min(lim, row - k0);
         if (row >= a.N) lim = -1;
-        uint32_t pk[16];
+        uint32_t pk[kSub / 2];
         float rs = 0.f;
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
+        for (int c = 0; c < kSub; c += 2) {
           float d0 = 0.f, d1 = 0.f;
           if (c <= lim) d0 = fast_exp2(fmaf(s[c], scale2, b2) - lse2) * (dp[c] - dl);
           if (c + 1 <= lim) d1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - lse2) * (dp[c + 1] - dl);
           rs += d0 + d1;
           pk[c / 2] = pack2(d0 * a.scale, d1 * a.scale, BF16);
         }
-        db_acc += rs;
-        const uint32_t db = ds_it & 1, dph = (ds_it >> 1) & 1;
-        if (!(ok = mbar_wait(&bars[DQ_DSEMPTY0 + db], dph ^ 1, a.status))) break;
-        st_half_row_sw128(sm + L::kDS + db * kRows * kSub * 2, rl, half * 4, pk);
+        // dS buffer sb is free once the dQ MMA of sub-tile s_it - 2 completed
+        if (!(ok = mbar_wait(&bars[DQ_DSEMPTY0 + sb], sph ^ 1, a.status))) break;
+        st_half_row_sw128(sm + L::kDS + sb * kRows * kSub * 2, rl, 0, pk);
+        st_half_row_sw128(sm + L::kDS + sb * kRows * kSub * 2, rl, 4, pk + 16);
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(&bars[DQ_DSFULL0 + db]);
-        ++ds_it;
-        if (a.dbias && (j % spb == spb - 1)) {
-          float v = db_acc;
+        mbar_arrive(&bars[DQ_DSFULL0 + sb]);
+        if (a.dbias) {
 #pragma unroll
-          for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          if (lane == 0) atomicAdd(&a.dbias[it.row_id * a.list_stride + slot], v);
-          db_acc = 0.f;
+          for (int o = 16; o; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+          if (lane == 0) atomicAdd(&a.dbias[it.row_id * a.list_stride + slot], rs);
         }
       }
       if (!ok) break;
@@ -402,8 +406,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         ++done_it;
         tc_fence_after();
       }
-      store_cols<D / 2>(a.dq, a.dqs, it.z, it.h, row, half * (D / 2),
-                        lane_addr + kColAcc + half * (D / 2), BF16, row < a.N, n_sub == 0);
+      store_cols<D / 2>(a.dq, a.dqs, it.z, it.h, row, grp * (D / 2),
+                        lane_addr + kColAcc + grp * (D / 2), BF16, row < a.N, n_sub == 0);
       tc_fence_before();
     }
   }
@@ -425,18 +429,18 @@ struct DkvLayout {
   static constexpr uint32_t kQD = 2 * kRows * D * 2;        // stages x (Q, dO, stats)
   static constexpr uint32_t kStats = 2 * kSub * D * 2;      // stage offset: lse2[64], delta[64]
   static constexpr uint32_t kStage = kStats + 1024;         // keeps the tiles 1024-aligned
-  static constexpr uint32_t kPT = kQD + kStages * kStage;   // P^T [128][64]
-  static constexpr uint32_t kDST = kPT + kRows * kSub * 2;  // dS^T [128][64]
-  static constexpr uint32_t kBars = kDST + kRows * kSub * 2;
+  static constexpr uint32_t kPT = kQD + kKvStages * kStage;  // 2 x P^T [128][64]
+  static constexpr uint32_t kDST = kPT + 2 * kRows * kSub * 2;  // 2 x dS^T [128][64]
+  static constexpr uint32_t kBars = kDST + 2 * kRows * kSub * 2;
   static constexpr uint32_t kMeta = kBars + 256;  // StageMeta[kStages]
   static constexpr uint32_t kRingOff = kMeta + 128;  // WorkEntry[kRing]
   static constexpr uint32_t kAlloc = kRingOff + 128 + 1024;
 };
 
-enum { KV_KVFULL = 0, KV_KVEMPTY, KV_QFULL0, KV_QEMPTY0 = KV_QFULL0 + kStages,
-       KV_SFULL0 = KV_QEMPTY0 + kStages, KV_SEMPTY0 = KV_SFULL0 + 2, KV_PFULL = KV_SEMPTY0 + 2,
-       KV_PEMPTY, KV_DONE, KV_WFULL0, KV_WEMPTY0 = KV_WFULL0 + kRing,
-       KV_NUM = KV_WEMPTY0 + kRing };
+enum { KV_KVFULL = 0, KV_KVEMPTY, KV_QFULL0, KV_QEMPTY0 = KV_QFULL0 + kKvStages,
+       KV_SFULL0 = KV_QEMPTY0 + kKvStages, KV_SEMPTY0 = KV_SFULL0 + 2, KV_PFULL0 = KV_SEMPTY0 + 2,
+       KV_PEMPTY0 = KV_PFULL0 + 2, KV_DONE = KV_PEMPTY0 + 2, KV_WFULL0,
+       KV_WEMPTY0 = KV_WFULL0 + kRing, KV_NUM = KV_WEMPTY0 + kRing };
 
 struct KvItem {
   int64_t z, hk, k0, kb;
@@ -503,8 +507,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
   if (threadIdx.x == 0) {
     uint32_t cnt[KV_NUM];
     for (int i = 0; i < KV_NUM; ++i) cnt[i] = 1;
-    cnt[KV_SEMPTY0] = cnt[KV_SEMPTY0 + 1] = kEwThreads;
-    cnt[KV_PFULL] = kEwThreads;
+    cnt[KV_SEMPTY0] = cnt[KV_SEMPTY0 + 1] = kEwThreads / 2;  // one group per buffer
+    cnt[KV_PFULL0] = cnt[KV_PFULL0 + 1] = kEwThreads / 2;
     for (int i = 0; i < kRing; ++i) cnt[KV_WEMPTY0 + i] = 1 + kEwThreads;
     init_bars(bars, cnt, KV_NUM);
   }
@@ -549,7 +553,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         uint32_t done = 0;
         ok = for_each_qtile(a, it, e.begin, e.end,
                             [&](int64_t h, int64_t qb, int64_t slot, int64_t q0) -> bool {
-          const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
+          const uint32_t st = qd % kKvStages, ph = (qd / kKvStages) & 1;
           if (!mbar_wait(&bars[KV_QEMPTY0 + st], ph ^ 1, a.status)) return false;
           unsigned char* stage = sm + L::kQD + st * L::kStage;
           meta[st].start = q0;
@@ -579,20 +583,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
       uint32_t qd = 0, s_it = 0, p_it = 0, jk = 0;
       bool ok = true;
       auto issue_acc = [&](uint32_t qd_u, bool first) -> bool {
-        if (!mbar_wait(&bars[KV_PFULL], p_it & 1, a.status)) return false;
+        const uint32_t pb = p_it & 1;
+        if (!mbar_wait(&bars[KV_PFULL0 + pb], (p_it >> 1) & 1, a.status)) return false;
         tc_fence_after();
-        const uint32_t st = qd_u % kStages;
+        const uint32_t st = qd_u % kKvStages;
         const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
         const uint32_t do_addr = q_addr + kSub * D * 2;
 #pragma unroll
         for (int kk = 0; kk < kSub / 16; ++kk) {
           const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
-          tc_mma_f16(tmem + kColAcc, smem_desc(pt_addr + kk * 32, 16, 1024),
+          tc_mma_f16(tmem + kColAcc, smem_desc(pt_addr + pb * kRows * kSub * 2 + kk * 32, 16, 1024),
                      smem_desc(do_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
-          tc_mma_f16(tmem + kColAcc + D, smem_desc(dst_addr + kk * 32, 16, 1024),
+          tc_mma_f16(tmem + kColAcc + D, smem_desc(dst_addr + pb * kRows * kSub * 2 + kk * 32, 16, 1024),
                      smem_desc(q_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
         }
-        tc_commit(&bars[KV_PEMPTY]);
+        tc_commit(&bars[KV_PEMPTY0 + pb]);
         tc_commit(&bars[KV_QEMPTY0 + st]);
         ++p_it;
         return true;
@@ -607,7 +612,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         ++jk;
         const uint32_t qd0 = qd;
         for (int i = 0; i < n && ok; ++i) {
-          const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
+          const uint32_t st = qd % kKvStages, ph = (qd / kKvStages) & 1;
           const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
           if (!(ok = mbar_wait(&bars[KV_QFULL0 + st], ph, a.status))) break;
           if (!(ok = mbar_wait(&bars[KV_SEMPTY0 + sb], sph ^ 1, a.status))) break;
@@ -635,11 +640,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
     }
   } else {
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;    // which 32 of the 64 query columns
+    // Two groups of 4 warps ping-pong over the sub-tiles: group g takes the sub-tiles with
+    // s_it % 2 == g (TMEM S^T/dP^T buffer g, P^T/dS^T buffer g); each thread owns one key
+    // row and all 64 query columns of its group's sub-tiles.
+    const int grp = (warp - 2) >> 2;
+    const int half = grp;                // epilogue: which half of the D columns
     const int rl = quarter * 32 + lane;  // key row within the tile
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const float scale2 = a.scale * kLog2e;
-    uint32_t s_it = 0, p_it = 0, done_it = 0, qd = 0;
+    uint32_t s_it = 0, done_it = 0, qd = 0;
     bool ok = true;
     for (uint32_t w = 0; ok; ++w) {
       WorkEntry e;
@@ -648,54 +657,61 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
       const KvItem it = kv_item(a, e.item);
       const int n = e.end - e.begin;
       const int64_t key = it.k0 + rl;
-      for (int i = 0; i < n && ok; ++i) {
+      for (int i = 0; i < n && ok; ++i, ++qd, ++s_it) {
+        const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
+        if ((int)sb != grp) continue;  // the other group's sub-tile
         // the stage's TMA writes (Q, dO, row stats) and its meta are visible once its phase
         // completed; the stage stays resident until the dV/dK MMAs of this sub-tile
-        const uint32_t st = qd % kStages, ph = (qd / kStages) & 1;
-        ++qd;
+        const uint32_t st = qd % kKvStages, ph = (qd / kKvStages) & 1;
         if (!(ok = mbar_wait(&bars[KV_QFULL0 + st], ph, a.status))) break;
         const float* stats = reinterpret_cast<const float*>(sm + L::kQD + st * L::kStage + L::kStats);
         const int64_t q0 = meta[st].start;
         const float b2 = meta[st].b2;
-        const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
         if (!(ok = mbar_wait(&bars[KV_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
-        float s[32], dp[32];
-        tmem_ld32(lane_addr + kColS + sb * kSub + half * 32, s);
-        tmem_ld32(lane_addr + kColP + sb * kSub + half * 32, dp);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&bars[KV_SEMPTY0 + sb]);
-        ++s_it;
         // query q0 + c sees this key iff key < N, q0 + c < N and, when causal, key <= q0 + c
-        const int64_t qh = q0 + half * 32;
         const bool key_ok = key < a.N;
-        const int64_t cmin = a.causal ? key - qh : 0;  // first visible query offset
-        const int64_t cend = a.N - qh;                 // offsets >= cend are padding rows
-        const float* l2 = stats + half * 32;
-        const float* dl = stats + kSub + half * 32;
-        uint32_t pk[16], dk[16];
+        const int64_t cmin = a.causal ? key - q0 : 0;  // first visible query offset
+        const int64_t cend = a.N - q0;                 // offsets >= cend are padding rows
+        unsigned char* pt = sm + L::kPT + sb * kRows * kSub * 2;
+        unsigned char* dt = sm + L::kDST + sb * kRows * kSub * 2;
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float p0 = 0.f, p1 = 0.f, d0 = 0.f, d1 = 0.f;
-          if (key_ok && c >= cmin && c < cend) {
-            p0 = fast_exp2(fmaf(s[c], scale2, b2) - l2[c]);
-            d0 = p0 * (dp[c] - dl[c]) * a.scale;
+        for (int hc = 0; hc < 2; ++hc) {  // two 32-column halves keep the live registers low
+          float s[32], dp[32];
+          tmem_ld32(lane_addr + kColS + sb * kSub + hc * 32, s);
+          tmem_ld32(lane_addr + kColP + sb * kSub + hc * 32, dp);
+          tmem_wait_ld();
+          if (hc == 1) {
+            tc_fence_before();
+            mbar_arrive(&bars[KV_SEMPTY0 + sb]);
           }
-          if (key_ok && c + 1 >= cmin && c + 1 < cend) {
-            p1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - l2[c + 1]);
-            d1 = p1 * (dp[c + 1] - dl[c + 1]) * a.scale;
+          const float* l2 = stats + hc * 32;
+          const float* dl = stats + kSub + hc * 32;
+          uint32_t pk[16], dk[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const int cc = hc * 32 + c;
+            float p0 = 0.f, p1 = 0.f, d0 = 0.f, d1 = 0.f;
+            if (key_ok && cc >= cmin && cc < cend) {
+              p0 = fast_exp2(fmaf(s[c], scale2, b2) - l2[c]);
+              d0 = p0 * (dp[c] - dl[c]) * a.scale;
+            }
+            if (key_ok && cc + 1 >= cmin && cc + 1 < cend) {
+              p1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - l2[c + 1]);
+              d1 = p1 * (dp[c + 1] - dl[c + 1]) * a.scale;
+            }
+            pk[c / 2] = pack2(p0, p1, BF16);
+            dk[c / 2] = pack2(d0, d1, BF16);
           }
-          pk[c / 2] = pack2(p0, p1, BF16);
-          dk[c / 2] = pack2(d0, d1, BF16);
+          // P^T/dS^T buffer sb is free once the dV/dK MMAs of sub-tile s_it - 2 completed
+          if (hc == 0 && !(ok = mbar_wait(&bars[KV_PEMPTY0 + sb], sph ^ 1, a.status))) break;
+          st_half_row_sw128(pt, rl, hc * 4, pk);
+          st_half_row_sw128(dt, rl, hc * 4, dk);
         }
-        if (!(ok = mbar_wait(&bars[KV_PEMPTY], (p_it & 1) ^ 1, a.status))) break;
-        st_half_row_sw128(sm + L::kPT, rl, half * 4, pk);
-        st_half_row_sw128(sm + L::kDST, rl, half * 4, dk);
+        if (!ok) break;
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(&bars[KV_PFULL]);
-        ++p_it;
+        mbar_arrive(&bars[KV_PFULL0 + sb]);
       }
       if (!ok) break;
       if (n > 0) {

@@ -154,6 +154,50 @@ __global__ void delta_kernel(AttnParams p) {
   }
 }
 
+// Vectorised Delta / row stats: LPR lanes per row, 16-byte loads of O and dO; same outputs
+// as delta_kernel.  Rows (and their bases) must be 16-byte aligned.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) delta_vec_kernel(AttnParams p) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int LPR = D / VEC;  // lanes per row (<= 32)
+  constexpr int RPW = 32 / LPR;
+  const int lane = threadIdx.x & 31;
+  const int64_t npad = (p.N + 63) / 64 * 64;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t gr = gw * RPW + lane / LPR;  // padded row index over (Z*H, npad)
+  const int li = lane % LPR;
+  const bool in_range = gr < p.Z * p.H * npad;
+  const int64_t row = in_range ? gr % npad : 0, zh = in_range ? gr / npad : 0;
+  const int64_t z = zh / p.H, h = zh % p.H;
+  float a = 0.f, l2 = 0.f;
+  if (in_range && row < p.N) {
+    const uint4 ov = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.out) + z * p.os[0] +
+                                                     h * p.os[1] + row * p.os[2] + li * VEC);
+    const uint4 gv = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.dout) + z * p.dos[0] +
+                                                     h * p.dos[1] + row * p.dos[2] + li * VEC);
+    const T* oe = reinterpret_cast<const T*>(&ov);
+    const T* ge = reinterpret_cast<const T*>(&gv);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) a = fmaf(to_f32<T>(oe[i]), to_f32<T>(ge[i]), a);
+  }
+#pragma unroll
+  for (int off = LPR / 2; off; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+  if (in_range && li == 0) {
+    if (row < p.N) {
+      const float lv = p.lse[zh * p.N + row];
+      l2 = lv == -INFINITY ? 0.f : lv * kLog2e;
+      p.delta[zh * p.N + row] = a;
+    } else {
+      a = 0.f;
+    }
+    if (p.stats) {
+      float* st = p.stats + (zh * (npad / 64) + row / 64) * 128;
+      st[row % 64] = l2;
+      st[64 + row % 64] = a;
+    }
+  }
+}
+
 // dQ over the forward lists (+ soft-bias gradient).  grid (ceil(N / kBM), Z*H).
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads) dq_simt_kernel(AttnParams p) {
@@ -437,9 +481,27 @@ int launch_bwd_simt(const AttnParams& p, cudaStream_t s, int parts) {
   return fail(SA_EUNSUPPORTED, "dtype");
 }
 
+template <typename T, int D>
+int launch_delta_vec(const AttnParams& p, cudaStream_t s, int64_t rows) {
+  constexpr int RPW = 32 / (D / (16 / (int)sizeof(T)));
+  const int64_t warps = (rows + RPW - 1) / RPW;
+  delta_vec_kernel<T, D><<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(p);
+  return check_launch("delta_vec_kernel");
+}
+
 int launch_delta(const AttnParams& p, cudaStream_t s) {
   const int64_t rows = p.Z * p.H * ((p.N + 63) / 64 * 64);
   if (rows == 0) return SA_OK;
+  const int esz = p.dtype == SA_F32 ? 4 : 2;
+  bool vec = reinterpret_cast<uintptr_t>(p.out) % 16 == 0 &&
+             reinterpret_cast<uintptr_t>(p.dout) % 16 == 0;
+  for (int i = 0; i < 3; ++i) vec = vec && (p.os[i] * esz) % 16 == 0 && (p.dos[i] * esz) % 16 == 0;
+  if (vec && p.dtype != SA_F32 && (p.D == 64 || p.D == 128)) {
+    const bool bf = p.dtype == SA_BF16;
+    if (p.D == 128) return bf ? launch_delta_vec<__nv_bfloat16, 128>(p, s, rows)
+                              : launch_delta_vec<__half, 128>(p, s, rows);
+    return bf ? launch_delta_vec<__nv_bfloat16, 64>(p, s, rows) : launch_delta_vec<__half, 64>(p, s, rows);
+  }
   const int threads = 256;
   const int64_t blocks = (rows * 32 + threads - 1) / threads;
   switch (p.dtype) {
