@@ -35,7 +35,7 @@ namespace {
 constexpr int kRows = 128;  // resident tile rows (TMEM lanes)
 constexpr int kSub = 64;    // streamed sub-tile rows
 constexpr int kStages = 3;    // streamed ring depth (dQ kernel)
-constexpr int kKvStages = 2;  // streamed ring depth (dK/dV kernel: P^T/dS^T are double-buffered)
+constexpr int kKvStages = 4;  // streamed ring depth (dK/dV kernel)
 constexpr int kEw = 8;                      // elementwise warps: 2 per TMEM lane quarter
 constexpr int kEwThreads = kEw * 32;
 constexpr int kBwdThreads = 64 + kEwThreads;
@@ -429,18 +429,15 @@ struct DkvLayout {
   static constexpr uint32_t kQD = 2 * kRows * D * 2;        // stages x (Q, dO, stats)
   static constexpr uint32_t kStats = 2 * kSub * D * 2;      // stage offset: lse2[64], delta[64]
   static constexpr uint32_t kStage = kStats + 1024;         // keeps the tiles 1024-aligned
-  static constexpr uint32_t kPT = kQD + kKvStages * kStage;  // 2 x P^T [128][64]
-  static constexpr uint32_t kDST = kPT + 2 * kRows * kSub * 2;  // 2 x dS^T [128][64]
-  static constexpr uint32_t kBars = kDST + 2 * kRows * kSub * 2;
+  static constexpr uint32_t kBars = kQD + kKvStages * kStage;
   static constexpr uint32_t kMeta = kBars + 256;  // StageMeta[kStages]
   static constexpr uint32_t kRingOff = kMeta + 128;  // WorkEntry[kRing]
   static constexpr uint32_t kAlloc = kRingOff + 128 + 1024;
 };
 
 enum { KV_KVFULL = 0, KV_KVEMPTY, KV_QFULL0, KV_QEMPTY0 = KV_QFULL0 + kKvStages,
-       KV_SFULL0 = KV_QEMPTY0 + kKvStages, KV_SEMPTY0 = KV_SFULL0 + 2, KV_PFULL0 = KV_SEMPTY0 + 2,
-       KV_PEMPTY0 = KV_PFULL0 + 2, KV_DONE = KV_PEMPTY0 + 2, KV_WFULL0,
-       KV_WEMPTY0 = KV_WFULL0 + kRing, KV_NUM = KV_WEMPTY0 + kRing };
+       KV_SFULL0 = KV_QEMPTY0 + kKvStages, KV_PFULL0 = KV_SFULL0 + 2, KV_DONE = KV_PFULL0 + 2,
+       KV_WFULL0, KV_WEMPTY0 = KV_WFULL0 + kRing, KV_NUM = KV_WEMPTY0 + kRing };
 
 struct KvItem {
   int64_t z, hk, k0, kb;
@@ -507,8 +504,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
   if (threadIdx.x == 0) {
     uint32_t cnt[KV_NUM];
     for (int i = 0; i < KV_NUM; ++i) cnt[i] = 1;
-    cnt[KV_SEMPTY0] = cnt[KV_SEMPTY0 + 1] = kEwThreads / 2;  // one group per buffer
-    cnt[KV_PFULL0] = cnt[KV_PFULL0 + 1] = kEwThreads / 2;
+    cnt[KV_PFULL0] = cnt[KV_PFULL0 + 1] = kEwThreads / 2;  // one group per buffer
     for (int i = 0; i < kRing; ++i) cnt[KV_WEMPTY0 + i] = 1 + kEwThreads;
     init_bars(bars, cnt, KV_NUM);
   }
@@ -579,7 +575,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
       constexpr uint32_t id_s = idesc_f16(kRows, kSub, BF16, false, false);
       constexpr uint32_t id_acc = idesc_f16(kRows, D, BF16, false, true);
       const uint32_t k_addr = smem_u32(sm + L::kK), v_addr = smem_u32(sm + L::kV);
-      const uint32_t pt_addr = smem_u32(sm + L::kPT), dst_addr = smem_u32(sm + L::kDST);
       uint32_t qd = 0, s_it = 0, p_it = 0, jk = 0;
       bool ok = true;
       auto issue_acc = [&](uint32_t qd_u, bool first) -> bool {
@@ -589,15 +584,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         const uint32_t st = qd_u % kKvStages;
         const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
         const uint32_t do_addr = q_addr + kSub * D * 2;
+        // P^T / dS^T sit in TMEM over the S^T / dP^T columns of buffer pb (bf16 pairs)
 #pragma unroll
         for (int kk = 0; kk < kSub / 16; ++kk) {
           const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
-          tc_mma_f16(tmem + kColAcc, smem_desc(pt_addr + pb * kRows * kSub * 2 + kk * 32, 16, 1024),
-                     smem_desc(do_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
-          tc_mma_f16(tmem + kColAcc + D, smem_desc(dst_addr + pb * kRows * kSub * 2 + kk * 32, 16, 1024),
-                     smem_desc(q_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
+          tc_mma_f16_ts(tmem + kColAcc, tmem + kColS + pb * kSub + kk * 8,
+                        smem_desc(do_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
+          tc_mma_f16_ts(tmem + kColAcc + D, tmem + kColP + pb * kSub + kk * 8,
+                        smem_desc(q_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
         }
-        tc_commit(&bars[KV_PEMPTY0 + pb]);
         tc_commit(&bars[KV_QEMPTY0 + st]);
         ++p_it;
         return true;
@@ -613,9 +608,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         const uint32_t qd0 = qd;
         for (int i = 0; i < n && ok; ++i) {
           const uint32_t st = qd % kKvStages, ph = (qd / kKvStages) & 1;
-          const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
+          const uint32_t sb = s_it & 1;
           if (!(ok = mbar_wait(&bars[KV_QFULL0 + st], ph, a.status))) break;
-          if (!(ok = mbar_wait(&bars[KV_SEMPTY0 + sb], sph ^ 1, a.status))) break;
+          // TMEM buffer sb is reusable: the dV/dK MMAs of sub-tile s_it - 2, which read its
+          // P^T / dS^T, were issued (after their PFULL wait) before this point, and MMAs of one
+          // thread execute in issue order.
           tc_fence_after();
           const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
           const uint32_t do_addr = q_addr + kSub * D * 2;
@@ -673,18 +670,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         const bool key_ok = key < a.N;
         const int64_t cmin = a.causal ? key - q0 : 0;  // first visible query offset
         const int64_t cend = a.N - q0;                 // offsets >= cend are padding rows
-        unsigned char* pt = sm + L::kPT + sb * kRows * kSub * 2;
-        unsigned char* dt = sm + L::kDST + sb * kRows * kSub * 2;
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc) {  // two 32-column halves keep the live registers low
           float s[32], dp[32];
           tmem_ld32(lane_addr + kColS + sb * kSub + hc * 32, s);
           tmem_ld32(lane_addr + kColP + sb * kSub + hc * 32, dp);
           tmem_wait_ld();
-          if (hc == 1) {
-            tc_fence_before();
-            mbar_arrive(&bars[KV_SEMPTY0 + sb]);
-          }
           const float* l2 = stats + hc * 32;
           const float* dl = stats + kSub + hc * 32;
           uint32_t pk[16], dk[16];
@@ -703,13 +694,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
             pk[c / 2] = pack2(p0, p1, BF16);
             dk[c / 2] = pack2(d0, d1, BF16);
           }
-          // P^T/dS^T buffer sb is free once the dV/dK MMAs of sub-tile s_it - 2 completed
-          if (hc == 0 && !(ok = mbar_wait(&bars[KV_PEMPTY0 + sb], sph ^ 1, a.status))) break;
-          st_half_row_sw128(pt, rl, hc * 4, pk);
-          st_half_row_sw128(dt, rl, hc * 4, dk);
+          // packed P^T / dS^T overwrite columns [hc*16, hc*16+16) of this lane's S^T / dP^T,
+          // which this thread has already read (half hc = 1 reads columns 32-63 only)
+          tmem_st16(lane_addr + kColS + sb * kSub + hc * 16, pk);
+          tmem_st16(lane_addr + kColP + sb * kSub + hc * 16, dk);
         }
-        if (!ok) break;
-        fence_proxy_async_smem();
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars[KV_PFULL0 + sb]);
       }
