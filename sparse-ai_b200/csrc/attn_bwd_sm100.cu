@@ -374,16 +374,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars[DQ_SEMPTY0 + sb]);
-        int64_t lim = a.N - 1 - k0;  // keys k0 + c with c <= lim are visible to this row
-        if (a.causal) lim = min(lim, row - k0);
-        if (row >= a.N) lim = -1;
+        int64_t lim64 = a.N - 1 - k0;  // keys k0 + c with c <= lim are visible to this row
+        if (a.causal) lim64 = min(lim64, row - k0);
+        if (row >= a.N) lim64 = -1;
+        const int lim = (int)max((int64_t)-1, min((int64_t)kSub, lim64));
+        const bool full = lim >= kSub - 1;
         uint32_t pk[kSub / 2];
         float rs = 0.f;
 #pragma unroll
         for (int c = 0; c < kSub; c += 2) {
-          float d0 = 0.f, d1 = 0.f;
-          if (c <= lim) d0 = fast_exp2(fmaf(s[c], scale2, b2) - lse2) * (dp[c] - dl);
-          if (c + 1 <= lim) d1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - lse2) * (dp[c + 1] - dl);
+          float d0 = fast_exp2(fmaf(s[c], scale2, b2) - lse2) * (dp[c] - dl);
+          float d1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - lse2) * (dp[c + 1] - dl);
+          if (!full) {
+            d0 = c <= lim ? d0 : 0.f;
+            d1 = c + 1 <= lim ? d1 : 0.f;
+          }
           rs += d0 + d1;
           pk[c / 2] = pack2(d0 * a.scale, d1 * a.scale, BF16);
         }
@@ -666,33 +671,42 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         const float b2 = meta[st].b2;
         if (!(ok = mbar_wait(&bars[KV_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
-        // query q0 + c sees this key iff key < N, q0 + c < N and, when causal, key <= q0 + c
-        const bool key_ok = key < a.N;
-        const int64_t cmin = a.causal ? key - q0 : 0;  // first visible query offset
-        const int64_t cend = a.N - q0;                 // offsets >= cend are padding rows
+        // query q0 + c sees this key iff key < N, q0 + c < N and, when causal, key <= q0 + c:
+        // visible columns are [lo, hi) (int32, clamped once per sub-tile)
+        const int64_t cmin = a.causal ? key - q0 : 0;
+        const int lo = (int)max((int64_t)0, min((int64_t)kSub, cmin));
+        const int hi = key < a.N ? (int)max((int64_t)0, min((int64_t)kSub, a.N - q0)) : 0;
+        const bool full = lo == 0 && hi == kSub;
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc) {  // two 32-column halves keep the live registers low
           float s[32], dp[32];
           tmem_ld32(lane_addr + kColS + sb * kSub + hc * 32, s);
           tmem_ld32(lane_addr + kColP + sb * kSub + hc * 32, dp);
           tmem_wait_ld();
-          const float* l2 = stats + hc * 32;
-          const float* dl = stats + kSub + hc * 32;
+          const float4* l2v = reinterpret_cast<const float4*>(stats + hc * 32);
+          const float4* dlv = reinterpret_cast<const float4*>(stats + kSub + hc * 32);
           uint32_t pk[16], dk[16];
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const int cc = hc * 32 + c;
-            float p0 = 0.f, p1 = 0.f, d0 = 0.f, d1 = 0.f;
-            if (key_ok && cc >= cmin && cc < cend) {
-              p0 = fast_exp2(fmaf(s[c], scale2, b2) - l2[c]);
-              d0 = p0 * (dp[c] - dl[c]) * a.scale;
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 l4 = l2v[c4], d4 = dlv[c4];
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+            float p[4], d[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int c = c4 * 4 + u;
+              p[u] = fast_exp2(fmaf(s[c], scale2, b2) - lv[u]);
+              d[u] = p[u] * (dp[c] - dv[u]) * a.scale;
+              if (!full) {
+                const int cc = hc * 32 + c;
+                const bool vis = cc >= lo && cc < hi;
+                p[u] = vis ? p[u] : 0.f;
+                d[u] = vis ? d[u] : 0.f;
+              }
             }
-            if (key_ok && cc + 1 >= cmin && cc + 1 < cend) {
-              p1 = fast_exp2(fmaf(s[c + 1], scale2, b2) - l2[c + 1]);
-              d1 = p1 * (dp[c + 1] - dl[c + 1]) * a.scale;
-            }
-            pk[c / 2] = pack2(p0, p1, BF16);
-            dk[c / 2] = pack2(d0, d1, BF16);
+            pk[c4 * 2] = pack2(p[0], p[1], BF16);
+            pk[c4 * 2 + 1] = pack2(p[2], p[3], BF16);
+            dk[c4 * 2] = pack2(d[0], d[1], BF16);
+            dk[c4 * 2 + 1] = pack2(d[2], d[3], BF16);
           }
           // packed P^T / dS^T overwrite columns [hc*16, hc*16+16) of this lane's S^T / dP^T,
           // which this thread has already read (half hc = 1 reads columns 32-63 only)

@@ -306,9 +306,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         if (!mbar_wait(&bars[B_VFULL0 + (kv & 1)], (kv >> 1) & 1, a.status)) { ok = false; break; }
         const int64_t ks = meta[kv & 1].key_start;
         const float b2 = meta[kv & 1].b2;
-        // keys key_start + c are visible for c <= lim
-        int64_t lim = a.N - 1 - ks;
-        if (a.causal) lim = min(lim, row - ks);
+        // keys key_start + c are visible for c <= lim (int32, clamped once per tile)
+        int64_t lim64 = a.N - 1 - ks;
+        if (a.causal) lim64 = min(lim64, row - ks);
+        const int lim = (int)max((int64_t)-1, min((int64_t)kT, lim64));
         float mt = -INFINITY;
         if (lim >= kT - 1) {
 #pragma unroll
