@@ -34,7 +34,7 @@ namespace {
 
 constexpr int kRows = 128;  // resident tile rows (TMEM lanes)
 constexpr int kSub = 64;    // streamed sub-tile rows
-constexpr int kStages = 3;    // streamed ring depth (dQ kernel)
+constexpr int kStages = 4;    // streamed ring depth (dQ kernel)
 constexpr int kKvStages = 4;  // streamed ring depth (dK/dV kernel)
 constexpr int kEw = 8;                      // elementwise warps: 2 per TMEM lane quarter
 constexpr int kEwThreads = kEw * 32;
@@ -119,19 +119,6 @@ __device__ __forceinline__ void store_cols(void* base, const int64_t* st, int64_
   }
 }
 
-// Half a row (32 elements, four 16-byte units starting at unit u0) into a [rows][64]
-// 128B-swizzled K-major chunk.
-__device__ __forceinline__ void st_half_row_sw128(unsigned char* chunk, int row, int u0,
-                                                  const uint32_t* pk) {
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const uint32_t off = row * 128 + (((u0 + u) ^ (row & 7)) << 4);
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + off)),
-                 "r"(pk[u * 4 + 0]), "r"(pk[u * 4 + 1]), "r"(pk[u * 4 + 2]), "r"(pk[u * 4 + 3])
-                 : "memory");
-  }
-}
-
 // Per streamed stage: what the producer read from the lists, handed to the elementwise
 // warps through shared memory (released by the stage's full mbarrier), so that no consumer
 // reads the lists from global memory on its critical path.
@@ -155,16 +142,15 @@ struct DqLayout {
   static constexpr uint32_t kDO = kRows * D * 2;             // [128][D]
   static constexpr uint32_t kKV = 2 * kRows * D * 2;         // stages x (K [64][D], V [64][D])
   static constexpr uint32_t kStage = 2 * kSub * D * 2;
-  static constexpr uint32_t kDS = kKV + kStages * kStage;    // 2 x [128][64]
-  static constexpr uint32_t kBars = kDS + 2 * kRows * kSub * 2;
+  static constexpr uint32_t kBars = kKV + kStages * kStage;
   static constexpr uint32_t kMeta = kBars + 256;  // StageMeta[kStages]
   static constexpr uint32_t kRingOff = kMeta + 128;  // WorkEntry[kRing]
   static constexpr uint32_t kAlloc = kRingOff + 128 + 1024;
 };
 
 enum { DQ_QFULL = 0, DQ_QEMPTY, DQ_KVFULL0, DQ_KVEMPTY0 = DQ_KVFULL0 + kStages,
-       DQ_SFULL0 = DQ_KVEMPTY0 + kStages, DQ_SEMPTY0 = DQ_SFULL0 + 2, DQ_DSFULL0 = DQ_SEMPTY0 + 2,
-       DQ_DSEMPTY0 = DQ_DSFULL0 + 2, DQ_DONE = DQ_DSEMPTY0 + 2, DQ_WFULL0,
+       DQ_SFULL0 = DQ_KVEMPTY0 + kStages, DQ_DSFULL0 = DQ_SFULL0 + 2, DQ_DONE = DQ_DSFULL0 + 2,
+       DQ_WFULL0,
        DQ_WEMPTY0 = DQ_WFULL0 + kRing, DQ_NUM = DQ_WEMPTY0 + kRing };
 
 struct DqItem {
@@ -206,8 +192,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
   if (threadIdx.x == 0) {
     uint32_t cnt[DQ_NUM];
     for (int i = 0; i < DQ_NUM; ++i) cnt[i] = 1;
-    cnt[DQ_SEMPTY0] = cnt[DQ_SEMPTY0 + 1] = kEwThreads / 2;  // one group per buffer
-    cnt[DQ_DSFULL0] = cnt[DQ_DSFULL0 + 1] = kEwThreads / 2;
+    cnt[DQ_DSFULL0] = cnt[DQ_DSFULL0 + 1] = kEwThreads / 2;  // one group per buffer
     for (int i = 0; i < kRing; ++i) cnt[DQ_WEMPTY0 + i] = 1 + kEwThreads;
     init_bars(bars, cnt, DQ_NUM);
   }
@@ -281,13 +266,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         tc_fence_after();
         const uint32_t st = kv_u % kStages;
         const uint32_t k_addr = smem_u32(sm + L::kKV + st * L::kStage);
-        const uint32_t ds_addr = smem_u32(sm + L::kDS + db * kRows * kSub * 2);
+        // dS (bf16 pairs) sits in TMEM over the S columns of buffer db
 #pragma unroll
         for (int kk = 0; kk < kSub / 16; ++kk)
-          tc_mma_f16(tmem + kColAcc, smem_desc(ds_addr + kk * 32, 16, 1024),
-                     smem_desc(k_addr + kk * 16 * 128, kSub * 128, 1024), id_dq,
-                     (!first || kk > 0) ? 1u : 0u);
-        tc_commit(&bars[DQ_DSEMPTY0 + db]);
+          tc_mma_f16_ts(tmem + kColAcc, tmem + kColS + db * kSub + kk * 8,
+                        smem_desc(k_addr + kk * 16 * 128, kSub * 128, 1024), id_dq,
+                        (!first || kk > 0) ? 1u : 0u);
         tc_commit(&bars[DQ_KVEMPTY0 + st]);
         ++ds_it;
         return true;
@@ -303,10 +287,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         const uint32_t kv0 = kv;
         for (int j = 0; j < n_sub && ok; ++j, ++kv) {
           const uint32_t st = kv % kStages, ph = (kv / kStages) & 1;
-          const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
-          ok = mbar_wait(&bars[DQ_KVFULL0 + st], ph, a.status) &&
-               mbar_wait(&bars[DQ_SEMPTY0 + sb], sph ^ 1, a.status);
-          if (!ok) break;
+          const uint32_t sb = s_it & 1;
+          // TMEM buffer sb is reusable: the dQ MMA of sub-tile s_it - 2 (which reads its dS)
+          // was issued after its DSFULL wait, before this point, in MMA issue order
+          if (!(ok = mbar_wait(&bars[DQ_KVFULL0 + st], ph, a.status))) break;
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sm + L::kKV + st * L::kStage);
           const uint32_t v_addr = k_addr + kSub * D * 2;
@@ -372,8 +356,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         tmem_ld32(lane_addr + kColP + sb * kSub, *reinterpret_cast<float(*)[32]>(dp));
         tmem_ld32(lane_addr + kColP + sb * kSub + 32, *reinterpret_cast<float(*)[32]>(dp + 32));
         tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&bars[DQ_SEMPTY0 + sb]);
         int64_t lim64 = a.N - 1 - k0;  // keys k0 + c with c <= lim are visible to this row
         if (a.causal) lim64 = min(lim64, row - k0);
         if (row >= a.N) lim64 = -1;
@@ -392,11 +374,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
           rs += d0 + d1;
           pk[c / 2] = pack2(d0 * a.scale, d1 * a.scale, BF16);
         }
-        // dS buffer sb is free once the dQ MMA of sub-tile s_it - 2 completed
-        if (!(ok = mbar_wait(&bars[DQ_DSEMPTY0 + sb], sph ^ 1, a.status))) break;
-        st_half_row_sw128(sm + L::kDS + sb * kRows * kSub * 2, rl, 0, pk);
-        st_half_row_sw128(sm + L::kDS + sb * kRows * kSub * 2, rl, 4, pk + 16);
-        fence_proxy_async_smem();
+        // packed dS overwrites columns [0, 32) of this lane's S (already in registers)
+        tmem_st16(lane_addr + kColS + sb * kSub, pk);
+        tmem_st16(lane_addr + kColS + sb * kSub + 16, pk + 16);
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars[DQ_DSFULL0 + sb]);
         if (a.dbias) {
