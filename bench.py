@@ -538,7 +538,7 @@ def run_decode(dev, seed, steps, warmup, flush, peaks):
         "dense_equivalent_bytes": dense_bytes,
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
-        "gpu_launches_per_step": 2,
+        "gpu_launches_per_step": 4,
     }
 
 

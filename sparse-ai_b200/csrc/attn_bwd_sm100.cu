@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
     bool ok = true;
     for (uint32_t w = 0; ok; ++w) {
       WorkEntry e;
-      if (!(ok = ring_get(ring, &bars[DQ_WFULL0], &bars[DQ_WEMPTY0], w, e, a.status))) break;
+      if (!(ok = ring_get_warp(ring, &bars[DQ_WFULL0], &bars[DQ_WEMPTY0], w, e, a.status))) break;
       if (e.item < 0) break;
       const DqItem it = dq_item(a, e.item);
       const int n_sub = e.end - e.begin;
@@ -344,11 +344,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         const int slot = j / spb;
         // this stage's K/V stay resident until the dQ MMA of sub-tile j, which waits for us
         const uint32_t st = kv % kStages;
-        if (!(ok = mbar_wait(&bars[DQ_KVFULL0 + st], (kv / kStages) & 1, a.status))) break;
+        if (!(ok = mbar_wait_warp(&bars[DQ_KVFULL0 + st], (kv / kStages) & 1, a.status))) break;
         const int64_t k0 = meta[st].start;
         const float b2 = meta[st].b2;
         const uint32_t sph = (s_it >> 1) & 1;
-        if (!(ok = mbar_wait(&bars[DQ_SFULL0 + sb], sph, a.status))) break;
+        if (!(ok = mbar_wait_warp(&bars[DQ_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
         float s[kSub], dp[kSub];
         tmem_ld32(lane_addr + kColS + sb * kSub, *reinterpret_cast<float(*)[32]>(s));
@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
       }
       if (!ok) break;
       if (n_sub > 0) {
-        if (!(ok = mbar_wait(&bars[DQ_DONE], done_it & 1, a.status))) break;
+        if (!(ok = mbar_wait_warp(&bars[DQ_DONE], done_it & 1, a.status))) break;
         ++done_it;
         tc_fence_after();
       }
@@ -635,7 +635,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
     bool ok = true;
     for (uint32_t w = 0; ok; ++w) {
       WorkEntry e;
-      if (!(ok = ring_get(ring, &bars[KV_WFULL0], &bars[KV_WEMPTY0], w, e, a.status))) break;
+      if (!(ok = ring_get_warp(ring, &bars[KV_WFULL0], &bars[KV_WEMPTY0], w, e, a.status))) break;
       if (e.item < 0) break;
       const KvItem it = kv_item(a, e.item);
       const int n = e.end - e.begin;
@@ -646,11 +646,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
         // the stage's TMA writes (Q, dO, row stats) and its meta are visible once its phase
         // completed; the stage stays resident until the dV/dK MMAs of this sub-tile
         const uint32_t st = qd % kKvStages, ph = (qd / kKvStages) & 1;
-        if (!(ok = mbar_wait(&bars[KV_QFULL0 + st], ph, a.status))) break;
+        if (!(ok = mbar_wait_warp(&bars[KV_QFULL0 + st], ph, a.status))) break;
         const float* stats = reinterpret_cast<const float*>(sm + L::kQD + st * L::kStage + L::kStats);
         const int64_t q0 = meta[st].start;
         const float b2 = meta[st].b2;
-        if (!(ok = mbar_wait(&bars[KV_SFULL0 + sb], sph, a.status))) break;
+        if (!(ok = mbar_wait_warp(&bars[KV_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
         // query q0 + c sees this key iff key < N, q0 + c < N and, when causal, key <= q0 + c:
         // visible columns are [lo, hi) (int32, clamped once per sub-tile)
@@ -700,7 +700,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
       }
       if (!ok) break;
       if (n > 0) {
-        if (!(ok = mbar_wait(&bars[KV_DONE], done_it & 1, a.status))) break;
+        if (!(ok = mbar_wait_warp(&bars[KV_DONE], done_it & 1, a.status))) break;
         ++done_it;
         tc_fence_after();
       }

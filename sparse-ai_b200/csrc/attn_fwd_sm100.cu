@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     bool ok = true;
     for (uint32_t w = 0; ok; ++w) {
       WorkEntry e;
-      if (!(ok = ring_get(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
+      if (!(ok = ring_get_warp(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
       if (e.item < 0) break;
       const ItemInfo it = item_info(a, e.item);
       const int n_sub = e.end - e.begin;
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       float m_used = -INFINITY, l_sum = 0.f;
       for (int t = 0; t < n_sub && ok; ++t, ++kv) {
         const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
-        if (!mbar_wait(&bars[B_SFULL0 + sb], sph, a.status)) { ok = false; break; }
+        if (!mbar_wait_warp(&bars[B_SFULL0 + sb], sph, a.status)) { ok = false; break; }
         tc_fence_after();
         float s[kT];
 #pragma unroll
@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         ++s_it;
 
         // the V stage of this tile stays resident until PV(t), which waits for this warp
-        if (!mbar_wait(&bars[B_VFULL0 + (kv & 1)], (kv >> 1) & 1, a.status)) { ok = false; break; }
+        if (!mbar_wait_warp(&bars[B_VFULL0 + (kv & 1)], (kv >> 1) & 1, a.status)) { ok = false; break; }
         const int64_t ks = meta[kv & 1].key_start;
         const float b2 = meta[kv & 1].b2;
         // keys key_start + c are visible for c <= lim (int32, clamped once per tile)
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         }
         // P buffer and O are free once PV of the previous tile completed
         if (t > 0) {
-          if (!mbar_wait(&bars[B_ODONE], od & 1, a.status)) { ok = false; break; }
+          if (!mbar_wait_warp(&bars[B_ODONE], od & 1, a.status)) { ok = false; break; }
           ++od;
           tc_fence_after();
           if (__any_sync(0xffffffffu, rescale)) {
@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       // ---------------------------------------------------------------- epilogue
       float inv = 0.f;
       if (n_sub > 0) {
-        if (!mbar_wait(&bars[B_ODONE], od & 1, a.status)) { ok = false; break; }
+        if (!mbar_wait_warp(&bars[B_ODONE], od & 1, a.status)) { ok = false; break; }
         ++od;
         tc_fence_after();
         inv = 1.f / (l_sum == 0.f ? 1.f : l_sum);

@@ -119,6 +119,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   return true;
 }
 
+// mbar_wait by every lane of a warp, with a warp-uniform result: a lane whose bounded wait
+// gave up must not leave the warp while the other lanes go on into warp-collective code
+// (shuffles, tcgen05.ld / st), which would then never complete.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, unsigned* st) {
+  const bool ok = mbar_wait(bar, parity, st);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Generic-proxy shared-memory writes -> visible to the async proxy (tcgen05.mma, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

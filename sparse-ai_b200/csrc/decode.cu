@@ -14,7 +14,7 @@
 // fp32 by log-sum-exp weights (slots in the CTA epilogue, splits in a second kernel).
 #include <string>
 
-#include "common.cuh"
+#include "decode.cuh"
 
 namespace sa {
 namespace {
@@ -22,30 +22,7 @@ namespace {
 constexpr int kDecThreads = 128;
 constexpr int kMaxSplits = 64;
 
-struct DecodeParams {
-  int64_t B, H, Hkv, G, D, page, num_pages, maxL, TD, r, local_blocks;
-  int sink;
-  const void* q;
-  int64_t qs[3];
-  const void* kc;
-  int64_t ks[4];
-  const void* vc;
-  int64_t vs[4];
-  const int32_t* bt;
-  int64_t bts[2];
-  const int32_t* ctx;
-  const void* router;
-  int router_dtype;
-  int64_t rs[3];
-  const void* qrouter;
-  int qrouter_dtype;
-  int64_t qrs[3];
-  void* out;
-  int64_t os[3];
-  float* part;  // [B][Hkv][S][G][D + 2]: m (log2 units), l, acc[D]
-  int S;
-  int stages;
-};
+
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
@@ -395,7 +372,9 @@ int64_t sa_ultrametric_decode_workspace_bytes(int64_t B, int64_t H, int64_t Hkv,
                                               int64_t max_logical_pages) {
   if (B <= 0 || H <= 0 || Hkv <= 0 || D <= 0) return 0;
   const int S = sa::choose_splits(B, Hkv, max_logical_pages);
-  return B * Hkv * (int64_t)S * (H / Hkv) * (D + 2) * (int64_t)sizeof(float);
+  const int64_t general = B * Hkv * (int64_t)S * (H / Hkv) * (D + 2) * (int64_t)sizeof(float);
+  const int64_t fast = sa::decode_fast_workspace_bytes(B, H, Hkv, D, max_logical_pages);
+  return general > fast ? general : fast;
 }
 
 int sa_ultrametric_decode(int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t D,
@@ -472,6 +451,7 @@ int sa_ultrametric_decode(int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t 
   p.part = static_cast<float*>(workspace);
   p.S = choose_splits(B, Hkv, max_logical_pages);
   cudaStream_t s = (cudaStream_t)stream;
+  if (decode_fast_eligible(p, dtype)) return launch_decode_fast(p, dtype, workspace, workspace_bytes, s);
   switch (dtype) {
     case SA_F32: return dispatch_dim<float>(p, s);
     case SA_F16: return dispatch_dim<__half>(p, s);

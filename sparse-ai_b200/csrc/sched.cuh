@@ -81,4 +81,14 @@ __device__ __forceinline__ bool ring_get(const WorkEntry* ring, uint64_t* full, 
   return true;
 }
 
+// ring_get for a whole warp (every lane reads the entry); the result is warp-uniform.
+__device__ __forceinline__ bool ring_get_warp(const WorkEntry* ring, uint64_t* full, uint64_t* empty,
+                                              uint32_t w, WorkEntry& e, unsigned* st) {
+  const uint32_t s = w % kRing, ph = (w / kRing) & 1;
+  if (!mbar_wait_warp(&full[s], ph, st)) return false;
+  e = ring[s];
+  mbar_arrive(&empty[s]);
+  return true;
+}
+
 }  // namespace sa

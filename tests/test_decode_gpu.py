@@ -97,6 +97,51 @@ def test_decode_gqa_vs_oracle(B, H, Hkv, D, page, lo, hi, TD, rd, local, sink, s
         assert_half_close(out, ref, "decode")
 
 
+@pytest.mark.parametrize("B,H,Hkv,D,page,lo,hi,TD,rd,local,sink,shared,dtype", [
+    (3, 16, 1, 128, 128, 1, 1000, 6, 2, 1, True, False, torch.bfloat16),  # 16 heads per KV head
+    (2, 4, 2, 64, 256, 300, 1200, 5, 1, 0, True, True, torch.float16),   # tiles inside a page
+    (6, 8, 8, 128, 16, 1, 400, 6, 3, 2, False, True, torch.bfloat16),    # 4 pages per tile
+    (5, 8, 4, 64, 32, 1, 700, 6, 2, 1, True, False, torch.bfloat16),     # 2 pages per tile
+    (4, 12, 4, 128, 64, 1, 5000, 7, 2, 3, True, False, torch.bfloat16),  # 3 heads per KV head
+    (3, 8, 2, 128, 48, 10, 900, 5, 2, 1, True, False, torch.bfloat16),   # general path (page 48)
+])
+def test_decode_fast_path_shapes(B, H, Hkv, D, page, lo, hi, TD, rd, local, sink, shared, dtype):
+    """Shapes of the tensor-core path: group sizes 1..16, page sizes 16..256 (several pages
+    per 64-token tile, several tiles per page, partial last pages), and one shape that
+    takes the general path, all against the fp64 oracle."""
+    q, kc, vc, bt, ctx, ri, qri = make_paged(B, H, Hkv, D, page, lo, hi, TD, seed=B * 11 + page,
+                                             dtype=dtype, shared_routes=shared)
+    out = ultrametric_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), ctx.to(DEV), ri.to(DEV),
+                             qri.to(DEV), rd, local_blocks=local, sink_block=sink)
+    ref = dor.ultrametric_decode_reference(q.float(), kc.float(), vc.float(), bt, ctx, ri, qri, rd,
+                                           local_blocks=local, sink_block=sink,
+                                           compute_dtype=torch.float64)
+    assert_half_close(out, ref, "decode")
+
+
+def test_decode_nonfinite_cache_past_context():
+    """Cache slots past a request's context length hold inf / NaN (stale memory); the
+    result must not see them (the reference loads them masked to 0)."""
+    B, H, Hkv, D, page, TD = 3, 8, 2, 128, 64, 6
+    q, kc, vc, bt, ctx, ri, qri = make_paged(B, H, Hkv, D, page, 70, 300, TD, seed=5,
+                                             shared_routes=True)
+    kc2, vc2 = kc.clone(), vc.clone()
+    for b in range(B):
+        n = int(ctx[b])
+        last = int(bt[b, (n - 1) // page])
+        r = n - ((n - 1) // page) * page
+        if r < page:
+            kc2[last, :, r:] = float("nan")
+            vc2[last, :, r:] = float("inf")
+    out = ultrametric_decode(q.to(DEV), kc2.to(DEV), vc2.to(DEV), bt.to(DEV), ctx.to(DEV),
+                             ri.to(DEV), qri.to(DEV), 2, local_blocks=1, sink_block=True)
+    ref = dor.ultrametric_decode_reference(q.float(), kc.float(), vc.float(), bt, ctx, ri, qri, 2,
+                                           local_blocks=1, sink_block=True,
+                                           compute_dtype=torch.float64)
+    assert torch.isfinite(out).all()
+    assert_half_close(out, ref, "decode")
+
+
 def test_decode_c3_shape_subset():
     """BASELINE C3 per-request shape (H=32/8, D=128, page 64, ctx in [2048, 32768],
     req_depth 4, sink + last page) with 16 of the 64 requests to bound host memory; the

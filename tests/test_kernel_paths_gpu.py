@@ -66,6 +66,27 @@ def test_builder_and_decode_kernels_run():
     ri = torch.zeros(8, H, 3, dtype=torch.int32, device=DEV)
     qri = torch.zeros(B, H, 3, dtype=torch.int32, device=DEV)
     names = kernel_names(lambda: ultrametric_decode(q, kc, kc, bt, ctx, ri, qri, 2))
-    assert any("decode_split_kernel" in n for n in names), names
-    assert any("decode_combine_kernel" in n for n in names), names
+    for k in ("decode_init_kernel", "decode_select_kernel", "decode_stream_kernel",
+              "decode_unit_combine_kernel"):
+        assert any(k in n for n in names), names
+    assert not any("decode_split_kernel" in n for n in names), names
+    assert _native.read_device_status() == 0
+
+
+def test_decode_general_path_for_other_shapes():
+    """fp32 caches (and page sizes other than 16, 32 or a multiple of 64) take the general
+    split-K kernel."""
+    B, H, Hkv, D, page = 2, 4, 2, 64, 48
+    gen = torch.Generator().manual_seed(0)
+    q = randn((B, H, D), gen).to(DEV)
+    kc = randn((6, Hkv, page, D), gen).to(DEV)
+    bt = torch.arange(6, dtype=torch.int32, device=DEV).view(2, 3)
+    ctx = torch.tensor([100, 144], dtype=torch.int32, device=DEV)
+    ri = torch.zeros(6, H, 3, dtype=torch.int32, device=DEV)
+    qri = torch.zeros(B, H, 3, dtype=torch.int32, device=DEV)
+    for dt in (torch.float32, torch.bfloat16):
+        names = kernel_names(lambda: ultrametric_decode(q.to(dt), kc.to(dt), kc.to(dt), bt, ctx, ri,
+                                                        qri, 2))
+        assert any("decode_split_kernel" in n for n in names), (dt, names)
+        assert not any("decode_stream_kernel" in n for n in names), (dt, names)
     assert _native.read_device_status() == 0
