@@ -557,6 +557,15 @@ def run_ours(args):
     peaks, peak_kind = load_peaks()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
+    if args.decode_only:  # profiling aid: the C3 decode alone, one JSON line
+        d = run_decode(dev, rank, args.steps, args.warmup, flush, peaks)
+        if rank == 0:
+            print(json.dumps({"decode": d}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
     t_heads = c2_thresholds(0) if args.threshold is None else [args.threshold] * C2["H"]
     prob = C2Problem(dev, seed=rank, t_heads=t_heads)
     with ClockSampler(local) as clk:
@@ -637,6 +646,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--quick", action="store_true", help="headline only (no sweep / decode)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="profiling aid: time only the C3 routed decode")
     ap.add_argument("--threshold", type=int, default=None,
                     help="profiling aid: every head uses this LCA threshold instead of the seeded mix")
     args = ap.parse_args()

@@ -226,8 +226,8 @@ SA_API int sa_ultrametric_decode(int dtype, int64_t B, int64_t H, int64_t Hkv, i
  * for callers that cannot allocate device memory when they decode (a serving loop whose
  * memory is carved up front by its own pool and that binds only this C ABI, or a host that
  * must not trigger cudaMalloc's implicit synchronisation mid-step).  Same arguments and
- * results as sa_ultrametric_decode minus the workspace pair; the split-K workspace comes
- * from a fixed 16 MiB device array inside the library (held by every GPU that loads it
+ * results as sa_ultrametric_decode minus the workspace pair; the workspace (page lists,
+ * chunk table, partials) comes from a fixed 16 MiB device array inside the library (held by every GPU that loads it
  * until exit).  Requests needing more than 16 MiB of workspace return SA_EWORKSPACE.  The
  * first call on a device looks the array up (make it before any stream capture).  All
  * calls share the array: calls that overlap on the GPU race.  Allocates nothing.

@@ -5,24 +5,27 @@
 // pairs, dS = P * (dP - Delta), dQ = scale * dS K, dK = scale * dS^T Q, dV = P^T dO,
 // d_soft_bias[z,h,qb,t] = sum of the unscaled dS of the block pair.
 //
-// Both kernels are persistent (one CTA per SM), 6 warps:
-//   warp 0      TMA producer
+// Both kernels are persistent (one CTA per SM, work from the planner's queue), 10 warps:
+//   warp 0      TMA producer (and the queue fetch)
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
-//   warps 2-9   elementwise warps: a thread owns one TMEM lane (row) and half of the
-//               64 columns of each streamed sub-tile (two warps per lane quarter)
+//   warps 2-9   two elementwise groups of 4 warps (a thread owns one TMEM lane = row); the
+//               groups ping-pong over the streamed sub-tiles (group = sub-tile index % 2), so
+//               one group's TMEM loads and exp2 overlap the other's
 //
 // dQ kernel:   work item = (128-row query tile, z, h); Q and dO tiles resident; the listed
-//              key blocks stream as 64-key sub-tiles (K and V) through a 3-stage ring.
+//              key blocks stream as 64-key sub-tiles (K and V) through a 4-stage ring.
 //                S[b]  = Q  K_j^T  (M=128, N=64, K=D)     b = j % 2 (TMEM double buffer)
 //                dP[b] = dO V_j^T  (M=128, N=64, K=D)
-//                dQ   += dS_j K_j  (M=128, N=D, K=64)     dS_j bf16/fp16 in smem (x2)
-// dK/dV kernel: work item = (128-key tile, z, KV head); K and V tiles resident; for every
+//                dQ   += dS_j K_j  (M=128, N=D, K=64)     dS_j (bf16 pairs) written back
+//                                                         into TMEM over S[b]: A from TMEM
+// dK/dV kernel: work item = (128-key tile, z, KV head) or a chunk of a heavy one (fp32
+//              partials, summed by dkdv_reduce_kernel); K and V tiles resident; for every
 //              query head of the GQA group and every query block of its transposed list,
-//              64-row sub-tiles of Q and dO stream through a 3-stage ring.
+//              64-row sub-tiles of Q, dO and their row stats stream through a 4-stage ring.
 //                S^T[b]  = K Q_i^T  (M=128, N=64, K=D)
 //                dP^T[b] = V dO_i^T (M=128, N=64, K=D)
-//                dV     += P^T_i dO_i (M=128, N=D, K=64)
-//                dK     += dS^T_i Q_i (M=128, N=D, K=64)
+//                dV     += P^T_i dO_i (M=128, N=D, K=64)  P^T (bf16) in TMEM over S^T[b]
+//                dK     += dS^T_i Q_i (M=128, N=D, K=64)  dS^T (bf16) in TMEM over dP^T[b]
 // The elementwise warps never rescale: the forward's LSE is final.
 #include <string>
 #include <type_traits>

@@ -16,7 +16,9 @@
 //               exp2, P (bf16/fp16) written to shared memory in the MMA's swizzled K-major
 //               layout; O rescaled in TMEM only when the row max grows by more than 2^8
 //               (lazy rescale); epilogue O / l -> global, LSE.
-// Work item = (query tile of 128 rows, z, h); items with late query tiles go first.
+// Work item = (query tile of 128 rows, z, h).  With a planner workspace the items come
+// heaviest-first from the device-built queue (one atomic per item); without one, round-robin
+// with late (heavier, under causal masking) query tiles first.
 #include <string>
 #include <type_traits>
 
