@@ -455,6 +455,7 @@ def run_sweep(dev, flush, steps):
             "sparsity_causal": round(1 - kept / (C2["H"] * NB * (NB + 1) / 2), 4),
             "step_ms": round(ms, 4), "fwd_ms": round(parts["fwd"], 4), "bwd_ms": round(bwd_ms, 4),
             "build_ms": round(parts["build"], 4),
+            "parts_ms": {k: round(v, 4) for k, v in parts.items()},
             "fwd_kept_tflops": round(fwd_tf, 2),
             "fwd_bwd_kept_tflops": round(prob.flops_alg / (ms * 1e-3) / 1e12, 2),
             "dense_sdpa": sd,

@@ -856,18 +856,18 @@ int64_t bwd_plan_bytes(int which, int64_t Z, int64_t H, int64_t Hkv, int64_t N, 
   return plan_workspace_bytes(kPlanDkdv, items, (int)std::min<int64_t>(items, sms), D);
 }
 
-int plan_bwd_sm100(const AttnParams& p, cudaStream_t stream) {
+int plan_bwd_sm100(const AttnParams& p, cudaStream_t stream, int which) {
   if (!bwd_sm100_eligible(p)) return SA_OK;
   const int64_t tiles = (p.N + kRows - 1) / kRows;
   const int sms = device_sm_count();
-  if (p.plan_dq) {
+  if (p.plan_dq && (which & kBwdDq)) {
     const int64_t items = p.Z * p.H * tiles;
     const int ctas = (int)std::min<int64_t>(items, sms);
     const int rc = launch_plan(kPlanDq, p, items, ctas, plan_carve(p.plan_dq, kPlanDq, items, ctas, p.D),
                                stream);
     if (rc) return rc;
   }
-  if (p.plan_dkdv) {
+  if (p.plan_dkdv && (which & kBwdDkDv)) {
     const int64_t items = p.Z * p.Hkv * tiles;
     const int ctas = (int)std::min<int64_t>(items, sms);
     const int rc = launch_plan(kPlanDkdv, p, items, ctas,

@@ -64,6 +64,8 @@ int launch_bwd_sm100(const AttnParams& p, cudaStream_t stream, int parts);
 // and the plan launches of the backward (run after the transposed lists exist).
 int64_t fwd_plan_bytes(int64_t Z, int64_t H, int64_t N, int64_t D);
 int64_t bwd_plan_bytes(int which, int64_t Z, int64_t H, int64_t Hkv, int64_t N, int64_t D);
-int plan_bwd_sm100(const AttnParams& p, cudaStream_t stream);
+// Work queues of the tcgen05 dQ (kBwdDq: needs the forward counts) and dK/dV (kBwdDkDv:
+// needs the transposed counts) kernels.
+int plan_bwd_sm100(const AttnParams& p, cudaStream_t stream, int which);
 
 }  // namespace sa

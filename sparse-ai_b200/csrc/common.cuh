@@ -294,6 +294,8 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool ab_bf16, boo
 // host: device properties and tensor maps
 // ---------------------------------------------------------------------------------------
 int device_sm_count();
+// Per-thread, per-device second stream with fork / join events (created on first use).
+int side_stream(cudaStream_t* stream, cudaEvent_t* fork, cudaEvent_t* join);
 // 4-D tiled TMA map over (Z, heads, N, D) with element strides (z, h, n, d==1).
 int make_tmap_4d(CUtensorMap* map, const void* base, int dtype, int64_t Z, int64_t Hh, int64_t N,
                  int64_t D, const int64_t* strides, uint32_t box_d, uint32_t box_n);

@@ -44,6 +44,34 @@ unsigned* device_status_ptr() {
   return ptrs[dev];
 }
 
+// A second stream (and a fork / join event pair) per host thread and device, created on
+// first use, for independent launches inside one entry point.  It has the highest stream
+// priority: its small latency-bound kernels get SM slots ahead of a wide kernel running
+// beside them on the caller's stream.
+int side_stream(cudaStream_t* out, cudaEvent_t* fork, cudaEvent_t* join) {
+  struct Side {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+  };
+  thread_local Side side[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(SA_ELAUNCH, "side stream: no current device");
+  Side& d = side[dev];
+  if (!d.s) {
+    int least = 0, greatest = 0;
+    cudaDeviceGetStreamPriorityRange(&least, &greatest);
+    if (cudaStreamCreateWithPriority(&d.s, cudaStreamNonBlocking, greatest) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d.join, cudaEventDisableTiming) != cudaSuccess)
+      return check_launch("side stream creation");
+  }
+  *out = d.s;
+  *fork = d.fork;
+  *join = d.join;
+  return SA_OK;
+}
+
 int device_sm_count() {
   static int counts[kMaxDevices] = {};
   int dev = 0;
