@@ -117,6 +117,18 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
+def max_over_ranks(values, world, device):
+    """Elementwise max over the ranks of per-rank device timings (ms): with weak scaling the
+    job takes as long as its slowest rank.  A no-op for one rank."""
+    vals = [float(v) for v in values]
+    if world <= 1:
+        return vals
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 def dist_setup(n_gpus):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -467,7 +479,7 @@ def run_sweep(dev, flush, steps):
     return rows
 
 
-def run_decode(dev, seed, steps, warmup, flush, peaks):
+def run_decode(dev, seed, steps, warmup, flush, peaks, world=1, barrier=None):
     """C3: 64 requests, H=32/8, D=128, page 64, ctx ~U[2048, 32768], shuffled pool,
     tree routes on the logical page index (depth 9), random query leaf, req_depth 4,
     sink + most recent page."""
@@ -520,6 +532,8 @@ def run_decode(dev, seed, steps, warmup, flush, peaks):
     for _ in range(warmup):
         one()
     torch.cuda.synchronize()
+    if barrier:
+        barrier()
     tot = 0.0
     for _ in range(steps):
         flush_l2(flush)
@@ -529,12 +543,14 @@ def run_decode(dev, seed, steps, warmup, flush, peaks):
         e1.record()
         e1.synchronize()
         tot += e0.elapsed_time(e1)
-    ms = tot / steps
-    gbs = routed_bytes / (ms * 1e-3) / 1e9
+    # each rank decodes its own batch (weak scaling): whole-job rates over the slowest rank
+    ms = max_over_ranks([tot / steps], world, dev)[0]
+    gbs = world * routed_bytes / (ms * 1e-3) / 1e9
     dense_bytes = int(n_log.sum()) * page * Hkv * D * 2 * 2
     return {
         "config": "C3: 64 req x 1 token, H=32/8, D=128, page 64, ctx~U[2048,32768], req_depth 4, sink+last page",
-        "ms_per_step": round(ms, 4), "tok_per_s": round(B / (ms * 1e-3), 1),
+        "ms_per_step": round(ms, 4), "tok_per_s": round(world * B / (ms * 1e-3), 1),
+        "requests_per_gpu": B,
         "routed_gbs": round(gbs, 1), "routed_bytes": routed_bytes, "routed_pages": sel_pages,
         "dense_equivalent_bytes": dense_bytes,
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
@@ -559,7 +575,7 @@ def run_ours(args):
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
     if args.decode_only:  # profiling aid: the C3 decode alone, one JSON line
-        d = run_decode(dev, rank, args.steps, args.warmup, flush, peaks)
+        d = run_decode(dev, rank, args.steps, args.warmup, flush, peaks, world, barrier)
         if rank == 0:
             print(json.dumps({"decode": d}), flush=True)
         if world > 1:
@@ -571,11 +587,10 @@ def run_ours(args):
     prob = C2Problem(dev, seed=rank, t_heads=t_heads)
     with ClockSampler(local) as clk:
         total_ms, parts = time_c2(prob, args.steps, args.warmup, flush, barrier)
-    my = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        import torch.distributed as dist
-        dist.all_reduce(my, op=dist.ReduceOp.MAX)
-    total_ms = float(my.item())
+    keys = list(parts)
+    red = max_over_ranks([total_ms] + [parts[k] for k in keys], world, dev)
+    total_ms = red[0]
+    parts = dict(zip(keys, red[1:]))
     ms_step = total_ms / args.steps
     value = prob.flops_alg * world / (ms_step * 1e-3) / 1e12
 
@@ -588,13 +603,16 @@ def run_ours(args):
         with open(tf) as f:
             traffic = json.load(f).get(kern)
 
+    if barrier:
+        barrier()
     e2e_ms, h2d, d2h = time_e2e(prob, max(3, args.steps // 2), 2)
+    e2e_ms = max_over_ranks([e2e_ms], world, dev)[0]
     e2e_value = prob.flops_alg * world / (e2e_ms * 1e-3) / 1e12
 
     extras = {}
     if not args.quick:
-        extras["sweep"] = run_sweep(dev, flush, steps=5)
-        extras["decode"] = run_decode(dev, rank, args.steps, args.warmup, flush, peaks)
+        extras["sweep"] = run_sweep(dev, flush, steps=5)  # per GPU (rank 0's numbers)
+        extras["decode"] = run_decode(dev, rank, args.steps, args.warmup, flush, peaks, world, barrier)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
