@@ -559,6 +559,61 @@ def run_decode(dev, seed, steps, warmup, flush, peaks, world=1, barrier=None):
     }
 
 
+C5 = dict(Z=1, H=16, Hkv=8, N=131072, D=128, RB=128, TD=10, t=7)
+
+
+def run_c5(dev, rank, world, steps, warmup, flush, barrier=None):
+    """C5 very long prefill forward: N=131072, H=16/8, D=128, RB=128 (NB=1024), tree routes
+    TD=10, threshold 7, causal + sink (5624 kept blocks per head).  One GPU: the whole
+    sequence.  N GPUs: the sequence sharded contiguously, K/V chunks rotating over NCCL
+    (ultrametric.ring), time = max over ranks."""
+    from ultrametric import build_block_lists
+    from ultrametric.block_list import _fwd
+    from ultrametric.ring import ring_block_list_attention
+    Z, H, Hkv, N, D, RB = (C5[k] for k in ("Z", "H", "Hkv", "N", "D", "RB"))
+    NB = N // RB
+    router = tree_router(Z, H, NB, C5["TD"]).to(dev)
+    bl = build_block_lists(router, C5["t"], is_causal=True, sink_block=True, arity=2)
+    kept = int(bl.counts.sum())
+    Nl = N // world
+    g = torch.Generator(device=dev).manual_seed(40 + rank)  # this rank's chunk of the sequence
+    q = torch.randn(Z, H, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(Z, Hkv, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(Z, Hkv, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
+    scale = 1.0 / math.sqrt(D)
+
+    def one():
+        if world == 1:
+            _fwd(q, k, v, bl.lists, bl.counts, RB, True, scale, True, None)
+        else:
+            ring_block_list_attention(q, k, v, bl, route_block=RB, is_causal=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    tot = 0.0
+    for _ in range(steps):
+        flush_l2(flush)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        one()
+        e1.record()
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    ms = max_over_ranks([tot / steps], world, dev)[0]
+    flops = kept * 4 * RB * RB * D
+    res = {"config": "C5: N=131072, H=16/8, D=128, RB=128, tree routes TD=10, t=7, causal + sink",
+           "kept_blocks": kept, "kept_per_head": kept / H, "ms": round(ms, 4),
+           "kept_tflops": round(flops / (ms * 1e-3) / 1e12, 2)}
+    if world > 1:
+        res["ring"] = {"ranks": world, "rows_per_rank": Nl,
+                       "kv_bytes_per_hop": 2 * Z * Hkv * Nl * D * 2, "hops": world - 1,
+                       "transport": "NCCL send/recv of each rank's K/V chunk (torch.distributed)"}
+    return res
+
+
 def run_ours(args):
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -612,6 +667,7 @@ def run_ours(args):
     extras = {}
     if not args.quick:
         extras["sweep"] = run_sweep(dev, flush, steps=5)  # per GPU (rank 0's numbers)
+        extras["c5"] = run_c5(dev, rank, world, max(3, args.steps // 2), args.warmup, flush, barrier)
         extras["decode"] = run_decode(dev, rank, args.steps, args.warmup, flush, peaks, world, barrier)
     if world > 1:
         import torch.distributed as dist

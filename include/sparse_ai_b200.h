@@ -244,6 +244,23 @@ SA_API int sa_ultrametric_decode_noalloc(int dtype, int64_t B, int64_t H, int64_
                           int64_t TD, int64_t req_depth, int64_t local_blocks, int sink_block,
                           void* out, const int64_t* out_strides, void* stream);
 
+/*
+ * Log-sum-exp merge of partial attention outputs (the combine step of the sequence-sharded
+ * ring for very long prefill; the reference has no ring -- its forward LSE output,
+ * src/ultrametric/block_list.py:467-470, is the hook this uses).  Per row:
+ *   lse_acc' = log(exp(lse_acc) + exp(lse_part))
+ *   o_acc'   = o_acc * exp(lse_acc - lse_acc') + o_part * exp(lse_part - lse_acc')
+ * o_part (Z, H, N, D) of dtype with strides (innermost 1) and lse_part fp32 (Z, H, N): one
+ * partial (normalised output + natural-log LSE, as sa_block_list_attention_fwd writes
+ * them); o_acc fp32 (Z, H, N, D) contiguous and lse_acc fp32 (Z, H, N) accumulate in place
+ * (init != 0: start from this partial).  Rows with -inf LSE contribute nothing.  out
+ * (optional, dtype, strides) receives the merged output after this partial.
+ */
+SA_API int sa_attention_lse_merge(int dtype, int64_t Z, int64_t H, int64_t N, int64_t D,
+                                  const void* o_part, const int64_t* o_part_strides,
+                                  const float* lse_part, float* o_acc, float* lse_acc, int init,
+                                  void* out, const int64_t* out_strides, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,6 +60,8 @@ _SIGNATURES = {
                                              _vp, _p64, _vp, _p64, _vp, _p64, _vp, _p64, _i64,
                                              _vp, _vp, _i32, _p64, _vp, _i32, _p64, _i64, _i64,
                                              _i64, _i32, _vp, _p64, _vp]),
+    "sa_attention_lse_merge": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _p64, _vp, _vp, _vp,
+                                      _i32, _vp, _p64, _vp]),
 }
 
 _lib = None
