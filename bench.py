@@ -569,7 +569,7 @@ def run_c5(dev, rank, world, steps, warmup, flush, barrier=None):
     (ultrametric.ring), time = max over ranks."""
     from ultrametric import build_block_lists
     from ultrametric.block_list import _fwd
-    from ultrametric.ring import ring_block_list_attention
+    from ultrametric.ring import RingPlan, ring_block_list_attention
     Z, H, Hkv, N, D, RB = (C5[k] for k in ("Z", "H", "Hkv", "N", "D", "RB"))
     NB = N // RB
     router = tree_router(Z, H, NB, C5["TD"]).to(dev)
@@ -581,12 +581,14 @@ def run_c5(dev, rank, world, steps, warmup, flush, barrier=None):
     k = torch.randn(Z, Hkv, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
     v = torch.randn(Z, Hkv, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(D)
+    # the ring's schedule depends only on the lists: planned once, like the lists themselves
+    plan = RingPlan(bl, world, rank, Nl, RB, True) if world > 1 else None
 
     def one():
         if world == 1:
             _fwd(q, k, v, bl.lists, bl.counts, RB, True, scale, True, None)
         else:
-            ring_block_list_attention(q, k, v, bl, route_block=RB, is_causal=True)
+            ring_block_list_attention(q, k, v, bl, route_block=RB, is_causal=True, plan=plan)
 
     for _ in range(warmup):
         one()
@@ -608,9 +610,12 @@ def run_c5(dev, rank, world, steps, warmup, flush, barrier=None):
            "kept_blocks": kept, "kept_per_head": kept / H, "ms": round(ms, 4),
            "kept_tflops": round(flops / (ms * 1e-3) / 1e12, 2)}
     if world > 1:
-        res["ring"] = {"ranks": world, "rows_per_rank": Nl,
-                       "kv_bytes_per_hop": 2 * Z * Hkv * Nl * D * 2, "hops": world - 1,
-                       "transport": "NCCL send/recv of each rank's K/V chunk (torch.distributed)"}
+        sent = sum(int(g.numel()) for _, g, _, _ in plan.exchange if g is not None)
+        res["ring"] = {"ranks": world, "rows_per_rank": Nl, "hops_computed": len(plan.hops),
+                       "kv_rows_sent_by_rank0": sent,
+                       "kv_bytes_sent_by_rank0": 2 * Z * Hkv * sent * D * 2,
+                       "dense_ring_bytes_per_hop": 2 * Z * Hkv * Nl * D * 2,
+                       "transport": "NCCL send/recv (torch.distributed) of the referenced K/V blocks only"}
     return res
 
 

@@ -125,6 +125,27 @@ SA_API int sa_block_list_attention_fwd(int dtype, int64_t Z, int64_t H, int64_t 
                                 int is_causal, float sm_scale,
                                 void* workspace, int64_t workspace_bytes, void* stream);
 
+/*
+ * sa_block_list_attention_fwd that continues from a previous result instead of starting
+ * from zero: out and lse hold the normalised output and natural-log LSE of the same rows
+ * over an earlier, disjoint set of keys (e.g. the previous hop of the sequence-sharded
+ * ring), and are updated in place to the result over both key sets -- the online softmax
+ * resumes from that state, so no separate merge pass runs.  Rows with no listed block keep
+ * their values.  No soft bias; tensor-core path only (bf16/fp16, head_dim 64/128,
+ * route_block a multiple of 128, 16-byte aligned rows), else SA_EUNSUPPORTED.  No
+ * counterpart in the reference (it has no sequence parallelism; block_list.py:467-470 is
+ * the LSE this consumes).
+ */
+SA_API int sa_block_list_attention_fwd_accumulate(int dtype, int64_t Z, int64_t H, int64_t Hkv,
+                                                  int64_t N, int64_t D, int64_t route_block,
+                                                  const void* q, const int64_t* q_strides,
+                                                  const void* k, const int64_t* k_strides,
+                                                  const void* v, const int64_t* v_strides,
+                                                  void* out, const int64_t* out_strides, float* lse,
+                                                  const int32_t* lists, int64_t list_stride,
+                                                  const int32_t* counts, int is_causal,
+                                                  float sm_scale, void* stream);
+
 /* Bytes of (optional) workspace for sa_block_list_attention_fwd, on the current device. */
 SA_API int64_t sa_block_list_attention_fwd_workspace_bytes(int64_t Z, int64_t H, int64_t N,
                                                     int64_t D, int64_t route_block);

@@ -46,6 +46,9 @@ class LseMergeCPU:
         self.acc = torch.zeros(Z, H, N, D, dtype=torch.float64)
         self.lse = torch.full((Z, H, N), float("-inf"), dtype=torch.float64)
 
+    def finish(self, out):
+        out.copy_(self.acc.to(out.dtype))
+
     def __call__(self, o, lse, first: bool, out):
         lj = lse.to(torch.float64)
         la = torch.full_like(lj, float("-inf")) if first else self.lse

@@ -96,6 +96,37 @@ int sa_block_list_attention_fwd(int dtype, int64_t Z, int64_t H, int64_t Hkv, in
   return launch_fwd_simt(p, s);
 }
 
+int sa_block_list_attention_fwd_accumulate(int dtype, int64_t Z, int64_t H, int64_t Hkv, int64_t N,
+                                           int64_t D, int64_t route_block, const void* q,
+                                           const int64_t* q_strides, const void* k,
+                                           const int64_t* k_strides, const void* v,
+                                           const int64_t* v_strides, void* out,
+                                           const int64_t* out_strides, float* lse,
+                                           const int32_t* lists, int64_t list_stride,
+                                           const int32_t* counts, int is_causal, float sm_scale,
+                                           void* stream) {
+  using namespace sa;
+  AttnParams p{};
+  int rc = fill_common(p, dtype, Z, H, Hkv, N, D, route_block, q, q_strides, k, k_strides, v,
+                       v_strides, lists, list_stride, counts, nullptr, 0, nullptr, is_causal,
+                       sm_scale);
+  if (rc) return rc;
+  if (!out_strides || out_strides[3] != 1)
+    return fail(SA_EUNSUPPORTED, "out: head_dim must be the contiguous dimension");
+  p.out = out;
+  for (int i = 0; i < 4; ++i) p.os[i] = out_strides[i];
+  p.lse = lse;
+  p.accumulate = 1;
+  if (Z * H * N == 0) return SA_OK;
+  if (!q || !k || !v || !out || !lse || !lists || !counts)
+    return fail(SA_EINVAL, "null pointer argument (accumulate needs out and lse)");
+  rc = launch_fwd_sm100(p, (cudaStream_t)stream);
+  if (rc == SA_EUNSUPPORTED)
+    return fail(SA_EUNSUPPORTED, "accumulating forward: needs the tensor-core path (bf16/fp16, "
+                                 "head_dim 64/128, route_block a multiple of 128, aligned rows)");
+  return rc;
+}
+
 int64_t sa_block_list_attention_fwd_workspace_bytes(int64_t Z, int64_t H, int64_t N, int64_t D,
                                                     int64_t route_block) {
   if (Z <= 0 || H <= 0 || N <= 0 || D <= 0 || route_block <= 0) return 0;

@@ -47,6 +47,7 @@ struct FwdArgs {
   float* lse;
   int causal;
   float scale;
+  int accumulate;  // continue the online softmax from the O / LSE already in out / lse
   unsigned* status;
   SchedArgs sched;
 };
@@ -265,9 +266,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           tc_commit(&bars[B_KEMPTY0 + st]);
           if (t == n_sub - 1) tc_commit(&bars[B_QEMPTY]);
           ++s_it;
-          if (t > 0) ok = issue_pv(kv0 + t - 1, t - 1 == 0);
+          if (t > 0) ok = issue_pv(kv0 + t - 1, t - 1 == 0 && !a.accumulate);
         }
-        if (ok) ok = issue_pv(kv0 + n_sub - 1, n_sub == 1);
+        if (ok) ok = issue_pv(kv0 + n_sub - 1, n_sub == 1 && !a.accumulate);
       }
     }
   } else {
@@ -287,6 +288,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       const int n_sub = e.end - e.begin;
       const int64_t row = it.q_start + rl;
       float m_used = -INFINITY, l_sum = 0.f;
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      T* orow = static_cast<T*>(a.out) + it.z * a.os[0] + it.h * a.os[1] + row * a.os[2];
+      if (a.accumulate && n_sub > 0) {
+        // Seed TMEM O and the softmax state with the previous (normalised) output and its
+        // LSE: with the reference max at the LSE, that output has weight 1 (l = 1).  The
+        // previous item's PV completed before its epilogue read O, so O is free here.
+        const float lp = row < a.N ? a.lse[(it.z * a.H + it.h) * a.N + row] : -INFINITY;
+        if (lp != -INFINITY) {
+          m_used = lp * kLog2e;
+          l_sum = 1.f;
+        }
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w = make_uint4(0, 0, 0, 0);
+            if (lp != -INFINITY) w = *reinterpret_cast<const uint4*>(orow + c * 32 + v * 8);
+            const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[v * 8 + i] = to_f32<T>(e[i]);
+          }
+          tmem_st32(lane_addr + kColO + c * 32, o);
+        }
+        tmem_wait_st();
+      }
       for (int t = 0; t < n_sub && ok; ++t, ++kv) {
         const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
         if (!mbar_wait_warp(&bars[B_SFULL0 + sb], sph, a.status)) { ok = false; break; }
@@ -341,11 +368,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           rs += p0 + p1;
           pk[c / 2] = pack2(p0, p1, BF16);
         }
-        // P buffer and O are free once PV of the previous tile completed
+        // P buffer and O are free once PV of the previous tile completed (a seeded O is
+        // ours from the start)
         if (t > 0) {
           if (!mbar_wait_warp(&bars[B_ODONE], od & 1, a.status)) { ok = false; break; }
           ++od;
           tc_fence_after();
+        }
+        if (t > 0 || a.accumulate) {
           if (__any_sync(0xffffffffu, rescale)) {
             const float f = rescale ? alpha : 1.f;
 #pragma unroll
@@ -385,8 +415,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         tc_fence_after();
         inv = 1.f / (l_sum == 0.f ? 1.f : l_sum);
       }
-      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      T* orow = static_cast<T*>(a.out) + it.z * a.os[0] + it.h * a.os[1] + row * a.os[2];
+      if (a.accumulate && n_sub == 0) continue;  // nothing new: out / lse stay as they are
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float o[32];
@@ -453,6 +482,7 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
   a.lse = p.lse;
   a.causal = p.causal;
   a.scale = p.scale;
+  a.accumulate = p.accumulate;
   a.status = p.status;
   const int64_t items = a.Z * a.H * a.QT;
   const int grid = (int)std::min<int64_t>(items, device_sm_count());

@@ -25,6 +25,7 @@ struct AttnParams {
   int64_t bs[4];
   int causal;
   float scale;
+  int accumulate;  // forward: continue from the output / LSE already in out / lse
   // backward only
   const void* dout;
   int64_t dos[4];

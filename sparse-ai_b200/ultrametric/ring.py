@@ -3,12 +3,12 @@
 The reference has no context parallelism (its forward's LSE output,
 ``src/ultrametric/block_list.py:467-470``, is the hook a ring needs).  Here each of P ranks
 holds a contiguous chunk of ``N/P`` query rows and the matching K/V rows; the global block
-lists are tiny and every rank holds all of them.  In P hops the K/V chunks rotate around
-the ring (rank r sends to r+1 and receives from r-1 into a second buffer; with NCCL the
-transfer runs beside this hop's compute): at hop j rank r attends its queries to chunk
-``c = (r - j) mod P``, restricted to the kept block pairs that fall in that chunk, and
-merges the partial (output, LSE) into an fp32 accumulator by log-sum-exp weights
-(``sa_attention_lse_merge``).
+lists are tiny and every rank holds all of them.  At hop j rank r attends its queries to
+chunk ``c = (r - j) mod P``, restricted to the kept block pairs that fall in that chunk,
+and merges the partial (output, LSE) into an fp32 accumulator by log-sum-exp weights
+(``sa_attention_lse_merge``).  Only the key blocks that rank r's lists reference leave
+rank c (a sparse ring: for tree routes these are few -- the sink block and subtrees that
+straddle a chunk boundary), so the exchange is small next to the compute.
 
 Causality needs no kernel change: the diagonal chunk (c == r) runs causally, earlier
 chunks lie entirely before this rank's queries, and later chunks hold no kept pair of a
@@ -60,6 +60,9 @@ class _CudaMerge:
         self.lse = torch.empty((Z, H, N), dtype=torch.float32, device=q.device)
         self.dtype = q.dtype
 
+    def finish(self, out: torch.Tensor) -> None:
+        out.copy_(self.acc.to(out.dtype))
+
     def __call__(self, o, lse, first: bool, out: Optional[torch.Tensor]):
         Z, H, N, D = o.shape
         nat.check(nat.lib().sa_attention_lse_merge(
@@ -79,59 +82,169 @@ def ring_hops(rank: int, world: int, is_causal: bool) -> list[tuple[int, int, bo
     return hops
 
 
+def reference_masks(lists: torch.Tensor, counts: torch.Tensor, nbl: int, world: int) -> torch.Tensor:
+    """(world, NB) bool: ref[r, kb] = some query block of rank r lists key block kb."""
+    Z, H, NB, mc = lists.shape
+    slot = torch.arange(mc, device=lists.device)
+    valid = slot < counts.long()[..., None]
+    owner = (torch.arange(NB, device=lists.device) // nbl).view(1, 1, NB, 1)
+    flat = torch.where(valid, owner * (NB + 1) + lists.long(), torch.full_like(lists, NB, dtype=torch.long))
+    ref = torch.zeros(world * (NB + 1), dtype=torch.bool, device=lists.device)
+    ref[flat.reshape(-1)] = True
+    return ref.view(world, NB + 1)[:, :NB]
+
+
+class RingPlan:
+    """One rank's ring schedule for one set of block lists, built once (two small host
+    reads) and reused by every call with those lists:
+
+    * ``hops``: (chunk, causal?, chunk-local lists, counts) for the chunks this rank attends;
+    * ``exchange``: per hop j > 0, the rows of this rank's chunk that rank r + j references
+      (sent) and the rows of chunk r - j that this rank references (received)."""
+
+    def __init__(self, block_lists: BlockLists, world: int, rank: int, rows_per_rank: int,
+                 route_block: int, is_causal: bool):
+        if rows_per_rank % route_block:
+            raise ValueError(f"the per-rank chunk ({rows_per_rank} rows) must be a multiple of route_block")
+        nbl = rows_per_rank // route_block
+        lists, counts = block_lists.lists, block_lists.counts
+        if lists.shape[2] != nbl * world:
+            raise ValueError(f"block_lists cover {lists.shape[2]} query blocks, "
+                             f"expected {nbl * world} (= N / route_block)")
+        mc = int(counts.max()) if counts.numel() else 0  # sync-free lists are NB slots wide
+        lists = lists[..., :max(mc, 1)]
+        self.world, self.rank, self.rows, self.route_block = world, rank, rows_per_rank, route_block
+        self.is_causal = is_causal
+        self.hops = []
+        for _, c, causal in ring_hops(rank, world, is_causal):
+            sub, cnt = chunk_lists(lists, counts, rank * nbl, (rank + 1) * nbl, c * nbl, (c + 1) * nbl)
+            self.hops.append((c, causal, sub, cnt))
+        self.exchange = []
+        if world > 1:
+            ref = reference_masks(lists, counts, nbl, world).cpu()
+            dev = lists.device
+            rows = torch.arange(route_block)
+            to_rows = lambda b: (b.view(-1, 1) * route_block + rows).reshape(-1).to(dev)
+            for j in range(1, world):
+                dst, src = (rank + j) % world, (rank - j) % world
+                give = ref[dst, rank * nbl:(rank + 1) * nbl].nonzero().view(-1)
+                need = ref[rank, src * nbl:(src + 1) * nbl].nonzero().view(-1)
+                self.exchange.append((dst, to_rows(give) if give.numel() else None,
+                                      src, to_rows(need) if need.numel() else None))
+
+
+def _fwd_direct(q, k, v, lists, counts, route_block, is_causal, scale, out, lse, accumulate):
+    """The forward into (out, lse), or continuing from them; static schedule (no planner)."""
+    Z, H, N, D = q.shape
+    if accumulate:
+        nat.check(nat.lib().sa_block_list_attention_fwd_accumulate(
+            nat.float_code(q.dtype), Z, H, k.shape[1], N, D, route_block, q.data_ptr(), nat.strides(q),
+            k.data_ptr(), nat.strides(k), v.data_ptr(), nat.strides(v), out.data_ptr(), nat.strides(out),
+            lse.data_ptr(), lists.data_ptr(), lists.shape[-1], counts.data_ptr(), int(bool(is_causal)),
+            float(scale), nat.stream_of(q)), "accumulating forward")
+    else:
+        nat.check(nat.lib().sa_block_list_attention_fwd(
+            nat.float_code(q.dtype), Z, H, k.shape[1], N, D, route_block, q.data_ptr(), nat.strides(q),
+            k.data_ptr(), nat.strides(k), v.data_ptr(), nat.strides(v), out.data_ptr(), nat.strides(out),
+            lse.data_ptr(), lists.data_ptr(), lists.shape[-1], counts.data_ptr(), None, 0, None,
+            int(bool(is_causal)), float(scale), None, 0, nat.stream_of(q)), "forward")
+
+
+def _accumulate_ok(q: torch.Tensor, route_block: int) -> bool:
+    return q.dtype in (torch.bfloat16, torch.float16) and q.shape[-1] in (64, 128) and route_block % 128 == 0
+
+
 def ring_block_list_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                               block_lists: BlockLists, *, route_block: int = 128,
                               is_causal: bool = False, sm_scale: Optional[float] = None,
-                              group=None, attn: Optional[Callable] = None,
+                              group=None, plan: Optional[RingPlan] = None,
+                              attn: Optional[Callable] = None,
                               merge_factory: Optional[Callable] = None,
                               ) -> tuple[torch.Tensor, torch.Tensor]:
     """Block-list attention forward over a sequence split across the ranks of ``group``.
 
     q: (Z, H, N/P, D) this rank's query rows (chunk ``rank``); k, v: (Z, Hkv, N/P, D) the
     matching K/V rows; ``block_lists``: the global lists for all N/route_block query
-    blocks.  N/P must be a multiple of ``route_block``.  Returns this rank's (out, lse)."""
+    blocks.  N/P must be a multiple of ``route_block``.  ``plan``: a ``RingPlan`` built
+    once for these lists (else one is built here).  Returns this rank's (out, lse).
+
+    Hop j pairs rank r with ranks r - j (whose chunk it attends) and r + j (which attends
+    r's chunk).  Only the key blocks that the receiver's lists reference cross the link --
+    all ranks hold the global lists, so sender and receiver agree on them without asking:
+    they are gathered into one buffer, exchanged with send/recv (all hops' exchanges are
+    posted at once and run beside the diagonal hop's compute), and put back at their rows
+    of a chunk-sized buffer that the kernel reads through the hop's lists (rows it does not
+    list are never read).  Hops after the first continue the forward from the previous
+    output and LSE in place (``sa_block_list_attention_fwd_accumulate``); shapes outside
+    the tensor-core path, and injected ``attn`` / ``merge_factory``, merge partials
+    instead."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     Z, H, Nl, D = q.shape
+    Hkv = k.shape[1]
     if k.shape != v.shape or k.shape[0] != Z or k.shape[2] != Nl or k.shape[3] != D:
         raise ValueError("k and v must be (Z, Hkv, N/P, D) chunks matching q")
-    if Nl % route_block:
-        raise ValueError(f"the per-rank chunk ({Nl} rows) must be a multiple of route_block")
-    nbl = Nl // route_block
-    if block_lists.lists.shape[2] != nbl * world:
-        raise ValueError(f"block_lists cover {block_lists.lists.shape[2]} query blocks, "
-                         f"expected {nbl * world} (= N / route_block)")
+    if plan is None:
+        plan = RingPlan(block_lists, world, rank, Nl, route_block, is_causal)
+    elif (plan.world, plan.rank, plan.rows, plan.route_block, plan.is_causal) != (
+            world, rank, Nl, route_block, is_causal):
+        raise ValueError("plan was built for another ring layout")
     scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(D)
-    attn = attn or _attn_cuda
-    merge = (merge_factory or _CudaMerge)(q)
-    hops = ring_hops(rank, world, is_causal)
-    last_j = hops[-1][0]
+    accumulate = attn is None and merge_factory is None and _accumulate_ok(q, route_block)
     out = torch.empty_like(q)
+    lse = torch.empty((Z, H, Nl), dtype=torch.float32, device=q.device)
+    merge = None if accumulate else (merge_factory or _CudaMerge)(q)
+    attn = attn or _attn_cuda
 
-    kv = torch.stack([k, v]).contiguous()
-    nxt = torch.empty_like(kv)
+    recv, ops = {}, []
+    for dst, give, src, need in plan.exchange:
+        if give is not None:
+            send = torch.stack([k.index_select(2, give), v.index_select(2, give)])
+            ops.append(dist.P2POp(dist.isend, send, dst, group))
+        if need is not None:
+            buf = torch.empty((2, Z, Hkv, need.numel(), D), dtype=k.dtype, device=q.device)
+            ops.append(dist.P2POp(dist.irecv, buf, src, group))
+            recv[src] = (need, buf)
+    reqs = dist.batch_isend_irecv(ops) if ops else []
+
     first = True
-    for j in range(world):
-        reqs = []
-        if j < world - 1:  # rotate: send this chunk on, receive the next one
-            ops = [dist.P2POp(dist.isend, kv, (rank + 1) % world, group),
-                   dist.P2POp(dist.irecv, nxt, (rank - 1) % world, group)]
-            reqs = dist.batch_isend_irecv(ops)
-        hop = next((h for h in hops if h[0] == j), None)
-        if hop is not None:
-            _, c, causal = hop
-            sub, cnt = chunk_lists(block_lists.lists, block_lists.counts, rank * nbl,
-                                   (rank + 1) * nbl, c * nbl, (c + 1) * nbl)
-            o_j, lse_j = attn(q, kv[0], kv[1], sub, cnt, route_block, causal, scale)
-            merge(o_j, lse_j, first, out if j == last_j else None)
-            first = False
-        for rq in reqs:
-            rq.wait()
-        if j < world - 1:
-            kv, nxt = nxt, kv
-    return out, merge.lse
+    chunk_k = chunk_v = None
+    n_hops = len(plan.hops)
+    for i, (c, causal, sub, cnt) in enumerate(plan.hops):
+        last = i == n_hops - 1
+        if c == rank:
+            kc, vc = k, v
+        elif c not in recv:  # none of this rank's lists reaches chunk c
+            if last and merge is not None and not first:
+                merge.finish(out)
+            continue
+        else:
+            for rq in reqs:
+                rq.wait()
+            reqs = []
+            need, buf = recv[c]
+            if chunk_k is None:  # the kernel reads only listed rows; a dense stand-in reads all
+                alloc = torch.empty_like if accumulate else torch.zeros_like
+                chunk_k, chunk_v = alloc(k), alloc(v)
+            chunk_k.index_copy_(2, need, buf[0])
+            chunk_v.index_copy_(2, need, buf[1])
+            kc, vc = chunk_k, chunk_v
+        if accumulate:
+            _fwd_direct(q, kc, vc, sub, cnt, route_block, causal, scale, out, lse, not first)
+        else:
+            o_j, lse_j = attn(q, kc, vc, sub, cnt, route_block, causal, scale)
+            merge(o_j, lse_j, first, out if last else None)
+        first = False
+    for rq in reqs:
+        rq.wait()
+    if merge is not None:
+        lse = merge.lse
+    if first:  # no hop attended anything (empty lists): zero rows, -inf LSE
+        out.zero_()
+        lse.fill_(float("-inf"))
+    return out, lse
 
 
 def ring_emulate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_lists: BlockLists,
@@ -150,15 +263,20 @@ def ring_emulate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_lists:
     for rank in range(world):
         rows = slice(rank * Nl, (rank + 1) * Nl)
         qr = q[:, :, rows]
-        merge = _CudaMerge(qr)
+        acc = _accumulate_ok(qr, route_block)
+        merge = None if acc else _CudaMerge(qr)
         out = torch.empty_like(qr)
+        lse = torch.empty(qr.shape[:3], dtype=torch.float32, device=q.device)
         hops = ring_hops(rank, world, is_causal)
         for i, (_, c, causal) in enumerate(hops):
             kr, vr = k[:, :, c * Nl:(c + 1) * Nl], v[:, :, c * Nl:(c + 1) * Nl]
             sub, cnt = chunk_lists(block_lists.lists, block_lists.counts, rank * nbl,
                                    (rank + 1) * nbl, c * nbl, (c + 1) * nbl)
-            o_j, lse_j = _attn_cuda(qr, kr, vr, sub, cnt, route_block, causal, scale)
-            merge(o_j, lse_j, i == 0, out if i == len(hops) - 1 else None)
+            if acc:
+                _fwd_direct(qr, kr, vr, sub, cnt, route_block, causal, scale, out, lse, i > 0)
+            else:
+                o_j, lse_j = _attn_cuda(qr, kr, vr, sub, cnt, route_block, causal, scale)
+                merge(o_j, lse_j, i == 0, out if i == len(hops) - 1 else None)
         outs.append(out)
-        lses.append(merge.lse)
+        lses.append(lse if acc else merge.lse)
     return torch.cat(outs, dim=2), torch.cat(lses, dim=2)
