@@ -53,7 +53,9 @@ SA_API const char* sa_last_error(void);
 SA_API int sa_abi_version(void);
 
 /* Read the current device's status word (synchronises the device).  Kernels OR in
- * 1 when a bounded wait gave up, 2 on an out-of-range index; reset != 0 clears it. */
+ * 1 when a bounded wait gave up, 2 on an out-of-range index, 4 when a kernel found its
+ * dynamic shared memory too small for its aligned layout (it then does nothing);
+ * reset != 0 clears it. */
 SA_API int sa_read_device_status(int reset, unsigned* value);
 
 /*

@@ -4,18 +4,30 @@
 // query block's own list, token-level causal and tail masks, exp2 online softmax, empty rows
 // -> 0 / lse -inf, natural-log LSE, optional per-(row block, slot) logit bias).
 //
-// Persistent kernel, one CTA per SM, 6 warps:
-//   warp 0      TMA producer: Q tile once per work item, K/V tiles of each listed key block
-//               into a 2-stage ring (128 x D bf16/fp16 tiles, 128-byte swizzle).
-//   warp 1      TMEM owner + single-thread tcgen05.mma issuer:
-//                 S[t%2] = Q K_t^T   (M=128, N=128, K=D; fp32 in TMEM)
-//                 O     += P_{t} V_t (M=128, N=D,   K=128; fp32 in TMEM)
-//               QK of tile t+1 is issued before PV of tile t so the tensor core works while
-//               the softmax warps process S_t.
-//   warps 2-5   softmax: thread = query row (TMEM lane); tcgen05.ld of S, masking, row max,
-//               exp2, P (bf16/fp16) written to shared memory in the MMA's swizzled K-major
-//               layout; O rescaled in TMEM only when the row max grows by more than 2^8
-//               (lazy rescale); epilogue O / l -> global, LSE.
+// Persistent kernel, one CTA per SM, 12 warps (softmax warpgroups raised to 224 registers with
+// setmaxnreg, the control warpgroup lowered to 56):
+//   warp 10     scheduler: takes work entries (queue atomic or round-robin), computes each
+//               item's indices once, reads its list 32 entries per coalesced warp load and
+//               pushes one key start (+ soft bias) per key tile into an 8-slot shared ring,
+//               prefetching the Q tile and every K/V tile into L2 as it goes.
+//   warp 8      TMA producer: Q tile once per work item, K tiles into a 2-stage ring and V
+//               tiles into another, V running two tiles behind K (the order in which the MMA
+//               frees the stages); it never touches global memory itself.
+//   warp 9      TMEM owner + single-thread tcgen05.mma issuer:
+//                 S[g] = Q K_t^T    (M=128, N=128, K=D; fp32 in TMEM), g = t & 1
+//                 O[g] += P_t V_t   (M=128, N=D,   K=128; fp32 in TMEM)
+//               Tiles go in pairs (one per group): the QKs of pair p+1 are issued before the PVs
+//               of pair p, so each group finds its next S computed when it finishes a tile, and
+//               the two groups run the same code at the same time (one instruction-cache
+//               footprint).
+//   warps 0-7   two softmax groups of 4 warps; group g takes the key tiles t = g, g+2, ... of
+//               the work item with its own running max / sum and its own O[g].  Thread = query
+//               row (TMEM lane); tcgen05.ld of S, masking, row max, exp2, P (bf16/fp16) into the
+//               group's shared-memory P buffer in the MMA's swizzled K-major layout; O[g]
+//               rescaled in TMEM only when the row max grows by more than 2^8 (lazy rescale).
+//               Epilogue: the groups swap (max, sum) per row through shared memory and each
+//               merges O[0] and O[1] for half of the head dim, O / l -> global, LSE.
+//   warp 11     idle (it completes the control warpgroup for setmaxnreg).
 // Work item = (query tile of 128 rows, z, h).  With a planner workspace the items come
 // heaviest-first from the device-built queue (one atomic per item); without one, round-robin
 // with late (heavier, under causal masking) query tiles first.
@@ -28,13 +40,23 @@ namespace sa {
 namespace {
 
 constexpr int kT = 128;           // rows of a query tile and of a key tile
-constexpr int kFwdThreads = 192;  // 6 warps
+constexpr int kFwdThreads = 384;  // 12 warps
+constexpr int kProducerWarp = 8, kMmaWarp = 9, kSchedWarp = 10;
+// Register split: the launch gives every thread kLaunchRegs; the control warpgroup (warps
+// 8-11) drops to kCtrlRegs and the two softmax warpgroups take what it frees.
+constexpr int kLaunchRegs = 168, kCtrlRegs = 56, kSoftmaxRegs = 224;
+static_assert(4 * 32 * kCtrlRegs + 8 * 32 * kSoftmaxRegs <= kFwdThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
+constexpr int kGroupThreads = 128;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr uint32_t kColS = 0;    // S[g] at kColS + g * kT
+constexpr uint32_t kColO = 256;  // O[g] at kColO + g * D
+constexpr int kKeyRing = 8;  // key tiles the scheduler may run ahead of the V loads
+constexpr uint32_t kMaxSmem = 232448;      // opt-in dynamic shared memory per block
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct FwdArgs {
-  CUtensorMap tm_q, tm_k, tm_v;
+  CUtensorMap tm_q, tm_k, tm_v, tm_o;
   int64_t Z, H, Hkv, N, RB, NB, QT;
   const int32_t* lists;
   int64_t list_stride;
@@ -52,29 +74,44 @@ struct FwdArgs {
   SchedArgs sched;
 };
 
+// barrier slots
+enum {
+  B_QFULL = 0, B_QEMPTY,
+  B_KFULL0, B_KEMPTY0 = B_KFULL0 + 2, B_VFULL0 = B_KEMPTY0 + 2, B_VEMPTY0 = B_VFULL0 + 2,
+  B_SFULL0 = B_VEMPTY0 + 2, B_SEMPTY0 = B_SFULL0 + 2, B_PFULL0 = B_SEMPTY0 + 2,
+  B_ODONE0 = B_PFULL0 + 2, B_XCH = B_ODONE0 + 2, B_EPI,
+  B_OFULL0, B_ODRAIN0 = B_OFULL0 + 2, B_KEYFULL0 = B_ODRAIN0 + 2,
+  B_KEYEMPTY0 = B_KEYFULL0 + kKeyRing,
+  B_WFULL0 = B_KEYEMPTY0 + kKeyRing, B_WEMPTY0 = B_WFULL0 + kRing, B_NUM = B_WEMPTY0 + kRing
+};
+
 template <int D>
 struct FwdLayout {
   static constexpr uint32_t kTileBytes = kT * D * 2;  // one 128 x D half-precision tile
+  static constexpr uint32_t kPBytes = kT * kT * 2;    // one 128 x 128 P tile
   static constexpr uint32_t kQ = 0;
   static constexpr uint32_t kK0 = kQ + kTileBytes;
   static constexpr uint32_t kV0 = kK0 + 2 * kTileBytes;
-  static constexpr uint32_t kP = kV0 + 2 * kTileBytes;
-  static constexpr uint32_t kBars = kP + kT * kT * 2;
-  static constexpr uint32_t kMeta = kBars + 256;  // TileMeta[2]
-  static constexpr uint32_t kRingOff = kMeta + 64;  // WorkEntry[kRing]
-  static constexpr uint32_t kBytes = kRingOff + 128;
-  static constexpr uint32_t kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+  static constexpr uint32_t kP0 = kV0 + 2 * kTileBytes;  // P[2], one per softmax group
+  static constexpr uint32_t kBars = kP0 + 2 * kPBytes;
+  static constexpr uint32_t kKeys = kBars + 384;              // TileKey[kKeyRing]
+  static constexpr uint32_t kRingOff = kKeys + kKeyRing * 16;  // WorkEntry[kRing]
+  static constexpr uint32_t kPos = kRingOff + 64;               // ItemPos[kRing]
+  static constexpr uint32_t kML = kPos + 64;                    // float2 [2][kT]: (max, sum)
+  static constexpr uint32_t kTmemSlot = kML + 2 * kT * 8;
+  static constexpr uint32_t kBytes = kTmemSlot + 16;
+  // up to 1024 bytes of slack for aligning the tiles, as far as the opt-in limit allows; the
+  // kernel checks the padding it needs against %dynamic_smem_size
+  static constexpr uint32_t kAlloc = kBytes + 1024 <= kMaxSmem ? kBytes + 1024 : kMaxSmem;
+  static_assert(kBytes <= kMaxSmem, "forward shared-memory layout too large");
+  static_assert(B_NUM * 8 <= 384, "barrier area too small");
+  static_assert(kRing * 16 <= 64, "work ring area too small");
 };
 
-// barrier slots
-enum { B_QFULL = 0, B_QEMPTY, B_KFULL0, B_KFULL1, B_KEMPTY0, B_KEMPTY1, B_VFULL0, B_VFULL1,
-       B_VEMPTY0, B_VEMPTY1, B_SFULL0, B_SFULL1, B_SEMPTY0, B_SEMPTY1, B_PFULL, B_ODONE,
-       B_WFULL0, B_WEMPTY0 = B_WFULL0 + kRing, B_NUM = B_WEMPTY0 + kRing };
-
-// Per K/V stage: what the producer learned from the lists, handed to the softmax warps
-// through shared memory (released by the stage's V mbarrier) so that no consumer reads
-// the lists from global memory on its critical path.
-struct TileMeta {
+// Per key tile: what the scheduler read from the lists, handed to the producer (K and V loads)
+// and to the owning softmax group (masking, bias) through a shared-memory ring, so that
+// neither reads the lists from global memory on its critical path.
+struct TileKey {
   int64_t key_start;
   float b2;  // soft-bias * log2(e) of the block pair
   int pad;
@@ -82,6 +119,12 @@ struct TileMeta {
 
 struct ItemInfo {
   int64_t z, h, hk, q_start, qb, row_id;
+};
+
+// What the softmax groups need of a work item, computed once by the producer beside the work
+// entry (no 64-bit index division on the groups' path between items).
+struct ItemPos {
+  int z, h, hk, q_start;
 };
 
 __device__ __forceinline__ ItemInfo item_info(const FwdArgs& a, int64_t item) {
@@ -104,12 +147,6 @@ __device__ __forceinline__ int item_tiles(const FwdArgs& a, int64_t item) {
   return a.counts[it.row_id] * (int)(a.RB / kT);
 }
 
-__device__ __forceinline__ int64_t key_start_of(const FwdArgs& a, const ItemInfo& it, int t) {
-  const int spb = (int)(a.RB / kT);
-  const int64_t kb = a.lists[it.row_id * a.list_stride + t / spb];
-  return kb * a.RB + (int64_t)(t % spb) * kT;
-}
-
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
   uint32_t r;
   if (bf16)
@@ -122,13 +159,25 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_constant__ FwdArgs a) {
   using L = FwdLayout<D>;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
+  {
+    const uint32_t base = smem_u32(smem_raw);
+    uint32_t dyn;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    if ((((base + 1023u) & ~1023u) - base) + L::kBytes > dyn) {  // uniform over the CTA
+      if (threadIdx.x == 0) raise_status(a.status, kStatusSmemLayout);
+      return;
+    }
+  }
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
-  TileMeta* meta = reinterpret_cast<TileMeta*>(sm + L::kMeta);  // [2], one per K/V stage
+  TileKey* keys = reinterpret_cast<TileKey*>(sm + L::kKeys);
   WorkEntry* ring = reinterpret_cast<WorkEntry*>(sm + L::kRingOff);
-  __shared__ uint32_t s_tmem_base;
+  ItemPos* pos = reinterpret_cast<ItemPos*>(sm + L::kPos);
+  float2* s_ml = reinterpret_cast<float2*>(sm + L::kML);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::kTmemSlot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -141,101 +190,195 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       mbar_init(&bars[B_VFULL0 + i], 1);
       mbar_init(&bars[B_VEMPTY0 + i], 1);
       mbar_init(&bars[B_SFULL0 + i], 1);
-      mbar_init(&bars[B_SEMPTY0 + i], 128);
+      mbar_init(&bars[B_SEMPTY0 + i], kGroupThreads);
+      mbar_init(&bars[B_PFULL0 + i], kGroupThreads);
+      mbar_init(&bars[B_ODONE0 + i], 1);
     }
-    mbar_init(&bars[B_PFULL], 128);
-    mbar_init(&bars[B_ODONE], 1);
+    mbar_init(&bars[B_XCH], 2 * kGroupThreads);
+    mbar_init(&bars[B_EPI], 2 * kGroupThreads);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[B_OFULL0 + i], kGroupThreads);  // output rows staged for the TMA store
+      mbar_init(&bars[B_ODRAIN0 + i], 1);             // that store has read its staging buffer
+    }
+    for (int i = 0; i < kKeyRing; ++i) {
+      mbar_init(&bars[B_KEYFULL0 + i], 1);
+      mbar_init(&bars[B_KEYEMPTY0 + i], 1 + kGroupThreads);  // the producer (after V), the owning group
+    }
     for (int i = 0; i < kRing; ++i) {
       mbar_init(&bars[B_WFULL0 + i], 1);
-      mbar_init(&bars[B_WEMPTY0 + i], 1 + 128);  // the MMA thread and the softmax threads
+      mbar_init(&bars[B_WEMPTY0 + i], 2 + 2 * kGroupThreads);  // producer, MMA thread, both groups
     }
     fence_mbar_init();
   }
-  if (warp == 1) {
-    tmem_alloc(&s_tmem_base, kTmemCols);
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = s_tmem_base;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  const uint32_t tmem = *tmem_slot;
+  if (warp >= kProducerWarp) {
+    // control warpgroup: the whole warpgroup lowers its registers, then warps 8 / 9 work
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtrlRegs));
+  if (warp == kSchedWarp) {
+    // ------------------------------------------------------------------ scheduler
     if (lane == 0) {
       prefetch_tmap(&a.tm_q);
       prefetch_tmap(&a.tm_k);
       prefetch_tmap(&a.tm_v);
+    }
+    auto weight = [&](int64_t i) { return item_tiles(a, i); };
+    WorkFetcher fetch;
+    if (lane == 0) fetch.init(&a.sched, weight);
+    const int spb = (int)(a.RB / kT);  // key tiles per list entry
+    uint32_t kq = 0;                   // key tiles pushed
+    bool ok = true;
+    for (uint32_t w = 0; ok; ++w) {
+      WorkEntry e{};
+      if (lane == 0) e = fetch.next(weight);
+      e.item = __shfl_sync(0xffffffffu, e.item, 0);
+      e.begin = __shfl_sync(0xffffffffu, e.begin, 0);
+      e.end = __shfl_sync(0xffffffffu, e.end, 0);
+      e.slot = __shfl_sync(0xffffffffu, e.slot, 0);
+      ItemInfo it{};
+      if (e.item >= 0) it = item_info(a, e.item);
+      if (lane == 0) {
+        const uint32_t slot = w % kRing;
+        ok = mbar_wait(&bars[B_WEMPTY0 + slot], ((w / kRing) & 1) ^ 1, a.status);
+        if (ok) {
+          ring[slot] = e;
+          pos[slot] = ItemPos{(int)it.z, (int)it.h, (int)it.hk, (int)it.q_start};
+          mbar_arrive(&bars[B_WFULL0 + slot]);
+          if (e.item >= 0 && e.end > e.begin)
+            for (int c = 0; c < D / 64; ++c)
+              tma_prefetch_4d(&a.tm_q, c * 64, (int)it.q_start, (int)it.h, (int)it.z);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok || e.item < 0) break;
+      // list entries [p0, p1) cover the entry's key tiles; one coalesced load per 32
+      const int p0 = e.begin / spb, p1 = e.end > e.begin ? (e.end - 1) / spb + 1 : p0;
+      for (int pc = p0; pc < p1 && ok; pc += 32) {
+        const int p = pc + lane;
+        int kb = 0;
+        float bb = 0.f;
+        if (p < p1) {
+          kb = a.lists[it.row_id * a.list_stride + p];
+          if (a.bias)
+            bb = load_any_f32(a.bias, a.bias_dtype,
+                              it.z * a.bs[0] + it.h * a.bs[1] + it.qb * a.bs[2] + (int64_t)p * a.bs[3]) *
+                 kLog2e;
+        }
+        const int t_lo = max(e.begin, pc * spb), t_hi = min(e.end, (pc + 32) * spb);
+        for (int t = t_lo; t < t_hi; ++t) {
+          const int src = t / spb - pc;
+          const int64_t ks = (int64_t)__shfl_sync(0xffffffffu, kb, src) * a.RB + (int64_t)(t % spb) * kT;
+          const float b2 = __shfl_sync(0xffffffffu, bb, src);
+          if (lane == 0) {
+            const uint32_t slot = kq % kKeyRing;
+            ok = mbar_wait(&bars[B_KEYEMPTY0 + slot], ((kq / kKeyRing) & 1) ^ 1, a.status);
+            if (ok) {
+              keys[slot] = TileKey{ks, b2, 0};
+              mbar_arrive(&bars[B_KEYFULL0 + slot]);
+              for (int c = 0; c < D / 64; ++c) {
+                tma_prefetch_4d(&a.tm_k, c * 64, (int)ks, (int)it.hk, (int)it.z);
+                tma_prefetch_4d(&a.tm_v, c * 64, (int)ks, (int)it.hk, (int)it.z);
+              }
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          ++kq;
+        }
+      }
+    }
+  } else if (warp == kProducerWarp) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
       uint32_t kv = 0, jq = 0;
       bool ok = true;
-      auto weight = [&](int64_t i) { return item_tiles(a, i); };
-      WorkFetcher fetch;
-      fetch.init(&a.sched, weight);
       for (uint32_t w = 0; ok; ++w) {
-        const WorkEntry e = fetch.next(weight);
-        if (!(ok = ring_put(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
-        if (e.item < 0) break;
-        const ItemInfo it = item_info(a, e.item);
-        if (e.end == e.begin) {
-          fetch.reserve(weight);
-          continue;
+        WorkEntry e;
+        ItemPos ip;
+        {
+          const uint32_t slot = w % kRing;
+          if (!(ok = mbar_wait(&bars[B_WFULL0 + slot], (w / kRing) & 1, a.status))) break;
+          e = ring[slot];
+          ip = pos[slot];
+          mbar_arrive(&bars[B_WEMPTY0 + slot]);
         }
+        if (e.item < 0) break;
+        const int n = e.end - e.begin;
+        if (n == 0) continue;
         ok = mbar_wait(&bars[B_QEMPTY], (jq & 1) ^ 1, a.status);
         if (!ok) break;
         mbar_arrive_expect_tx(&bars[B_QFULL], L::kTileBytes);
         for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sm + L::kQ + c * kT * 128, &a.tm_q, &bars[B_QFULL], c * 64,
-                      (int)it.q_start, (int)it.h, (int)it.z);
+          tma_load_4d(sm + L::kQ + c * kT * 128, &a.tm_q, &bars[B_QFULL], c * 64, ip.q_start, ip.h,
+                      ip.z);
         ++jq;
-        for (int t = e.begin; t < e.end && ok; ++t, ++kv) {
-          const int64_t ks = key_start_of(a, it, t);
-          const uint32_t st = kv & 1, ph = (kv >> 1) & 1;
-          ok = mbar_wait(&bars[B_KEMPTY0 + st], ph ^ 1, a.status);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&bars[B_KFULL0 + st], L::kTileBytes);
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_4d(sm + L::kK0 + st * L::kTileBytes + c * kT * 128, &a.tm_k,
-                        &bars[B_KFULL0 + st], c * 64, (int)ks, (int)it.hk, (int)it.z);
-          ok = mbar_wait(&bars[B_VEMPTY0 + st], ph ^ 1, a.status);
-          if (!ok) break;
-          meta[st].key_start = ks;
-          meta[st].b2 = a.bias ? load_any_f32(a.bias, a.bias_dtype,
-                                              it.z * a.bs[0] + it.h * a.bs[1] + it.qb * a.bs[2] +
-                                                  (t / (int)(a.RB / kT)) * a.bs[3]) *
-                                     kLog2e
-                               : 0.f;
-          mbar_arrive_expect_tx(&bars[B_VFULL0 + st], L::kTileBytes);
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_4d(sm + L::kV0 + st * L::kTileBytes + c * kT * 128, &a.tm_v,
-                        &bars[B_VFULL0 + st], c * 64, (int)ks, (int)it.hk, (int)it.z);
-          if (t == e.end - 1) fetch.reserve(weight);
+        // step i: K of tile i, then V of tile i - 2 (whose key slot it then releases)
+        for (int i = 0; i < n + 2 && ok; ++i) {
+          if (i < n) {
+            const uint32_t u = kv + i, ks_slot = u % kKeyRing;
+            ok = mbar_wait(&bars[B_KEYFULL0 + ks_slot], (u / kKeyRing) & 1, a.status);
+            if (!ok) break;
+            const int ks = (int)keys[ks_slot].key_start;
+            const uint32_t st = u & 1, ph = (u >> 1) & 1;
+            ok = mbar_wait(&bars[B_KEMPTY0 + st], ph ^ 1, a.status);
+            if (!ok) break;
+            mbar_arrive_expect_tx(&bars[B_KFULL0 + st], L::kTileBytes);
+            for (int c = 0; c < D / 64; ++c)
+              tma_load_4d(sm + L::kK0 + st * L::kTileBytes + c * kT * 128, &a.tm_k,
+                          &bars[B_KFULL0 + st], c * 64, ks, ip.hk, ip.z);
+          }
+          if (i >= 2) {
+            const uint32_t u = kv + i - 2, ks_slot = u % kKeyRing, st = u & 1, ph = (u >> 1) & 1;
+            const int ks = (int)keys[ks_slot].key_start;
+            ok = mbar_wait(&bars[B_VEMPTY0 + st], ph ^ 1, a.status);
+            if (!ok) break;
+            mbar_arrive_expect_tx(&bars[B_VFULL0 + st], L::kTileBytes);
+            for (int c = 0; c < D / 64; ++c)
+              tma_load_4d(sm + L::kV0 + st * L::kTileBytes + c * kT * 128, &a.tm_v,
+                          &bars[B_VFULL0 + st], c * 64, ks, ip.hk, ip.z);
+            mbar_arrive(&bars[B_KEYEMPTY0 + ks_slot]);
+          }
         }
+        kv += n;
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(kT, kT, BF16, false, false);
       constexpr uint32_t idesc_pv = idesc_f16(kT, D, BF16, false, true);
       const uint32_t q_addr = smem_u32(sm + L::kQ);
-      const uint32_t p_addr = smem_u32(sm + L::kP);
-      uint32_t kv = 0, s_it = 0, pv = 0, jq = 0;
+      uint32_t kv = 0, jq = 0, nitem = 0;
+      uint32_t sq[2] = {0, 0}, pv[2] = {0, 0};
       bool ok = true;
-      auto issue_pv = [&](uint32_t kv_u, bool first) -> bool {
-        const uint32_t st = kv_u & 1, ph = (kv_u >> 1) & 1;
-        if (!mbar_wait(&bars[B_PFULL], pv & 1, a.status)) return false;
+      // PV of tile u (item-local index t) into O[t & 1]; the item's first PV waits until both
+      // groups have read O[0] / O[1] for the previous item's epilogue.
+      auto issue_pv = [&](uint32_t u, int t) -> bool {
+        const int g = t & 1;
+        const uint32_t st = u & 1, ph = (u >> 1) & 1;
+        if (t == 0 && nitem > 0 && !mbar_wait(&bars[B_EPI], (nitem - 1) & 1, a.status)) return false;
+        if (!mbar_wait(&bars[B_PFULL0 + g], pv[g] & 1, a.status)) return false;
         if (!mbar_wait(&bars[B_VFULL0 + st], ph, a.status)) return false;
         tc_fence_after();
+        const uint32_t p_addr = smem_u32(sm + L::kP0 + g * L::kPBytes);
         const uint32_t v_addr = smem_u32(sm + L::kV0 + st * L::kTileBytes);
+        // the group's first PV of the item starts O[g] afresh, except a seeded O[0]
+        const bool first = t < 2 && !(a.accumulate && g == 0);
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk) {
           const uint64_t ad = smem_desc(p_addr + (kk >> 2) * (kT * 128) + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = smem_desc(v_addr + kk * 16 * 128, kT * 128, 1024);
-          tc_mma_f16(tmem + kColO, ad, bd, idesc_pv, (!first || kk > 0) ? 1u : 0u);
+          tc_mma_f16(tmem + kColO + g * D, ad, bd, idesc_pv, (!first || kk > 0) ? 1u : 0u);
         }
-        tc_commit(&bars[B_ODONE]);
+        tc_commit(&bars[B_ODONE0 + g]);
         tc_commit(&bars[B_VEMPTY0 + st]);
-        ++pv;
+        ++pv[g];
         return true;
       };
       for (uint32_t w = 0; ok; ++w) {
@@ -247,54 +390,102 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         ok = mbar_wait(&bars[B_QFULL], jq & 1, a.status);
         ++jq;
         if (!ok) break;
-        const uint32_t kv0 = kv;
-        for (int t = 0; t < n_sub && ok; ++t, ++kv) {
-          const uint32_t st = kv & 1, ph = (kv >> 1) & 1;
-          const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
+        int pv_next = 0;
+        for (int t = 0; t < n_sub && ok; ++t) {
+          const uint32_t u = kv + t, g = t & 1;
+          const uint32_t st = u & 1, ph = (u >> 1) & 1;
           ok = mbar_wait(&bars[B_KFULL0 + st], ph, a.status) &&
-               mbar_wait(&bars[B_SEMPTY0 + sb], sph ^ 1, a.status);
+               mbar_wait(&bars[B_SEMPTY0 + g], (sq[g] & 1) ^ 1, a.status);
           if (!ok) break;
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sm + L::kK0 + st * L::kTileBytes);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
-            tc_mma_f16(tmem + (sb ? kColS1 : kColS0), smem_desc(q_addr + off, 16, 1024),
+            tc_mma_f16(tmem + kColS + g * kT, smem_desc(q_addr + off, 16, 1024),
                        smem_desc(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
           }
-          tc_commit(&bars[B_SFULL0 + sb]);
+          tc_commit(&bars[B_SFULL0 + g]);
           tc_commit(&bars[B_KEMPTY0 + st]);
           if (t == n_sub - 1) tc_commit(&bars[B_QEMPTY]);
-          ++s_it;
-          if (t > 0) ok = issue_pv(kv0 + t - 1, t - 1 == 0 && !a.accumulate);
+          ++sq[g];
+          // after the QKs of pair (t-1, t): the PVs of the previous pair, so that both groups
+          // run the same code in step (one instruction-cache footprint) and find the next S ready
+          if (t & 1)
+            for (; pv_next <= t - 2 && ok; ++pv_next) ok = issue_pv(kv + pv_next, pv_next);
         }
-        if (ok) ok = issue_pv(kv0 + n_sub - 1, n_sub == 1 && !a.accumulate);
+        for (; pv_next < n_sub && ok; ++pv_next) ok = issue_pv(kv + pv_next, pv_next);
+        kv += n_sub;
+        ++nitem;
       }
     }
+  }
   } else {
-    // ------------------------------------------------------------------ softmax warps
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    // ------------------------------------------------------------------ softmax groups
+    const int grp = warp >> 2;
     const int quarter = warp & 3;
     const int rl = quarter * 32 + lane;  // row within the tile == TMEM lane
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t col_s = kColS + grp * kT;
+    const uint32_t col_o = kColO + grp * D, col_oo = kColO + (grp ^ 1) * D;
     const float scale2 = a.scale * kLog2e;
-    unsigned char* p_tile = sm + L::kP;
-    uint32_t s_it = 0, od = 0, kv = 0;
+    const bool neg_scale = scale2 < 0.f;
+    // |scale| (a sign flip of the scores handles a negative one); a zero scale becomes 1e-30,
+    // which keeps -inf * scale = -inf for masked keys and changes nothing else representable
+    const float sc2 = fmaxf(fabsf(scale2), 1e-30f);
+    unsigned char* p_tile = sm + L::kP0 + grp * L::kPBytes;
+    // D = 128: each group merges and stores its 64-column half; D = 64: group 0 does all
+    const bool merges = D == 128 || grp == 0;
+    const int col0 = D == 128 ? grp * 64 : 0;
+    const bool issuer = quarter == 0 && lane == 0;  // issues this group's output store
+    uint32_t sc = 0, od = 0, kv = 0, nitem = 0, n_store = 0, n_drain = 0;
+    // P[g] is rewritten (P tiles, or the next output staging) only after this group's last
+    // output store has read it
+    auto drain = [&]() -> bool {
+      if (n_drain == n_store) return true;
+      if (issuer) {
+        tma_store_wait_read();
+        mbar_arrive(&bars[B_ODRAIN0 + grp]);
+      }
+      if (!mbar_wait_warp(&bars[B_ODRAIN0 + grp], n_drain & 1, a.status)) return false;
+      ++n_drain;
+      return true;
+    };
     bool ok = true;
     for (uint32_t w = 0; ok; ++w) {
       WorkEntry e;
-      if (!(ok = ring_get_warp(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
+      ItemPos ip;
+      {
+        const uint32_t slot = w % kRing;
+        if (!(ok = mbar_wait_warp(&bars[B_WFULL0 + slot], (w / kRing) & 1, a.status))) break;
+        e = ring[slot];
+        ip = pos[slot];
+        mbar_arrive(&bars[B_WEMPTY0 + slot]);
+      }
       if (e.item < 0) break;
-      const ItemInfo it = item_info(a, e.item);
       const int n_sub = e.end - e.begin;
-      const int64_t row = it.q_start + rl;
+      const int64_t row = (int64_t)ip.q_start + rl;
+      const int64_t zh = (int64_t)ip.z * a.H + ip.h;
+      T* orow = static_cast<T*>(a.out) + ip.z * a.os[0] + ip.h * a.os[1] + row * a.os[2];
+      if (n_sub == 0) {
+        // no key at all: O = 0, lse = -inf (in accumulate mode out / lse stay as they are)
+        if (!a.accumulate && row < a.N) {
+#pragma unroll
+          for (int v = 0; v < D / 16; ++v)
+            *reinterpret_cast<uint4*>(orow + grp * (D / 2) + v * 8) = make_uint4(0, 0, 0, 0);
+          if (grp == 0 && a.lse) a.lse[zh * a.N + row] = -INFINITY;
+        }
+        continue;
+      }
+      const int n_mine = (n_sub + 1 - grp) >> 1, n_other = (n_sub + grp) >> 1;
       float m_used = -INFINITY, l_sum = 0.f;
-      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      T* orow = static_cast<T*>(a.out) + it.z * a.os[0] + it.h * a.os[1] + row * a.os[2];
-      if (a.accumulate && n_sub > 0) {
-        // Seed TMEM O and the softmax state with the previous (normalised) output and its
-        // LSE: with the reference max at the LSE, that output has weight 1 (l = 1).  The
-        // previous item's PV completed before its epilogue read O, so O is free here.
-        const float lp = row < a.N ? a.lse[(it.z * a.H + it.h) * a.N + row] : -INFINITY;
+      if (a.accumulate && grp == 0) {
+        // Seed TMEM O[0] and group 0's softmax state with the previous (normalised) output and
+        // its LSE: with the reference max at the LSE, that output has weight 1 (l = 1).  O[0]
+        // is free once both groups have read it for the previous item's epilogue.
+        if (nitem > 0 && !mbar_wait_warp(&bars[B_EPI], (nitem - 1) & 1, a.status)) { ok = false; break; }
+        const float lp = row < a.N ? a.lse[zh * a.N + row] : -INFINITY;
         if (lp != -INFINITY) {
           m_used = lp * kLog2e;
           l_sum = 1.f;
@@ -304,150 +495,195 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           float o[32];
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
-            uint4 w = make_uint4(0, 0, 0, 0);
-            if (lp != -INFINITY) w = *reinterpret_cast<const uint4*>(orow + c * 32 + v * 8);
-            const T* e = reinterpret_cast<const T*>(&w);
+            uint4 wv = make_uint4(0, 0, 0, 0);
+            if (lp != -INFINITY) wv = *reinterpret_cast<const uint4*>(orow + c * 32 + v * 8);
+            const T* ev = reinterpret_cast<const T*>(&wv);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[v * 8 + i] = to_f32<T>(e[i]);
+            for (int i = 0; i < 8; ++i) o[v * 8 + i] = to_f32<T>(ev[i]);
           }
-          tmem_st32(lane_addr + kColO + c * 32, o);
+          tmem_st32(lane_addr + col_o + c * 32, o);
         }
         tmem_wait_st();
       }
-      for (int t = 0; t < n_sub && ok; ++t, ++kv) {
-        const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
-        if (!mbar_wait_warp(&bars[B_SFULL0 + sb], sph, a.status)) { ok = false; break; }
+      for (int j = 0; j < n_mine && ok; ++j) {
+        const uint32_t u = kv + grp + 2 * j;
+        if (!mbar_wait_warp(&bars[B_SFULL0 + grp], sc & 1, a.status)) { ok = false; break; }
+        ++sc;
         tc_fence_after();
         float s[kT];
 #pragma unroll
         for (int c = 0; c < kT / 32; ++c) {
           float chunk[32];
-          tmem_ld32(lane_addr + (sb ? kColS1 : kColS0) + c * 32, chunk);
+          tmem_ld32(lane_addr + col_s + c * 32, chunk);
 #pragma unroll
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = chunk[i];
         }
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&bars[B_SEMPTY0 + sb]);
-        ++s_it;
+        mbar_arrive(&bars[B_SEMPTY0 + grp]);
 
-        // the V stage of this tile stays resident until PV(t), which waits for this warp
-        if (!mbar_wait_warp(&bars[B_VFULL0 + (kv & 1)], (kv >> 1) & 1, a.status)) { ok = false; break; }
-        const int64_t ks = meta[kv & 1].key_start;
-        const float b2 = meta[kv & 1].b2;
-        // keys key_start + c are visible for c <= lim (int32, clamped once per tile)
+        const uint32_t ks_slot = u % kKeyRing;
+        if (!mbar_wait_warp(&bars[B_KEYFULL0 + ks_slot], (u / kKeyRing) & 1, a.status)) { ok = false; break; }
+        const int64_t ks = keys[ks_slot].key_start;
+        const float b2 = keys[ks_slot].b2;
+        mbar_arrive(&bars[B_KEYEMPTY0 + ks_slot]);
+        // keys key_start + c are visible for c <= lim (int32, clamped once per tile); masked
+        // scores become -inf in place, so one exp path serves every tile
         int64_t lim64 = a.N - 1 - ks;
         if (a.causal) lim64 = min(lim64, row - ks);
         const int lim = (int)max((int64_t)-1, min((int64_t)kT, lim64));
-        float mt = -INFINITY;
-        if (lim >= kT - 1) {
+        if (neg_scale || lim < kT - 1) {
 #pragma unroll
           for (int c = 0; c < kT; ++c) {
-            s[c] = fmaf(s[c], scale2, b2);
-            mt = fmaxf(mt, s[c]);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < kT; ++c) {
-            s[c] = c <= lim ? fmaf(s[c], scale2, b2) : -INFINITY;
-            mt = fmaxf(mt, s[c]);
+            const float v = neg_scale ? -s[c] : s[c];
+            s[c] = c <= lim ? v : -INFINITY;
           }
         }
+        // row max of the raw scores: three-input max, eight independent chains
+        float mx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+        for (int c = 16; c < kT; c += 2) mx[(c >> 1) & 7] = fmax3(mx[(c >> 1) & 7], s[c], s[c + 1]);
+        const float mraw = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
+        const float mt = fmaf(mraw, sc2, b2);  // -inf when every key of the tile is masked
         // lazy rescale: move the reference max only when it grows by > 2^8
         float m_new = m_used;
         if (mt > -INFINITY && (m_used == -INFINITY || mt > m_used + kRescaleThreshold)) m_new = mt;
         const float m_ref = m_new == -INFINITY ? 0.f : m_new;
         const float alpha = (m_used == -INFINITY) ? 1.f : fast_exp2(m_used - m_ref);
         const bool rescale = (m_new != m_used) && (m_used != -INFINITY);
-        float rs = 0.f;
+        const float bm = b2 - m_ref;
+        // exponent arguments and row sums two lanes at a time (f32x2 FMA / add)
+        const uint64_t scale_x2 = f32x2(sc2, sc2), bias_x2 = f32x2(bm, bm);
+        uint64_t rs[4] = {0, 0, 0, 0};
         uint32_t pk[kT / 2];
 #pragma unroll
         for (int c = 0; c < kT; c += 2) {
-          const float p0 = fast_exp2(s[c] - m_ref);
-          const float p1 = fast_exp2(s[c + 1] - m_ref);
-          rs += p0 + p1;
+          float x0, x1;
+          f32x2_split(fma_f32x2(f32x2(s[c], s[c + 1]), scale_x2, bias_x2), x0, x1);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          rs[(c >> 1) & 3] = add_f32x2(rs[(c >> 1) & 3], f32x2(p0, p1));
           pk[c / 2] = pack2(p0, p1, BF16);
         }
-        // P buffer and O are free once PV of the previous tile completed (a seeded O is
-        // ours from the start)
-        if (t > 0) {
-          if (!mbar_wait_warp(&bars[B_ODONE], od & 1, a.status)) { ok = false; break; }
+        // P[g] and O[g] are free once the group's previous PV completed (a seeded O is ours
+        // from the start)
+        if (j > 0) {
+          if (!mbar_wait_warp(&bars[B_ODONE0 + grp], od & 1, a.status)) { ok = false; break; }
           ++od;
           tc_fence_after();
         }
-        if (t > 0 || a.accumulate) {
+        if (j > 0 || (a.accumulate && grp == 0)) {
           if (__any_sync(0xffffffffu, rescale)) {
             const float f = rescale ? alpha : 1.f;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
               float o[32];
-              tmem_ld32(lane_addr + kColO + c * 32, o);
+              tmem_ld32(lane_addr + col_o + c * 32, o);
               tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 32; ++i) o[i] *= f;
-              tmem_st32(lane_addr + kColO + c * 32, o);
+              tmem_st32(lane_addr + col_o + c * 32, o);
             }
             tmem_wait_st();
           }
         }
+        if (j == 0 && !drain()) { ok = false; break; }
         // P row -> shared memory, 128-byte swizzled K-major (two 64-key chunks)
 #pragma unroll
-        for (int u = 0; u < kT / 8; ++u) {
-          const int kc = u >> 3, unit = u & 7;
+        for (int q = 0; q < kT / 8; ++q) {
+          const int kc = q >> 3, unit = q & 7;
           const uint32_t off = kc * (kT * 128) + rl * 128 + ((unit ^ (rl & 7)) << 4);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p_tile + off)),
-                       "r"(pk[u * 4 + 0]), "r"(pk[u * 4 + 1]), "r"(pk[u * 4 + 2]),
-                       "r"(pk[u * 4 + 3])
+                       "r"(pk[q * 4 + 0]), "r"(pk[q * 4 + 1]), "r"(pk[q * 4 + 2]),
+                       "r"(pk[q * 4 + 3])
                        : "memory");
         }
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(&bars[B_PFULL]);
-        l_sum = (m_used == -INFINITY ? 0.f : l_sum * alpha) + rs;
+        mbar_arrive(&bars[B_PFULL0 + grp]);
+        float r0, r1;
+        f32x2_split(add_f32x2(add_f32x2(rs[0], rs[1]), add_f32x2(rs[2], rs[3])), r0, r1);
+        l_sum = (m_used == -INFINITY ? 0.f : l_sum * alpha) + (r0 + r1);
         if (rescale || m_used == -INFINITY) m_used = m_new;
       }
       if (!ok) break;
       // ---------------------------------------------------------------- epilogue
-      float inv = 0.f;
-      if (n_sub > 0) {
-        if (!mbar_wait_warp(&bars[B_ODONE], od & 1, a.status)) { ok = false; break; }
+      if (n_mine > 0) {
+        if (!mbar_wait_warp(&bars[B_ODONE0 + grp], od & 1, a.status)) { ok = false; break; }
         ++od;
         tc_fence_after();
-        inv = 1.f / (l_sum == 0.f ? 1.f : l_sum);
       }
-      if (a.accumulate && n_sub == 0) continue;  // nothing new: out / lse stay as they are
+      // the partner row's (max, sum) slot is reused once both groups finished the previous
+      // item's epilogue
+      if (nitem > 0 && !mbar_wait_warp(&bars[B_EPI], (nitem - 1) & 1, a.status)) { ok = false; break; }
+      s_ml[grp * kT + rl] = make_float2(m_used, l_sum);
+      mbar_arrive(&bars[B_XCH]);
+      if (!mbar_wait_warp(&bars[B_XCH], nitem & 1, a.status)) { ok = false; break; }
+      const float2 other = s_ml[(grp ^ 1) * kT + rl];
+      const float m = fmaxf(m_used, other.x);
+      const float f_s = m == -INFINITY ? 0.f : fast_exp2(m_used - m);
+      const float f_o = m == -INFINITY ? 0.f : fast_exp2(other.x - m);
+      const float l = l_sum * f_s + other.y * f_o;
+      const float inv = 1.f / (l == 0.f ? 1.f : l);
+      const float w_s = f_s * inv, w_o = f_o * inv;
+      // The merging group stages its 128 rows x 64 columns in its P buffer (free: its last PV
+      // completed and the previous store out of it drained) in the TMA store's 128-byte
+      // swizzled layout, then one thread stores the box.
+      if (merges) {
+        if (!drain()) { ok = false; break; }
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float o[32];
-        if (n_sub > 0) {
-          tmem_ld32(lane_addr + kColO + c * 32, o);
+        for (int c = 0; c < 2; ++c) {
+          // both loads unconditional (a group without tiles in this item leaves stale
+          // columns, which the selects below discard)
+          float os[32], oo[32];
+          tmem_ld32(lane_addr + col_o + col0 + c * 32, os);
+          tmem_ld32(lane_addr + col_oo + col0 + c * 32, oo);
           tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0.f;
-        }
-        if (row < a.N) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack2(o[v * 8 + 0] * inv, o[v * 8 + 1] * inv, BF16);
-            w.y = pack2(o[v * 8 + 2] * inv, o[v * 8 + 3] * inv, BF16);
-            w.z = pack2(o[v * 8 + 4] * inv, o[v * 8 + 5] * inv, BF16);
-            w.w = pack2(o[v * 8 + 6] * inv, o[v * 8 + 7] * inv, BF16);
-            *reinterpret_cast<uint4*>(orow + c * 32 + v * 8) = w;
+            float r[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              r[i] = (n_mine > 0 ? os[v * 8 + i] * w_s : 0.f) + (n_other > 0 ? oo[v * 8 + i] * w_o : 0.f);
+            const uint32_t off = rl * 128 + (((c * 4 + v) ^ (rl & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p_tile + off)),
+                         "r"(pack2(r[0], r[1], BF16)), "r"(pack2(r[2], r[3], BF16)),
+                         "r"(pack2(r[4], r[5], BF16)), "r"(pack2(r[6], r[7], BF16))
+                         : "memory");
           }
         }
+        fence_proxy_async_smem();
       }
       tc_fence_before();
-      if (a.lse && row < a.N)
-        a.lse[(it.z * a.H + it.h) * a.N + row] =
-            n_sub > 0 ? (m_used + log2f(l_sum)) * kLn2 : -INFINITY;
+      mbar_arrive(&bars[B_EPI]);  // O[0], O[1] and the (max, sum) slots are read
+      if (merges) {
+        mbar_arrive(&bars[B_OFULL0 + grp]);
+        if (issuer) {
+          if (mbar_wait(&bars[B_OFULL0 + grp], n_store & 1, a.status))
+            tma_store_4d(&a.tm_o, p_tile, col0, ip.q_start, ip.h, ip.z);
+          else
+            ok = false;
+        }
+        __syncwarp();
+        ok = __all_sync(0xffffffffu, ok);
+        ++n_store;
+        if (!ok) break;
+      }
+      if (grp == 0 && a.lse && row < a.N)
+        a.lse[zh * a.N + row] = m == -INFINITY ? -INFINITY : (m + log2f(l)) * kLn2;
+      kv += n_sub;
+      ++nitem;
     }
   }
 
+  // output stores still in flight must have read their staging buffers (and finished) before
+  // the CTA's shared memory goes away
+  if (warp < kProducerWarp && (warp & 3) == 0 && lane == 0)
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -459,6 +695,7 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
   int rc = make_tmap_4d(&a.tm_q, p.q, p.dtype, p.Z, p.H, p.N, D, p.qs, 64, kT);
   if (!rc) rc = make_tmap_4d(&a.tm_k, p.k, p.dtype, p.Z, p.Hkv, p.N, D, p.ks, 64, kT);
   if (!rc) rc = make_tmap_4d(&a.tm_v, p.v, p.dtype, p.Z, p.Hkv, p.N, D, p.vs, 64, kT);
+  if (!rc) rc = make_tmap_4d(&a.tm_o, p.out, p.dtype, p.Z, p.H, p.N, D, p.os, 64, kT);
   // The shape passed the eligibility checks: a failure here is an error, never a silent
   // hand-off to the CUDA-core kernel.
   if (rc) return fail(SA_ELAUNCH, std::string("forward tensor maps: ") + sa_last_error());
@@ -494,6 +731,12 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
     a.sched = SchedArgs{pp.header, pp.queue, items};
   }
   auto kern = fwd_sm100_kernel<D, BF16>;
+  // setmaxnreg.inc waits until the registers it asks for are free: launch only when the
+  // per-thread launch allocation is the one the split was sized against.
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != kLaunchRegs)
+    return fail(SA_ELAUNCH, "forward kernel: launch register count " + std::to_string(fa.numRegs) +
+                                " differs from the register split's " + std::to_string(kLaunchRegs));
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdLayout<D>::kAlloc);
   kern<<<grid, kFwdThreads, FwdLayout<D>::kAlloc, stream>>>(a);
   return check_launch("fwd_sm100_kernel");
