@@ -4,29 +4,34 @@
 // query block's own list, token-level causal and tail masks, exp2 online softmax, empty rows
 // -> 0 / lse -inf, natural-log LSE, optional per-(row block, slot) logit bias).
 //
-// Persistent kernel, one CTA per SM, 12 warps (softmax warpgroups raised to 224 registers with
-// setmaxnreg, the control warpgroup lowered to 56):
+// Persistent kernel, one CTA per SM, 12 warps (softmax warpgroups raised to 216 registers with
+// setmaxnreg, the control warpgroup lowered to 72):
 //   warp 10     scheduler: takes work entries (queue atomic or round-robin), computes each
 //               item's indices once, reads its list 32 entries per coalesced warp load and
 //               pushes one key start (+ soft bias) per key tile into an 8-slot shared ring,
-//               prefetching the Q tile and every K/V tile into L2 as it goes.
+//               and prefetches each item's Q tile into L2 (an L2 prefetch of every K/V tile as
+//               well measured slower: it shares the SM's TMA throughput with the loads).
 //   warp 8      TMA producer: Q tile once per work item, K tiles into a 2-stage ring and V
-//               tiles into another, V running two tiles behind K (the order in which the MMA
-//               frees the stages); it never touches global memory itself.
+//               tiles into another, V running two tiles behind K within an item (the order in
+//               which the MMA frees the stages); it never touches global memory itself.
 //   warp 9      TMEM owner + single-thread tcgen05.mma issuer:
-//                 S[g] = Q K_t^T    (M=128, N=128, K=D; fp32 in TMEM), g = t & 1
+//                 S[g] = Q K_t^T    (M=128, N=128, K=D; fp32 in TMEM)
 //                 O[g] += P_t V_t   (M=128, N=D,   K=128; fp32 in TMEM)
-//               Tiles go in pairs (one per group): the QKs of pair p+1 are issued before the PVs
-//               of pair p, so each group finds its next S computed when it finishes a tile, and
-//               the two groups run the same code at the same time (one instruction-cache
-//               footprint).
-//   warps 0-7   two softmax groups of 4 warps; group g takes the key tiles t = g, g+2, ... of
-//               the work item with its own running max / sum and its own O[g].  Thread = query
-//               row (TMEM lane); tcgen05.ld of S, masking, row max, exp2, P (bf16/fp16) into the
-//               group's shared-memory P buffer in the MMA's swizzled K-major layout; O[g]
-//               rescaled in TMEM only when the row max grows by more than 2^8 (lazy rescale).
-//               Epilogue: the groups swap (max, sum) per row through shared memory and each
-//               merges O[0] and O[1] for half of the head dim, O / l -> global, LSE.
+//               Key tiles alternate between the two softmax groups (g = running tile index
+//               mod 2, across items).  Tiles go in pairs: the QKs of pair p+1 are issued
+//               before the PVs of pair p, so each group finds its next S computed, and the
+//               two groups run the same code at the same time (one instruction-cache
+//               footprint).  A one-tile item's PV waits until the next item's first QK, so
+//               runs of one-tile items (very sparse lists) keep both groups busy.
+//   warps 0-7   two softmax groups of 4 warps, each with its own running max / sum and O[g].
+//               Thread = query row (TMEM lane); tcgen05.ld of S, masking (-inf in place),
+//               row max, exp2, P (bf16/fp16) into the group's shared-memory P buffer in the
+//               MMA's swizzled K-major layout; O[g] rescaled in TMEM only when the row max
+//               grows by more than 2^8 (lazy rescale).
+//               Epilogue of an item of >= 2 tiles: the groups swap (max, sum) per row through
+//               shared memory and each merges O[0] and O[1] for half of the head dim; of a
+//               one-tile item: its owner alone.  O / l is staged (128B swizzle) in the P
+//               buffer and written by TMA tile stores; LSE.
 //   warp 11     idle (it completes the control warpgroup for setmaxnreg).
 // Work item = (query tile of 128 rows, z, h).  With a planner workspace the items come
 // heaviest-first from the device-built queue (one atomic per item); without one, round-robin
@@ -44,7 +49,7 @@ constexpr int kFwdThreads = 384;  // 12 warps
 constexpr int kProducerWarp = 8, kMmaWarp = 9, kSchedWarp = 10;
 // Register split: the launch gives every thread kLaunchRegs; the control warpgroup (warps
 // 8-11) drops to kCtrlRegs and the two softmax warpgroups take what it frees.
-constexpr int kLaunchRegs = 168, kCtrlRegs = 56, kSoftmaxRegs = 224;
+constexpr int kLaunchRegs = 168, kCtrlRegs = 72, kSoftmaxRegs = 216;
 static_assert(4 * 32 * kCtrlRegs + 8 * 32 * kSoftmaxRegs <= kFwdThreads * kLaunchRegs,
               "register split exceeds the launch allocation");
 constexpr int kGroupThreads = 128;
@@ -79,8 +84,8 @@ enum {
   B_QFULL = 0, B_QEMPTY,
   B_KFULL0, B_KEMPTY0 = B_KFULL0 + 2, B_VFULL0 = B_KEMPTY0 + 2, B_VEMPTY0 = B_VFULL0 + 2,
   B_SFULL0 = B_VEMPTY0 + 2, B_SEMPTY0 = B_SFULL0 + 2, B_PFULL0 = B_SEMPTY0 + 2,
-  B_ODONE0 = B_PFULL0 + 2, B_XCH = B_ODONE0 + 2, B_EPI,
-  B_OFULL0, B_ODRAIN0 = B_OFULL0 + 2, B_KEYFULL0 = B_ODRAIN0 + 2,
+  B_ODONE0 = B_PFULL0 + 2, B_XCH = B_ODONE0 + 2, B_EPI, B_EPI1_0,
+  B_OFULL0 = B_EPI1_0 + 2, B_ODRAIN0 = B_OFULL0 + 2, B_KEYFULL0 = B_ODRAIN0 + 2,
   B_KEYEMPTY0 = B_KEYFULL0 + kKeyRing,
   B_WFULL0 = B_KEYEMPTY0 + kKeyRing, B_WEMPTY0 = B_WFULL0 + kRing, B_NUM = B_WEMPTY0 + kRing
 };
@@ -94,7 +99,7 @@ struct FwdLayout {
   static constexpr uint32_t kV0 = kK0 + 2 * kTileBytes;
   static constexpr uint32_t kP0 = kV0 + 2 * kTileBytes;  // P[2], one per softmax group
   static constexpr uint32_t kBars = kP0 + 2 * kPBytes;
-  static constexpr uint32_t kKeys = kBars + 384;              // TileKey[kKeyRing]
+  static constexpr uint32_t kKeys = kBars + 448;              // TileKey[kKeyRing]
   static constexpr uint32_t kRingOff = kKeys + kKeyRing * 16;  // WorkEntry[kRing]
   static constexpr uint32_t kPos = kRingOff + 64;               // ItemPos[kRing]
   static constexpr uint32_t kML = kPos + 64;                    // float2 [2][kT]: (max, sum)
@@ -104,7 +109,7 @@ struct FwdLayout {
   // kernel checks the padding it needs against %dynamic_smem_size
   static constexpr uint32_t kAlloc = kBytes + 1024 <= kMaxSmem ? kBytes + 1024 : kMaxSmem;
   static_assert(kBytes <= kMaxSmem, "forward shared-memory layout too large");
-  static_assert(B_NUM * 8 <= 384, "barrier area too small");
+  static_assert(B_NUM * 8 <= 448, "barrier area too small");
   static_assert(kRing * 16 <= 64, "work ring area too small");
 };
 
@@ -196,6 +201,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     }
     mbar_init(&bars[B_XCH], 2 * kGroupThreads);
     mbar_init(&bars[B_EPI], 2 * kGroupThreads);
+    mbar_init(&bars[B_EPI1_0], kGroupThreads);  // a one-tile item's owner has read O[0]
+    mbar_init(&bars[B_EPI1_0 + 1], kGroupThreads);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_OFULL0 + i], kGroupThreads);  // output rows staged for the TMA store
       mbar_init(&bars[B_ODRAIN0 + i], 1);             // that store has read its staging buffer
@@ -281,10 +288,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
             if (ok) {
               keys[slot] = TileKey{ks, b2, 0};
               mbar_arrive(&bars[B_KEYFULL0 + slot]);
-              for (int c = 0; c < D / 64; ++c) {
-                tma_prefetch_4d(&a.tm_k, c * 64, (int)ks, (int)it.hk, (int)it.z);
-                tma_prefetch_4d(&a.tm_v, c * 64, (int)ks, (int)it.hk, (int)it.z);
-              }
             }
           }
           ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -298,6 +301,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     if (lane == 0) {
       uint32_t kv = 0, jq = 0;
       bool ok = true;
+      // Within an item, V of tile u is loaded after K of tile u + 2 (the order in which the
+      // MMA frees the stages).  At the next item's start, before the wait for the Q slot, the
+      // item's pending V loads go out: the MMA needs them before (or, for a one-tile item,
+      // right after) the next item's first QK, and their stages were freed by PVs of earlier
+      // items.
+      struct PendV {
+        uint32_t u;
+        int ks, hk, z;
+      };
+      PendV pq[3];
+      int pq_n = 0;
+      auto load_v = [&](const PendV& pv) -> bool {
+        const uint32_t st = pv.u & 1, ph = (pv.u >> 1) & 1;
+        if (!mbar_wait(&bars[B_VEMPTY0 + st], ph ^ 1, a.status)) return false;
+        mbar_arrive_expect_tx(&bars[B_VFULL0 + st], L::kTileBytes);
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(sm + L::kV0 + st * L::kTileBytes + c * kT * 128, &a.tm_v,
+                      &bars[B_VFULL0 + st], c * 64, pv.ks, pv.hk, pv.z);
+        mbar_arrive(&bars[B_KEYEMPTY0 + pv.u % kKeyRing]);  // the tile's key slot is done
+        return true;
+      };
       for (uint32_t w = 0; ok; ++w) {
         WorkEntry e;
         ItemPos ip;
@@ -311,6 +335,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         if (e.item < 0) break;
         const int n = e.end - e.begin;
         if (n == 0) continue;
+        for (int i = 0; i < pq_n && ok; ++i) ok = load_v(pq[i]);
+        pq_n = 0;
+        if (!ok) break;
         ok = mbar_wait(&bars[B_QEMPTY], (jq & 1) ^ 1, a.status);
         if (!ok) break;
         mbar_arrive_expect_tx(&bars[B_QFULL], L::kTileBytes);
@@ -318,35 +345,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           tma_load_4d(sm + L::kQ + c * kT * 128, &a.tm_q, &bars[B_QFULL], c * 64, ip.q_start, ip.h,
                       ip.z);
         ++jq;
-        // step i: K of tile i, then V of tile i - 2 (whose key slot it then releases)
-        for (int i = 0; i < n + 2 && ok; ++i) {
-          if (i < n) {
-            const uint32_t u = kv + i, ks_slot = u % kKeyRing;
-            ok = mbar_wait(&bars[B_KEYFULL0 + ks_slot], (u / kKeyRing) & 1, a.status);
-            if (!ok) break;
-            const int ks = (int)keys[ks_slot].key_start;
-            const uint32_t st = u & 1, ph = (u >> 1) & 1;
-            ok = mbar_wait(&bars[B_KEMPTY0 + st], ph ^ 1, a.status);
-            if (!ok) break;
-            mbar_arrive_expect_tx(&bars[B_KFULL0 + st], L::kTileBytes);
-            for (int c = 0; c < D / 64; ++c)
-              tma_load_4d(sm + L::kK0 + st * L::kTileBytes + c * kT * 128, &a.tm_k,
-                          &bars[B_KFULL0 + st], c * 64, ks, ip.hk, ip.z);
-          }
-          if (i >= 2) {
-            const uint32_t u = kv + i - 2, ks_slot = u % kKeyRing, st = u & 1, ph = (u >> 1) & 1;
-            const int ks = (int)keys[ks_slot].key_start;
-            ok = mbar_wait(&bars[B_VEMPTY0 + st], ph ^ 1, a.status);
-            if (!ok) break;
-            mbar_arrive_expect_tx(&bars[B_VFULL0 + st], L::kTileBytes);
-            for (int c = 0; c < D / 64; ++c)
-              tma_load_4d(sm + L::kV0 + st * L::kTileBytes + c * kT * 128, &a.tm_v,
-                          &bars[B_VFULL0 + st], c * 64, ks, ip.hk, ip.z);
-            mbar_arrive(&bars[B_KEYEMPTY0 + ks_slot]);
+        for (int i = 0; i < n && ok; ++i) {
+          const uint32_t u = kv + i, ks_slot = u % kKeyRing;
+          ok = mbar_wait(&bars[B_KEYFULL0 + ks_slot], (u / kKeyRing) & 1, a.status);
+          if (!ok) break;
+          const int ks = (int)keys[ks_slot].key_start;
+          const uint32_t st = u & 1, ph = (u >> 1) & 1;
+          ok = mbar_wait(&bars[B_KEMPTY0 + st], ph ^ 1, a.status);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&bars[B_KFULL0 + st], L::kTileBytes);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(sm + L::kK0 + st * L::kTileBytes + c * kT * 128, &a.tm_k,
+                        &bars[B_KFULL0 + st], c * 64, ks, ip.hk, ip.z);
+          pq[pq_n++] = PendV{u, ks, ip.hk, ip.z};
+          if (pq_n == 3) {
+            ok = load_v(pq[0]);
+            pq[0] = pq[1];
+            pq[1] = pq[2];
+            pq_n = 2;
           }
         }
         kv += n;
       }
+      for (int i = 0; i < pq_n && ok; ++i) ok = load_v(pq[i]);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
@@ -354,22 +375,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       constexpr uint32_t idesc_qk = idesc_f16(kT, kT, BF16, false, false);
       constexpr uint32_t idesc_pv = idesc_f16(kT, D, BF16, false, true);
       const uint32_t q_addr = smem_u32(sm + L::kQ);
-      uint32_t kv = 0, jq = 0, nitem = 0;
+      uint32_t kv = 0, jq = 0, n_multi = 0, n_solo[2] = {0, 0};
       uint32_t sq[2] = {0, 0}, pv[2] = {0, 0};
+      // O[g] is free for a new item once the readers of its last item are done: that item's
+      // epilogue barrier and phase (EPI for items of >= 2 tiles, EPI1[g] for one-tile items)
+      int guard_bar[2] = {-1, -1};
+      uint32_t guard_ph[2] = {0, 0};
       bool ok = true;
-      // PV of tile u (item-local index t) into O[t & 1]; the item's first PV waits until both
-      // groups have read O[0] / O[1] for the previous item's epilogue.
-      auto issue_pv = [&](uint32_t u, int t) -> bool {
-        const int g = t & 1;
+      // PV of tile u into O[g]; the group's first PV of an item (first_of_g) waits for O[g]'s
+      // guard and, unless O[g] was seeded, starts it afresh
+      auto issue_pv = [&](uint32_t u, int g, bool first_of_g, bool seeded) -> bool {
         const uint32_t st = u & 1, ph = (u >> 1) & 1;
-        if (t == 0 && nitem > 0 && !mbar_wait(&bars[B_EPI], (nitem - 1) & 1, a.status)) return false;
+        if (first_of_g && guard_bar[g] >= 0 &&
+            !mbar_wait(&bars[guard_bar[g]], guard_ph[g] & 1, a.status))
+          return false;
         if (!mbar_wait(&bars[B_PFULL0 + g], pv[g] & 1, a.status)) return false;
         if (!mbar_wait(&bars[B_VFULL0 + st], ph, a.status)) return false;
         tc_fence_after();
         const uint32_t p_addr = smem_u32(sm + L::kP0 + g * L::kPBytes);
         const uint32_t v_addr = smem_u32(sm + L::kV0 + st * L::kTileBytes);
-        // the group's first PV of the item starts O[g] afresh, except a seeded O[0]
-        const bool first = t < 2 && !(a.accumulate && g == 0);
+        const bool first = first_of_g && !seeded;
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk) {
           const uint64_t ad = smem_desc(p_addr + (kk >> 2) * (kT * 128) + (kk & 3) * 32, 16, 1024);
@@ -381,6 +406,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         ++pv[g];
         return true;
       };
+      // A one-tile item's PV waits until the next item's first QK is issued, so that runs of
+      // one-tile items (owned by alternating groups) overlap their softmax.  Safe: a QK only
+      // needs its group to have started its previous tile, never a finished epilogue.
+      bool pend = false;
+      uint32_t pend_u = 0;
+      int pend_g = 0;
+      auto issue_pending = [&]() -> bool {
+        if (!pend) return true;
+        pend = false;
+        if (!issue_pv(pend_u, pend_g, true, a.accumulate != 0)) return false;
+        guard_bar[pend_g] = B_EPI1_0 + pend_g;
+        guard_ph[pend_g] = n_solo[pend_g]++;
+        return true;
+      };
       for (uint32_t w = 0; ok; ++w) {
         WorkEntry e;
         if (!(ok = ring_get(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
@@ -390,9 +429,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         ok = mbar_wait(&bars[B_QFULL], jq & 1, a.status);
         ++jq;
         if (!ok) break;
+        const int gb = (int)(kv & 1);  // tile t goes to group (gb + t) & 1
         int pv_next = 0;
         for (int t = 0; t < n_sub && ok; ++t) {
-          const uint32_t u = kv + t, g = t & 1;
+          const uint32_t u = kv + t, g = (gb + t) & 1;
           const uint32_t st = u & 1, ph = (u >> 1) & 1;
           ok = mbar_wait(&bars[B_KFULL0 + st], ph, a.status) &&
                mbar_wait(&bars[B_SEMPTY0 + g], (sq[g] & 1) ^ 1, a.status);
@@ -409,15 +449,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           tc_commit(&bars[B_KEMPTY0 + st]);
           if (t == n_sub - 1) tc_commit(&bars[B_QEMPTY]);
           ++sq[g];
+          if (t == 0) ok = issue_pending();
           // after the QKs of pair (t-1, t): the PVs of the previous pair, so that both groups
           // run the same code in step (one instruction-cache footprint) and find the next S ready
           if (t & 1)
-            for (; pv_next <= t - 2 && ok; ++pv_next) ok = issue_pv(kv + pv_next, pv_next);
+            for (; pv_next <= t - 2 && ok; ++pv_next)
+              ok = issue_pv(kv + pv_next, (gb + pv_next) & 1, pv_next < 2, a.accumulate && pv_next == 0);
         }
-        for (; pv_next < n_sub && ok; ++pv_next) ok = issue_pv(kv + pv_next, pv_next);
+        if (!ok) break;
+        if (n_sub == 1) {
+          pend = true;
+          pend_u = kv;
+          pend_g = gb;
+        } else {
+          for (; pv_next < n_sub && ok; ++pv_next)
+            ok = issue_pv(kv + pv_next, (gb + pv_next) & 1, pv_next < 2, a.accumulate && pv_next == 0);
+          guard_bar[0] = guard_bar[1] = B_EPI;
+          guard_ph[0] = guard_ph[1] = n_multi++;
+        }
         kv += n_sub;
-        ++nitem;
       }
+      if (ok) ok = issue_pending();
     }
   }
   } else {
@@ -435,11 +487,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     // which keeps -inf * scale = -inf for masked keys and changes nothing else representable
     const float sc2 = fmaxf(fabsf(scale2), 1e-30f);
     unsigned char* p_tile = sm + L::kP0 + grp * L::kPBytes;
-    // D = 128: each group merges and stores its 64-column half; D = 64: group 0 does all
-    const bool merges = D == 128 || grp == 0;
-    const int col0 = D == 128 ? grp * 64 : 0;
     const bool issuer = quarter == 0 && lane == 0;  // issues this group's output store
-    uint32_t sc = 0, od = 0, kv = 0, nitem = 0, n_store = 0, n_drain = 0;
+    // n_multi: items of >= 2 tiles so far (XCH / EPI phases); n_solo: one-tile items owned
+    uint32_t sc = 0, od = 0, kv = 0, n_multi = 0, n_solo = 0, n_store = 0, n_drain = 0;
     // P[g] is rewritten (P tiles, or the next output staging) only after this group's last
     // output store has read it
     auto drain = [&]() -> bool {
@@ -478,13 +528,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         }
         continue;
       }
-      const int n_mine = (n_sub + 1 - grp) >> 1, n_other = (n_sub + grp) >> 1;
+      // tile t goes to group (gb + t) & 1 (the alternation runs on across items); an item of
+      // one tile is finished by its owner alone, the other group skips it
+      const int gb = (int)(kv & 1);
+      const bool solo = n_sub == 1;
+      if (solo && grp != gb) {
+        kv += 1;
+        continue;
+      }
+      const int first_t = (grp ^ gb) & 1;
+      const int n_mine = n_sub > first_t ? (n_sub - first_t + 1) >> 1 : 0;
       float m_used = -INFINITY, l_sum = 0.f;
-      if (a.accumulate && grp == 0) {
-        // Seed TMEM O[0] and group 0's softmax state with the previous (normalised) output and
-        // its LSE: with the reference max at the LSE, that output has weight 1 (l = 1).  O[0]
-        // is free once both groups have read it for the previous item's epilogue.
-        if (nitem > 0 && !mbar_wait_warp(&bars[B_EPI], (nitem - 1) & 1, a.status)) { ok = false; break; }
+      if (a.accumulate && grp == gb) {
+        // Seed TMEM O[g] and this group's softmax state with the previous (normalised) output
+        // and its LSE: with the reference max at the LSE, that output has weight 1 (l = 1).
+        // O[g] is free once the readers of the last multi-tile item are done (a one-tile item
+        // that used O[g] was this group's own).
+        if (n_multi > 0 && !mbar_wait_warp(&bars[B_EPI], (n_multi - 1) & 1, a.status)) { ok = false; break; }
         const float lp = row < a.N ? a.lse[zh * a.N + row] : -INFINITY;
         if (lp != -INFINITY) {
           m_used = lp * kLog2e;
@@ -506,7 +566,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         tmem_wait_st();
       }
       for (int j = 0; j < n_mine && ok; ++j) {
-        const uint32_t u = kv + grp + 2 * j;
+        const uint32_t u = kv + first_t + 2 * j;
         if (!mbar_wait_warp(&bars[B_SFULL0 + grp], sc & 1, a.status)) { ok = false; break; }
         ++sc;
         tc_fence_after();
@@ -573,7 +633,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           ++od;
           tc_fence_after();
         }
-        if (j > 0 || (a.accumulate && grp == 0)) {
+        if (j > 0 || (a.accumulate && grp == gb)) {
           if (__any_sync(0xffffffffu, rescale)) {
             const float f = rescale ? alpha : 1.f;
 #pragma unroll
@@ -614,40 +674,49 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         ++od;
         tc_fence_after();
       }
-      // the partner row's (max, sum) slot is reused once both groups finished the previous
-      // item's epilogue
-      if (nitem > 0 && !mbar_wait_warp(&bars[B_EPI], (nitem - 1) & 1, a.status)) { ok = false; break; }
-      s_ml[grp * kT + rl] = make_float2(m_used, l_sum);
-      mbar_arrive(&bars[B_XCH]);
-      if (!mbar_wait_warp(&bars[B_XCH], nitem & 1, a.status)) { ok = false; break; }
-      const float2 other = s_ml[(grp ^ 1) * kT + rl];
+      // An item of >= 2 tiles: the groups swap (max, sum) per row; the (max, sum) slots are
+      // reused once both groups finished the previous such item.  A one-tile item: the owner's
+      // own state is the whole result.
+      float2 other = make_float2(-INFINITY, 0.f);
+      if (!solo) {
+        if (n_multi > 0 && !mbar_wait_warp(&bars[B_EPI], (n_multi - 1) & 1, a.status)) { ok = false; break; }
+        s_ml[grp * kT + rl] = make_float2(m_used, l_sum);
+        mbar_arrive(&bars[B_XCH]);
+        if (!mbar_wait_warp(&bars[B_XCH], n_multi & 1, a.status)) { ok = false; break; }
+        other = s_ml[(grp ^ 1) * kT + rl];
+      }
       const float m = fmaxf(m_used, other.x);
       const float f_s = m == -INFINITY ? 0.f : fast_exp2(m_used - m);
       const float f_o = m == -INFINITY ? 0.f : fast_exp2(other.x - m);
       const float l = l_sum * f_s + other.y * f_o;
       const float inv = 1.f / (l == 0.f ? 1.f : l);
       const float w_s = f_s * inv, w_o = f_o * inv;
-      // The merging group stages its 128 rows x 64 columns in its P buffer (free: its last PV
-      // completed and the previous store out of it drained) in the TMA store's 128-byte
-      // swizzled layout, then one thread stores the box.
-      if (merges) {
+      // Columns this group stages: all of them for a one-tile item; otherwise its 64-column half
+      // (D = 128) or, for D = 64, group 0 all.  Staging goes to the group's P buffer (free: its
+      // last PV completed, the previous store out of it drained) in the TMA store's 128-byte
+      // swizzled layout, one 128 x 64 box per 16 KB; one thread then stores the boxes.
+      const int cols_lo = solo ? 0 : (D == 128 ? grp * 64 : 0);
+      const int n_chunks = solo ? D / 32 : ((D == 128 || grp == 0) ? 2 : 0);
+      // both O buffers hold this item's data for a multi-tile item; a one-tile item reads its
+      // own twice (weight 0 on the second)
+      const uint32_t col_other = solo ? col_o : col_oo;
+      if (n_chunks > 0) {
         if (!drain()) { ok = false; break; }
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          // both loads unconditional (a group without tiles in this item leaves stale
-          // columns, which the selects below discard)
+#pragma unroll 1
+        for (int c = 0; c < n_chunks; ++c) {
+          const uint32_t col = cols_lo + c * 32;
           float os[32], oo[32];
-          tmem_ld32(lane_addr + col_o + col0 + c * 32, os);
-          tmem_ld32(lane_addr + col_oo + col0 + c * 32, oo);
+          tmem_ld32(lane_addr + col_o + col, os);
+          tmem_ld32(lane_addr + col_other + col, oo);
           tmem_wait_ld();
+          unsigned char* box = p_tile + (c >> 1) * (kT * 128);
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             float r[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              r[i] = (n_mine > 0 ? os[v * 8 + i] * w_s : 0.f) + (n_other > 0 ? oo[v * 8 + i] * w_o : 0.f);
-            const uint32_t off = rl * 128 + (((c * 4 + v) ^ (rl & 7)) << 4);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p_tile + off)),
+            for (int i = 0; i < 8; ++i) r[i] = os[v * 8 + i] * w_s + oo[v * 8 + i] * w_o;
+            const uint32_t off = rl * 128 + (((((c & 1) * 4) + v) ^ (rl & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(box + off)),
                          "r"(pack2(r[0], r[1], BF16)), "r"(pack2(r[2], r[3], BF16)),
                          "r"(pack2(r[4], r[5], BF16)), "r"(pack2(r[6], r[7], BF16))
                          : "memory");
@@ -656,24 +725,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         fence_proxy_async_smem();
       }
       tc_fence_before();
-      mbar_arrive(&bars[B_EPI]);  // O[0], O[1] and the (max, sum) slots are read
-      if (merges) {
+      // O[0] / O[1] (and the (max, sum) slots) are read
+      mbar_arrive(solo ? &bars[B_EPI1_0 + grp] : &bars[B_EPI]);
+      if (n_chunks > 0) {
         mbar_arrive(&bars[B_OFULL0 + grp]);
         if (issuer) {
-          if (mbar_wait(&bars[B_OFULL0 + grp], n_store & 1, a.status))
-            tma_store_4d(&a.tm_o, p_tile, col0, ip.q_start, ip.h, ip.z);
-          else
+          if (mbar_wait(&bars[B_OFULL0 + grp], n_store & 1, a.status)) {
+            for (int b = 0; b < n_chunks / 2; ++b)
+              tma_store_4d(&a.tm_o, p_tile + b * (kT * 128), cols_lo + b * 64, ip.q_start, ip.h, ip.z);
+          } else {
             ok = false;
+          }
         }
         __syncwarp();
         ok = __all_sync(0xffffffffu, ok);
         ++n_store;
         if (!ok) break;
       }
-      if (grp == 0 && a.lse && row < a.N)
+      if ((solo || grp == 0) && a.lse && row < a.N)
         a.lse[zh * a.N + row] = m == -INFINITY ? -INFINITY : (m + log2f(l)) * kLn2;
       kv += n_sub;
-      ++nitem;
+      if (solo)
+        ++n_solo;
+      else
+        ++n_multi;
     }
   }
 
