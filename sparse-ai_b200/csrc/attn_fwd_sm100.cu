@@ -798,13 +798,6 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
   a.status = p.status;
   const int64_t items = a.Z * a.H * a.QT;
   const int grid = (int)std::min<int64_t>(items, device_sm_count());
-  a.sched = SchedArgs{nullptr, nullptr, items};
-  if (p.plan_fwd) {
-    const PlanPtrs pp = plan_carve(p.plan_fwd, kPlanFwd, items, grid, D);
-    rc = launch_plan(kPlanFwd, p, items, grid, pp, stream);
-    if (rc) return rc;
-    a.sched = SchedArgs{pp.header, pp.queue, items};
-  }
   auto kern = fwd_sm100_kernel<D, BF16>;
   // setmaxnreg.inc waits until the registers it asks for are free: launch only when the
   // per-thread launch allocation is the one the split was sized against.
@@ -812,7 +805,21 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
   if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != kLaunchRegs)
     return fail(SA_ELAUNCH, "forward kernel: launch register count " + std::to_string(fa.numRegs) +
                                 " differs from the register split's " + std::to_string(kLaunchRegs));
+  a.sched = SchedArgs{nullptr, nullptr, items, 0};
+  if (p.plan_fwd) {
+    // Each CTA's first item is its own index (the static order starts with the late query
+    // tiles, heavy under causal masking); the planner orders the rest heaviest-first while
+    // that first wave runs: the kernel is its programmatic dependent and waits for it only
+    // before the second fetch.
+    const PlanPtrs pp = plan_carve(p.plan_fwd, kPlanFwd, items, grid, D);
+    rc = launch_plan(kPlanFwd, p, items, grid, pp, stream, grid);
+    if (rc) return rc;
+    a.sched = SchedArgs{pp.header, pp.queue, items, 1};
+  }
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdLayout<D>::kAlloc);
+  if (p.plan_fwd)
+    return launch_dependent(kern, dim3(grid), dim3(kFwdThreads), FwdLayout<D>::kAlloc, stream,
+                            "fwd_sm100_kernel", a);
   kern<<<grid, kFwdThreads, FwdLayout<D>::kAlloc, stream>>>(a);
   return check_launch("fwd_sm100_kernel");
 }

@@ -20,6 +20,7 @@ struct PlanArgs {
   const int32_t* counts;    // forward lists' counts (Z, H, NB)
   const int32_t* q_counts;  // transposed lists' counts (Z, H, NB)
   int ctas;
+  int skip;  // items [0, skip) are not queued (the forward's first wave takes them directly)
   PlanPtrs plan;
   int* weights;
 };
@@ -58,8 +59,11 @@ constexpr int kPlanWarps = kPlanThreads / 32;
 // takes its queue slots with an atomic on its warp's cursor.  The order inside a bin does
 // not matter: items write disjoint outputs and split items are reduced in chunk order.
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
-  // Items tid + k * blockDim for k < kRegItems keep their weight in registers; larger item
-  // counts spill the rest to a.weights.  Every pass over the items is one coalesced sweep.
+  // a kernel launched as this grid's programmatic dependent may start now; it waits for this
+  // grid (griddepcontrol.wait) before it reads the queue
+  pdl_trigger();
+  // Items skip + tid + k * blockDim for k < kRegItems keep their weight in registers; larger
+  // item counts spill the rest to a.weights.  Every pass over the items is one coalesced sweep.
   constexpr int kRegItems = 8;
   __shared__ int s_cnt[kBins][kPlanWarps];  // counts, then cursors
   __shared__ int s_wsum[kPlanWarps];
@@ -79,11 +83,11 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
   unsigned long long tot = 0;
 #pragma unroll
   for (int k = 0; k < kRegItems; ++k) {  // independent loads, all in flight together
-    const int i = tid + k * nthr;
+    const int i = a.skip + tid + k * nthr;
     wreg[k] = i < a.items ? item_weight(a, i) : 0;
     tot += (unsigned long long)wreg[k];
   }
-  for (int i = tid + kRegItems * nthr; i < a.items; i += nthr) {
+  for (int i = a.skip + tid + kRegItems * nthr; i < a.items; i += nthr) {
     const int w = item_weight(a, i);
     a.weights[i] = w;
     tot += (unsigned long long)w;
@@ -102,13 +106,13 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
   // ---- per-warp histograms
 #pragma unroll
   for (int k = 0; k < kRegItems; ++k) {
-    const int i = tid + k * nthr;
+    const int i = a.skip + tid + k * nthr;
     if (i < a.items) {
       const int c = chunks_of(wreg[k]);
       atomicAdd(&s_cnt[bin_of(wreg[k], c)][warp], c);
     }
   }
-  for (int i = tid + kRegItems * nthr; i < a.items; i += nthr) {
+  for (int i = a.skip + tid + kRegItems * nthr; i < a.items; i += nthr) {
     const int w = a.weights[i], c = chunks_of(w);
     atomicAdd(&s_cnt[bin_of(w, c)][warp], c);
   }
@@ -159,10 +163,10 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
   };
 #pragma unroll
   for (int k = 0; k < kRegItems; ++k) {
-    const int i = tid + k * nthr;
+    const int i = a.skip + tid + k * nthr;
     if (i < a.items) scatter_one(i, wreg[k]);
   }
-  for (int i = tid + kRegItems * nthr; i < a.items; i += nthr) scatter_one(i, a.weights[i]);
+  for (int i = a.skip + tid + kRegItems * nthr; i < a.items; i += nthr) scatter_one(i, a.weights[i]);
   __syncthreads();
   if (tid == 0) {
     a.plan.header->counter = 0;
@@ -255,7 +259,7 @@ PlanPtrs plan_carve(void* ws, int kind, int64_t items, int ctas, int64_t D) {
 }
 
 int launch_plan(int kind, const AttnParams& p, int64_t items, int ctas, const PlanPtrs& plan,
-                cudaStream_t stream) {
+                cudaStream_t stream, int skip) {
   if (items > INT32_MAX || p.Z * p.H * p.NB > INT32_MAX)
     return fail(SA_EUNSUPPORTED, "too many work items");
   PlanArgs a{};
@@ -270,6 +274,7 @@ int launch_plan(int kind, const AttnParams& p, int64_t items, int ctas, const Pl
   a.counts = p.counts;
   a.q_counts = p.q_counts;
   a.ctas = ctas;
+  a.skip = skip;
   a.plan = plan;
   a.weights = reinterpret_cast<int*>(reinterpret_cast<char*>(plan.splits) +
                                      align256((size_t)(ctas + 1) * sizeof(SplitItem)));

@@ -52,7 +52,7 @@ PlanPtrs plan_carve(void* ws, int kind, int64_t items, int ctas, int64_t D);
 
 // Launch the planner for `kind` over the items of `p` (sizes and lists as in the kernels).
 int launch_plan(int kind, const AttnParams& p, int64_t items, int ctas, const PlanPtrs& plan,
-                cudaStream_t stream);
+                cudaStream_t stream, int skip = 0);
 
 // Sum the split dK/dV partials and store bf16/fp16 dK, dV rows of the split items.
 int launch_dkdv_reduce(const AttnParams& p, const PlanPtrs& plan, int ctas, cudaStream_t stream);

@@ -148,31 +148,6 @@ size_t carve(void* base, int64_t B, int64_t Hkv, int64_t maxL, int64_t G, int64_
   return o;
 }
 
-// Programmatic dependent launch: let the next kernel in the stream start its prologue /
-// wait until the previous kernel's results are visible.
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-// Launch `kern` as a programmatic dependent of the previous kernel in the stream: it may
-// start while that kernel finishes and must call pdl_wait() before reading its results.
-template <typename... KArgs, typename... Args>
-int launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                     const char* name, Args&&... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-  if (e != cudaSuccess) return fail(SA_ELAUNCH, std::string(name) + ": " + cudaGetErrorString(e));
-  return check_launch(name);
-}
-
 // ---------------------------------------------------------------------------------------
 // 1-2. page selection and chunking
 // ---------------------------------------------------------------------------------------

@@ -17,6 +17,8 @@ struct SchedArgs {
   PlanHeader* header;       // null: static round-robin over `items`
   const WorkEntry* queue;
   int64_t items;
+  int first_static;         // 1: each CTA's first entry is item blockIdx.x (not in the queue),
+                            // taken before waiting for the planner (a PDL prerequisite)
 };
 
 __device__ __forceinline__ WorkEntry no_work() { return WorkEntry{-1, 0, 0, -1}; }
@@ -31,12 +33,22 @@ struct WorkFetcher {
   WorkEntry e_next;
   uint32_t w;
   bool reserved;
+  bool waited;
 
   template <typename WeightFn>
   __device__ __forceinline__ void reserve(WeightFn&& weight) {
     if (reserved) return;
     reserved = true;
-    if (s->header) {
+    if (s->header && s->first_static && w == 0) {
+      // first wave: item = CTA index, while the planner (this grid's programmatic
+      // prerequisite) still orders the rest
+      e_next = (int64_t)blockIdx.x < s->items ? WorkEntry{(int)blockIdx.x, 0, weight(blockIdx.x), -1}
+                                              : no_work();
+    } else if (s->header) {
+      if (s->first_static && !waited) {
+        pdl_wait();  // the planner's queue and header are complete from here on
+        waited = true;
+      }
       const int idx = atomicAdd(&s->header->counter, 1);
       e_next = idx < s->header->n_entries ? s->queue[idx] : no_work();
     } else {
@@ -50,6 +62,7 @@ struct WorkFetcher {
     s = args;
     w = 0;
     reserved = false;
+    waited = false;
     reserve(weight);
   }
 
