@@ -619,6 +619,66 @@ def run_c5(dev, rank, world, steps, warmup, flush, barrier=None):
     return res
 
 
+C4 = dict(Z=4, H=4, Hkv=1, N=32768, D=128, RB=128, levels=8, depth=(3, 4, 4, 4), layers=32)
+
+
+def run_c4(dev, rank, world, warmup, flush, barrier=None):
+    """C4 Llama-3.1-8B-shaped surgery prefill, the attention sublayer on one GPU's KV group:
+    batch 4, N=32768, 4 query heads / 1 KV head, D=128, route_block 128 (NB=256), 32 layers,
+    bf16, random init.  Per layer: that layer's Q/K/V and fresh random block routes (levels 8,
+    arity 2: a stand-in for the random-init router's per-block majority vote), then
+    build_block_lists(per-head depth 3/4/4/4, causal, sink, one local block) and the
+    block-list forward.  Depth r keeps ~2^-r of the causal triangle (plus sink and diagonal),
+    ~10 % on average over the four heads.  One step = all 32 layers; time = max over ranks."""
+    from ultrametric import build_block_lists
+    from ultrametric.block_list import _fwd
+    Z, H, Hkv, N, D, RB, L = (C4[k] for k in ("Z", "H", "Hkv", "N", "D", "RB", "layers"))
+    NB = N // RB
+    g = torch.Generator(device=dev).manual_seed(400 + rank)
+    layers = []
+    for _ in range(L):
+        layers.append((torch.randn(Z, H, N, D, generator=g, device=dev, dtype=torch.bfloat16),
+                       torch.randn(Z, Hkv, N, D, generator=g, device=dev, dtype=torch.bfloat16),
+                       torch.randn(Z, Hkv, N, D, generator=g, device=dev, dtype=torch.bfloat16),
+                       torch.randint(0, 2, (Z, H, NB, C4["levels"]), generator=g, device=dev,
+                                     dtype=torch.int32)))
+    scale = 1.0 / math.sqrt(D)
+    depth = torch.tensor(C4["depth"], dtype=torch.int32, device=dev)
+
+    def step(collect=None):
+        for q, k, v, routes in layers:
+            bl = build_block_lists(routes, depth, is_causal=True, sink_block=True,
+                                   local_blocks=1, arity=2)
+            _fwd(q, k, v, bl.lists, bl.counts, RB, True, scale, True, None)
+            if collect is not None:
+                collect.append(bl.counts.sum())
+
+    counts = []
+    for _ in range(max(1, warmup)):
+        step(counts if not counts else None)
+    kept = int(torch.stack(counts).sum())
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    flush_l2(flush)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    step()
+    e1.record()
+    e1.synchronize()
+    ms = max_over_ranks([e0.elapsed_time(e1)], world, dev)[0]
+    causal_pairs = Z * H * NB * (NB + 1) // 2 * L
+    return {"config": "C4: Llama-3.1-8B-shaped attention sublayer per GPU, batch 4, N=32768, "
+                      "H=4/1 per GPU, D=128, RB=128, 32 layers, random block routes, per-head "
+                      "depth 3/4/4/4, causal + sink + local",
+            "layers": L, "ms_all_layers": round(ms, 3), "ms_per_layer": round(ms / L, 4),
+            "kept_blocks_all_layers": kept,
+            "density_causal": round(kept / causal_pairs, 4),
+            "kept_tflops": round(kept * 4 * RB * RB * D / (ms * 1e-3) / 1e12, 2),
+            "whole_job_kept_tflops": round(world * kept * 4 * RB * RB * D / (ms * 1e-3) / 1e12, 2),
+            "timed": "per layer: list build + forward (router projection not included)"}
+
+
 def run_ours(args):
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -673,6 +733,7 @@ def run_ours(args):
     if not args.quick:
         extras["sweep"] = run_sweep(dev, flush, steps=5)  # per GPU (rank 0's numbers)
         extras["c5"] = run_c5(dev, rank, world, max(3, args.steps // 2), args.warmup, flush, barrier)
+        extras["c4"] = run_c4(dev, rank, world, 1, flush, barrier)
         extras["decode"] = run_decode(dev, rank, args.steps, args.warmup, flush, peaks, world, barrier)
     if world > 1:
         import torch.distributed as dist

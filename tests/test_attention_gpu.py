@@ -178,6 +178,35 @@ def test_tcgen05_forward_vs_oracle(Z, H, Hkv, N, D, RB, depth, causal, sink, loc
     assert torch.equal(out, out2), "storing the LSE changed the output"
 
 
+@pytest.mark.parametrize("D,dtype,causal", [(128, torch.bfloat16, False), (64, torch.float16, False),
+                                             (128, torch.float16, True), (64, torch.bfloat16, True)])
+def test_tcgen05_forward_one_tile_items(D, dtype, causal):
+    """Lists of 0-3 blocks per query block in a pattern that gives runs of one-tile work items
+    (finished by one softmax group alone, alternating groups) between longer items (both
+    groups, merged) and empty ones."""
+    Z, H, Hkv, RB, NB = 1, 4, 2, 128, 40
+    N = NB * RB - 37  # a ragged tail
+    gen = torch.Generator().manual_seed(D + 3)
+    q = randn((Z, H, N, D), gen).to(dtype)
+    k = randn((Z, Hkv, N, D), gen).to(dtype)
+    v = randn((Z, Hkv, N, D), gen).to(dtype)
+    m = torch.zeros(Z, H, NB, NB, dtype=torch.bool)
+    for h in range(H):
+        for i in range(NB):
+            n = (1, 1, 1, 2, 1, 0, 3, 1, 1)[(i * 5 + h) % 9]
+            hi = i + 1 if causal else NB
+            cols = torch.randperm(hi, generator=gen)[:n]
+            if causal and n > 0:
+                cols[0] = i  # keep the diagonal so that causal rows see a key
+            m[0, h, i, cols] = True
+    bl = build_block_lists_from_mask(m.to(DEV))
+    out, lse = block_list_attention(q.to(DEV), k.to(DEV), v.to(DEV), bl, route_block=RB,
+                                    is_causal=causal, return_lse=True)
+    ref, ref_lse = oracle_fwd(q.float(), k.float(), v.float(), bl, RB, causal)
+    assert_half_close(out, ref, "out")
+    lse_close(lse, ref_lse, 2e-2)
+
+
 def test_tcgen05_forward_bias_empty_rows_and_strides():
     Z, H, N, D, RB = 1, 4, 640, 128, 128
     gen = torch.Generator().manual_seed(5)
