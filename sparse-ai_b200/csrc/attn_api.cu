@@ -214,19 +214,18 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
 
   if (phase < 0 || phase > 3) return fail(SA_EINVAL, "backward phase must be 0..3");
   if (phase == 0 || phase == 1) {
-    // Delta (HBM-bound, a wide grid) runs on the caller's stream; the dQ planner, the
-    // transposition and the dK/dV planner (small, latency-bound, independent of Delta) on a
-    // high-priority second stream beside it.  The caller's stream waits for both.
+    // Delta (HBM-bound, a wide grid) runs on the caller's stream; the transposition and the
+    // dK/dV planner (small, latency-bound, independent of Delta) on a high-priority second
+    // stream beside it.  The caller's stream waits for both.  (The dQ planner runs with the
+    // dQ kernel, under its first wave.)
     cudaStream_t side;
     cudaEvent_t fork, join;
     rc = side_stream(&side, &fork, &join);
     if (rc) return rc;
     if (cudaEventRecord(fork, s) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
       return check_launch("backward fork");
-    rc = plan_bwd_sm100(p, side, kBwdDq);
-    if (!rc)
-      rc = launch_transpose_lists(lists, list_stride, counts, Z * H, NB, NB, k_lists, NB,
-                                  q_counts, k_slots, 0, side);
+    rc = launch_transpose_lists(lists, list_stride, counts, Z * H, NB, NB, k_lists, NB,
+                                q_counts, k_slots, 0, side);
     if (!rc) rc = plan_bwd_sm100(p, side, kBwdDkDv);
     if (cudaEventRecord(join, side) != cudaSuccess) return check_launch("backward join");
     if (!rc) rc = launch_delta(p, s);

@@ -789,16 +789,25 @@ int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
     a.tiles = (p.N + kRows - 1) / kRows;
     const int64_t items = a.Z * a.H * a.tiles;
     const int ctas = (int)std::min<int64_t>(items, sms);
-    a.sched = SchedArgs{nullptr, nullptr, items};
-    if (p.plan_dq) {
-      const PlanPtrs pp = plan_carve(p.plan_dq, kPlanDq, items, ctas, D);
-      a.sched = SchedArgs{pp.header, pp.queue, items};
-    }
+    a.sched = SchedArgs{nullptr, nullptr, items, 0};
     auto kern = bwd_dq_sm100_kernel<D, BF16>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DqLayout<D>::kAlloc);
-    kern<<<(unsigned)ctas, kBwdThreads, DqLayout<D>::kAlloc, stream>>>(a);
-    int e = check_launch("bwd_dq_sm100_kernel");
-    if (e) return e;
+    if (p.plan_dq) {
+      // As in the forward: each CTA's first item is its own index (late query tiles first);
+      // the planner, launched just before with this kernel as its programmatic dependent,
+      // queues the rest heaviest-first while that first wave runs.
+      const PlanPtrs pp = plan_carve(p.plan_dq, kPlanDq, items, ctas, D);
+      int e = launch_plan(kPlanDq, p, items, ctas, pp, stream, ctas);
+      if (e) return e;
+      a.sched = SchedArgs{pp.header, pp.queue, items, 1};
+      e = launch_dependent(kern, dim3((unsigned)ctas), dim3(kBwdThreads), DqLayout<D>::kAlloc,
+                           stream, "bwd_dq_sm100_kernel", a);
+      if (e) return e;
+    } else {
+      kern<<<(unsigned)ctas, kBwdThreads, DqLayout<D>::kAlloc, stream>>>(a);
+      int e = check_launch("bwd_dq_sm100_kernel");
+      if (e) return e;
+    }
   }
   if (parts & kBwdDkDv) {
     int rc = make_tmap_4d(&a.tm_q, p.q, p.dtype, p.Z, p.H, p.N, D, p.qs, 64, kSub);
@@ -809,11 +818,11 @@ int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
     a.tiles = (p.N + kRows - 1) / kRows;
     const int64_t items = a.Z * a.Hkv * a.tiles;
     const int ctas = (int)std::min<int64_t>(items, sms);
-    a.sched = SchedArgs{nullptr, nullptr, items};
+    a.sched = SchedArgs{nullptr, nullptr, items, 0};
     PlanPtrs pp{};
     if (p.plan_dkdv) {
       pp = plan_carve(p.plan_dkdv, kPlanDkdv, items, ctas, D);
-      a.sched = SchedArgs{pp.header, pp.queue, items};
+      a.sched = SchedArgs{pp.header, pp.queue, items, 0};
       a.partials = pp.partials;
     }
     auto kern = bwd_dkdv_sm100_kernel<D, BF16>;
