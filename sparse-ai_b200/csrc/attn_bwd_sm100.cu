@@ -46,7 +46,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 128, kColAcc = 256;  // S[2]: 0/64, dP[2]: 128/192
 
 struct BwdArgs {
-  CUtensorMap tm_q, tm_do, tm_k, tm_v;
+  CUtensorMap tm_q, tm_do, tm_k, tm_v, tm_dq;
   int64_t Z, H, Hkv, N, RB, NB, tiles;
   const int32_t* lists;
   int64_t list_stride;
@@ -145,15 +145,17 @@ struct DqLayout {
   static constexpr uint32_t kDO = kRows * D * 2;             // [128][D]
   static constexpr uint32_t kKV = 2 * kRows * D * 2;         // stages x (K [64][D], V [64][D])
   static constexpr uint32_t kStage = 2 * kSub * D * 2;
-  static constexpr uint32_t kBars = kKV + kStages * kStage;
+  static constexpr uint32_t kOut = kKV + kStages * kStage;  // dQ staging: D/64 boxes [128][64]
+  static constexpr uint32_t kBars = kOut + kRows * D * 2;
   static constexpr uint32_t kMeta = kBars + 256;  // StageMeta[kStages]
   static constexpr uint32_t kRingOff = kMeta + 128;  // WorkEntry[kRing]
   static constexpr uint32_t kAlloc = kRingOff + 128 + 1024;
+  static_assert(kAlloc <= 232448, "dQ shared-memory layout too large");
 };
 
 enum { DQ_QFULL = 0, DQ_QEMPTY, DQ_KVFULL0, DQ_KVEMPTY0 = DQ_KVFULL0 + kStages,
        DQ_SFULL0 = DQ_KVEMPTY0 + kStages, DQ_DSFULL0 = DQ_SFULL0 + 2, DQ_DONE = DQ_DSFULL0 + 2,
-       DQ_WFULL0,
+       DQ_OFULL, DQ_ODRAIN, DQ_WFULL0,
        DQ_WEMPTY0 = DQ_WFULL0 + kRing, DQ_NUM = DQ_WEMPTY0 + kRing };
 
 struct DqItem {
@@ -196,6 +198,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
     uint32_t cnt[DQ_NUM];
     for (int i = 0; i < DQ_NUM; ++i) cnt[i] = 1;
     cnt[DQ_DSFULL0] = cnt[DQ_DSFULL0 + 1] = kEwThreads / 2;  // one group per buffer
+    cnt[DQ_OFULL] = kEwThreads;  // the dQ tile is staged for its TMA store
     for (int i = 0; i < kRing; ++i) cnt[DQ_WEMPTY0 + i] = 1 + kEwThreads;
     init_bars(bars, cnt, DQ_NUM);
   }
@@ -325,7 +328,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
     const int rl = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const float scale2 = a.scale * kLog2e;
-    uint32_t s_it = 0, done_it = 0, kv = 0;
+    const bool issuer = warp == 2 && lane == 0;  // issues the dQ tile stores
+    uint32_t s_it = 0, done_it = 0, kv = 0, n_store = 0, n_drain = 0;
     bool ok = true;
     for (uint32_t w = 0; ok; ++w) {
       WorkEntry e;
@@ -395,11 +399,60 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dq_sm100_kernel(const __gr
         ++done_it;
         tc_fence_after();
       }
-      store_cols<D / 2>(a.dq, a.dqs, it.z, it.h, row, grp * (D / 2),
-                        lane_addr + kColAcc + grp * (D / 2), BF16, row < a.N, n_sub == 0);
+      // dQ tile -> shared memory (128-byte swizzled 128 x 64 boxes; each group its D/2
+      // columns) -> one TMA tile store per box.  The staging buffer is rewritten only after
+      // the previous item's store has read it.
+      if (n_store > n_drain) {
+        if (issuer) {
+          tma_store_wait_read();
+          mbar_arrive(&bars[DQ_ODRAIN]);
+        }
+        if (!(ok = mbar_wait_warp(&bars[DQ_ODRAIN], n_drain & 1, a.status))) break;
+        ++n_drain;
+      }
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        const int col = grp * (D / 2) + c * 32;
+        float o[32];
+        if (n_sub > 0) {
+          tmem_ld32(lane_addr + kColAcc + col, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        unsigned char* box = sm + L::kOut + (col >> 6) * (kRows * 128);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const int unit = ((col & 63) >> 3) + v;
+          const uint32_t off = rl * 128 + ((unit ^ (rl & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(box + off)),
+                       "r"(pack2(o[v * 8 + 0], o[v * 8 + 1], BF16)),
+                       "r"(pack2(o[v * 8 + 2], o[v * 8 + 3], BF16)),
+                       "r"(pack2(o[v * 8 + 4], o[v * 8 + 5], BF16)),
+                       "r"(pack2(o[v * 8 + 6], o[v * 8 + 7], BF16))
+                       : "memory");
+        }
+      }
+      fence_proxy_async_smem();
       tc_fence_before();
+      mbar_arrive(&bars[DQ_OFULL]);
+      if (issuer) {
+        if (mbar_wait(&bars[DQ_OFULL], n_store & 1, a.status)) {
+          for (int b = 0; b < D / 64; ++b)
+            tma_store_4d(&a.tm_dq, sm + L::kOut + b * (kRows * 128), b * 64, (int)it.q_start,
+                         (int)it.h, (int)it.z);
+        } else {
+          ok = false;
+        }
+      }
+      __syncwarp();
+      ok = __all_sync(0xffffffffu, ok);
+      ++n_store;
     }
   }
+  // dQ stores still in flight must have read the staging buffer before shared memory goes away
+  if (warp == 2 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -785,6 +838,7 @@ int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
     if (!rc) rc = make_tmap_4d(&a.tm_do, p.dout, p.dtype, p.Z, p.H, p.N, D, p.dos, 64, kRows);
     if (!rc) rc = make_tmap_4d(&a.tm_k, p.k, p.dtype, p.Z, p.Hkv, p.N, D, p.ks, 64, kSub);
     if (!rc) rc = make_tmap_4d(&a.tm_v, p.v, p.dtype, p.Z, p.Hkv, p.N, D, p.vs, 64, kSub);
+    if (!rc) rc = make_tmap_4d(&a.tm_dq, p.dq, p.dtype, p.Z, p.H, p.N, D, p.dqs, 64, kRows);
     if (rc) return fail(SA_ELAUNCH, std::string("dQ tensor maps: ") + sa_last_error());
     a.tiles = (p.N + kRows - 1) / kRows;
     const int64_t items = a.Z * a.H * a.tiles;
