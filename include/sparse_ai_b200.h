@@ -49,7 +49,8 @@ extern "C" {
 /* Message of the calling thread's last failed call ("" if none). */
 SA_API const char* sa_last_error(void);
 
-/* ABI version of this library (bumped on any signature change). */
+/* ABI version of this library (bumped on any signature change; 3: the accumulating
+ * forward takes the forward's optional workspace). */
 SA_API int sa_abi_version(void);
 
 /* Read the current device's status word (synchronises the device).  Kernels OR in
@@ -134,8 +135,9 @@ SA_API int sa_block_list_attention_fwd(int dtype, int64_t Z, int64_t H, int64_t 
  * ring), and are updated in place to the result over both key sets -- the online softmax
  * resumes from that state, so no separate merge pass runs.  Rows with no listed block keep
  * their values.  No soft bias; tensor-core path only (bf16/fp16, head_dim 64/128,
- * route_block a multiple of 128, 16-byte aligned rows), else SA_EUNSUPPORTED.  No
- * counterpart in the reference (it has no sequence parallelism; block_list.py:467-470 is
+ * route_block a multiple of 128, 16-byte aligned rows), else SA_EUNSUPPORTED.  The
+ * optional workspace is the forward's (sa_block_list_attention_fwd_workspace_bytes; NULL:
+ * static round-robin schedule).  No counterpart in the reference (it has no sequence parallelism; block_list.py:467-470 is
  * the LSE this consumes).
  */
 SA_API int sa_block_list_attention_fwd_accumulate(int dtype, int64_t Z, int64_t H, int64_t Hkv,
@@ -146,7 +148,8 @@ SA_API int sa_block_list_attention_fwd_accumulate(int dtype, int64_t Z, int64_t 
                                                   void* out, const int64_t* out_strides, float* lse,
                                                   const int32_t* lists, int64_t list_stride,
                                                   const int32_t* counts, int is_causal,
-                                                  float sm_scale, void* stream);
+                                                  float sm_scale, void* workspace,
+                                                  int64_t workspace_bytes, void* stream);
 
 /* Bytes of (optional) workspace for sa_block_list_attention_fwd, on the current device. */
 SA_API int64_t sa_block_list_attention_fwd_workspace_bytes(int64_t Z, int64_t H, int64_t N,

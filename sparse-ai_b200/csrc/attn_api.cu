@@ -104,6 +104,7 @@ int sa_block_list_attention_fwd_accumulate(int dtype, int64_t Z, int64_t H, int6
                                            const int64_t* out_strides, float* lse,
                                            const int32_t* lists, int64_t list_stride,
                                            const int32_t* counts, int is_causal, float sm_scale,
+                                           void* workspace, int64_t workspace_bytes,
                                            void* stream) {
   using namespace sa;
   AttnParams p{};
@@ -120,6 +121,13 @@ int sa_block_list_attention_fwd_accumulate(int dtype, int64_t Z, int64_t H, int6
   if (Z * H * N == 0) return SA_OK;
   if (!q || !k || !v || !out || !lse || !lists || !counts)
     return fail(SA_EINVAL, "null pointer argument (accumulate needs out and lse)");
+  if (workspace) {
+    if (reinterpret_cast<uintptr_t>(workspace) % 256)
+      return fail(SA_EINVAL, "workspace must be 256-byte aligned");
+    if (workspace_bytes < fwd_plan_bytes(Z, H, N, D))
+      return fail(SA_EWORKSPACE, "forward workspace too small");
+    p.plan_fwd = workspace;
+  }
   rc = launch_fwd_sm100(p, (cudaStream_t)stream);
   if (rc == SA_EUNSUPPORTED)
     return fail(SA_EUNSUPPORTED, "accumulating forward: needs the tensor-core path (bf16/fp16, "

@@ -135,7 +135,7 @@ extern "C" {
 
 const char* sa_last_error(void) { return sa::t_last_error.c_str(); }
 
-int sa_abi_version(void) { return 2; }
+int sa_abi_version(void) { return 3; }
 
 // Read (and optionally clear) the current device's status word.  Synchronises the device.
 int sa_read_device_status(int reset, unsigned* value) {

@@ -62,7 +62,8 @@ _SIGNATURES = {
                                              _i64, _i32, _vp, _p64, _vp]),
     "sa_block_list_attention_fwd_accumulate": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _i64,
                                                       _vp, _p64, _vp, _p64, _vp, _p64, _vp, _p64,
-                                                      _vp, _vp, _i64, _vp, _i32, _f32, _vp]),
+                                                      _vp, _vp, _i64, _vp, _i32, _f32, _vp, _i64,
+                                                      _vp]),
     "sa_attention_lse_merge": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _p64, _vp, _vp, _vp,
                                       _i32, _vp, _p64, _vp]),
 }

@@ -133,21 +133,23 @@ class RingPlan:
                                       src, to_rows(need) if need.numel() else None))
 
 
-def _fwd_direct(q, k, v, lists, counts, route_block, is_causal, scale, out, lse, accumulate):
-    """The forward into (out, lse), or continuing from them; static schedule (no planner)."""
+def _fwd_direct(q, k, v, lists, counts, route_block, is_causal, scale, out, lse, accumulate, ws):
+    """The forward into (out, lse), or continuing from them, with the planner workspace ``ws``
+    (heaviest-first work queue; None: static round-robin schedule)."""
     Z, H, N, D = q.shape
+    wp, wn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
     if accumulate:
         nat.check(nat.lib().sa_block_list_attention_fwd_accumulate(
             nat.float_code(q.dtype), Z, H, k.shape[1], N, D, route_block, q.data_ptr(), nat.strides(q),
             k.data_ptr(), nat.strides(k), v.data_ptr(), nat.strides(v), out.data_ptr(), nat.strides(out),
             lse.data_ptr(), lists.data_ptr(), lists.shape[-1], counts.data_ptr(), int(bool(is_causal)),
-            float(scale), nat.stream_of(q)), "accumulating forward")
+            float(scale), wp, wn, nat.stream_of(q)), "accumulating forward")
     else:
         nat.check(nat.lib().sa_block_list_attention_fwd(
             nat.float_code(q.dtype), Z, H, k.shape[1], N, D, route_block, q.data_ptr(), nat.strides(q),
             k.data_ptr(), nat.strides(k), v.data_ptr(), nat.strides(v), out.data_ptr(), nat.strides(out),
             lse.data_ptr(), lists.data_ptr(), lists.shape[-1], counts.data_ptr(), None, 0, None,
-            int(bool(is_causal)), float(scale), None, 0, nat.stream_of(q)), "forward")
+            int(bool(is_causal)), float(scale), wp, wn, nat.stream_of(q)), "forward")
 
 
 def _accumulate_ok(q: torch.Tensor, route_block: int) -> bool:
@@ -211,6 +213,7 @@ def ring_block_list_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
     first = True
     chunk_k = chunk_v = None
+    ws = None
     n_hops = len(plan.hops)
     for i, (c, causal, sub, cnt) in enumerate(plan.hops):
         last = i == n_hops - 1
@@ -232,7 +235,11 @@ def ring_block_list_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
             chunk_v.index_copy_(2, need, buf[1])
             kc, vc = chunk_k, chunk_v
         if accumulate:
-            _fwd_direct(q, kc, vc, sub, cnt, route_block, causal, scale, out, lse, not first)
+            if ws is None:
+                ws_bytes = int(nat.lib().sa_block_list_attention_fwd_workspace_bytes(
+                    Z, H, Nl, D, route_block))
+                ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)
+            _fwd_direct(q, kc, vc, sub, cnt, route_block, causal, scale, out, lse, not first, ws)
         else:
             o_j, lse_j = attn(q, kc, vc, sub, cnt, route_block, causal, scale)
             merge(o_j, lse_j, first, out if last else None)
@@ -273,7 +280,12 @@ def ring_emulate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_lists:
             sub, cnt = chunk_lists(block_lists.lists, block_lists.counts, rank * nbl,
                                    (rank + 1) * nbl, c * nbl, (c + 1) * nbl)
             if acc:
-                _fwd_direct(qr, kr, vr, sub, cnt, route_block, causal, scale, out, lse, i > 0)
+                # odd ranks without a planner workspace: both schedules stay exercised
+                ws = None
+                if rank % 2 == 0:
+                    ws = torch.empty(max(int(nat.lib().sa_block_list_attention_fwd_workspace_bytes(
+                        Z, H, Nl, D, route_block)), 256), dtype=torch.uint8, device=q.device)
+                _fwd_direct(qr, kr, vr, sub, cnt, route_block, causal, scale, out, lse, i > 0, ws)
             else:
                 o_j, lse_j = _attn_cuda(qr, kr, vr, sub, cnt, route_block, causal, scale)
                 merge(o_j, lse_j, i == 0, out if i == len(hops) - 1 else None)

@@ -35,7 +35,7 @@ def test_header_symbols_exported():
 
 def test_abi_version_and_workspace_sizes():
     lib = nat.lib()
-    assert lib.sa_abi_version() == 2
+    assert lib.sa_abi_version() == 3
     ws = lib.sa_block_list_attention_bwd_workspace_bytes(1, 32, 8, 8192, 128, 128)
     assert lib.sa_block_list_attention_fwd_workspace_bytes(1, 32, 8192, 128, 128) > 0
     NB = 64
