@@ -58,6 +58,8 @@ constexpr int kStreamThreads = 32 * (3 + kCw);  // + producer, epilogue and sche
 constexpr int kSchedWarp = 2 + kCw;
 constexpr int kMaxG = 16;           // MMA rows = query heads of a group
 constexpr int kMaxStages = 8;
+constexpr int kQBufs = 4;   // query buffers: the producer may run 3 chunks ahead of the consumers
+constexpr int kDescs = 4;   // chunk descriptors: the scheduler reserves up to 3 chunks ahead
 constexpr int kFirst = 1, kLast = 2, kEnd = 4;
 
 struct DecHeader {
@@ -437,27 +439,27 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   constexpr int KC = D / 64;
   constexpr uint32_t kHalf = kTile * D * 2;  // K (or V) bytes of one stage
   constexpr uint32_t kStage = 2 * kHalf;
-  constexpr uint32_t kQBuf = kMaxG * D * 2;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int stages = a.stages, G = a.G;
   constexpr int RS = D + 4;  // state / partial row: m, l, 0, 0, acc[D]
+  const uint32_t kQBuf = (uint32_t)G * D * 2;  // one chunk's G query rows (a multiple of 128 B)
   unsigned char* ring = sm;
-  unsigned char* qbuf = sm + stages * kStage;  // 2 x [16][D]
-  float* mbuf = reinterpret_cast<float*>(qbuf + 2 * kQBuf);  // 2 x [kCw][G][RS]
+  unsigned char* qbuf = sm + stages * kStage;  // kQBufs x [G][D]
+  float* mbuf = reinterpret_cast<float*>(qbuf + kQBufs * kQBuf);  // 2 x [kCw][G][RS]
   TileMeta* meta = reinterpret_cast<TileMeta*>(mbuf + 2 * kCw * G * RS);
   uint64_t* full = reinterpret_cast<uint64_t*>(meta + stages);
   uint64_t* empty = full + stages;
   uint64_t* qfull = empty + stages;
-  uint64_t* qempty = qfull + 2;
-  uint64_t* mfull = qempty + 2;
+  uint64_t* qempty = qfull + kQBufs;
+  uint64_t* mfull = qempty + kQBufs;
   uint64_t* mempty = mfull + 2;
   int* einfo = reinterpret_cast<int*>(mempty + 2);   // [2] chunk handed to the epilogue warp
   int2* s_sel = reinterpret_cast<int2*>(einfo + 4);  // [32] producer's page batch
-  ChunkDesc* desc = reinterpret_cast<ChunkDesc*>(s_sel + 32);  // [2] scheduler -> producer
-  uint64_t* dfull = reinterpret_cast<uint64_t*>(desc + 2);
-  uint64_t* dempty = dfull + 2;
+  ChunkDesc* desc = reinterpret_cast<ChunkDesc*>(s_sel + 32);  // [kDescs] scheduler -> producer
+  uint64_t* dfull = reinterpret_cast<uint64_t*>(desc + kDescs);
+  uint64_t* dempty = dfull + kDescs;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -465,24 +467,21 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kCw);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kQBufs; ++i) {
       mbar_init(&qfull[i], 1);
       mbar_init(&qempty[i], kCw);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&mfull[i], kCw);
       mbar_init(&mempty[i], 1);
+    }
+    for (int i = 0; i < kDescs; ++i) {
       mbar_init(&dfull[i], 1);
       mbar_init(&dempty[i], 1);
     }
     fence_mbar_init();
     prefetch_tmap(&a.tm_k);
     prefetch_tmap(&a.tm_v);
-  }
-  // query rows >= G of both buffers stay zero (the bulk copies write rows < G only)
-  if (warp >= 1 && warp <= kCw) {
-    for (int i = threadIdx.x - 32; i < 2 * kMaxG * D * 2 / 16; i += kCw * 32) {
-      const int row = (i % (kMaxG * D * 2 / 16)) / (D * 2 / 16);
-      if (row >= G) reinterpret_cast<uint4*>(qbuf)[i] = make_uint4(0, 0, 0, 0);
-    }
   }
   __syncthreads();
   pdl_wait();  // the selection kernel's lists, table and header are complete from here on
@@ -492,16 +491,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     uint32_t tile = 0, qi = 0;
     bool ok = true;
     for (uint32_t d = 0; ok; ++d) {
-      const uint32_t ds = d & 1;
-      if (!(ok = mbar_wait_warp(&dfull[ds], (d >> 1) & 1, a.status))) break;
+      const uint32_t ds = d % kDescs;
+      if (!(ok = mbar_wait_warp(&dfull[ds], (d / kDescs) & 1, a.status))) break;
       const ChunkDesc& cd = desc[ds];
       const int c = cd.chunk;
       if (c < 0) break;
       const int bg = cd.bg, p0 = cd.p0, p1 = cd.p1;
       const int64_t b = bg / a.Hkv, g = bg % a.Hkv;
       if (lane == 0) {
-        const uint32_t qb = qi & 1;
-        ok = mbar_wait(&qempty[qb], ((qi >> 1) & 1) ^ 1, a.status);
+        const uint32_t qb = qi % kQBufs;
+        ok = mbar_wait(&qempty[qb], ((qi / kQBufs) & 1) ^ 1, a.status);
         if (ok) {
           mbar_arrive_expect_tx(&qfull[qb], (uint32_t)(G * D * 2));
           const char* src = static_cast<const char*>(a.q) + (b * a.qs0 + g * G * a.qs1) * 2;
@@ -618,16 +617,19 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         break;
       }
       if (flags & kFirst) {
-        const uint32_t qb = qi & 1;
-        if (!mbar_wait_warp(&qfull[qb], (qi >> 1) & 1, a.status)) break;
-        const uint32_t* r0 = reinterpret_cast<const uint32_t*>(qbuf + qb * kQBuf + gq * D * 2);
-        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(qbuf + qb * kQBuf + (gq + 8) * D * 2);
+        const uint32_t qb = qi % kQBufs;
+        if (!mbar_wait_warp(&qfull[qb], (qi / kQBufs) & 1, a.status)) break;
+        // MMA rows >= G (no query head) are zero
+        const bool v0 = gq < G, v1 = gq + 8 < G;
+        const uint32_t* r0 = reinterpret_cast<const uint32_t*>(qbuf + qb * kQBuf + (v0 ? gq : 0) * D * 2);
+        const uint32_t* r1 =
+            reinterpret_cast<const uint32_t*>(qbuf + qb * kQBuf + (v1 ? gq + 8 : 0) * D * 2);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
-          qa[ks][0] = r0[ks * 8 + cq];
-          qa[ks][1] = r1[ks * 8 + cq];
-          qa[ks][2] = r0[ks * 8 + 4 + cq];
-          qa[ks][3] = r1[ks * 8 + 4 + cq];
+          qa[ks][0] = v0 ? r0[ks * 8 + cq] : 0u;
+          qa[ks][1] = v1 ? r1[ks * 8 + cq] : 0u;
+          qa[ks][2] = v0 ? r0[ks * 8 + 4 + cq] : 0u;
+          qa[ks][3] = v1 ? r1[ks * 8 + 4 + cq] : 0u;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&qempty[qb]);
@@ -758,14 +760,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
   } else if (warp == kSchedWarp) {
     // ---------------- scheduler: reserve the next chunk and fetch its entries ----------------
-    // One descriptor ahead of the producer: a CTA holds at most one reserved chunk that it
-    // has not started, so the queue still balances to within a chunk at its end.
+    // Up to kDescs - 1 descriptors ahead of the producer, so that runs of one-page chunks do
+    // not wait on the queue's atomic -> table -> list chain.  CTA x takes chunk x first; the
+    // queue counter hands out the rest from chunk gridDim.x on.
     const int n_chunks = __ldcg(&a.w.hdr->n_chunks);
     for (uint32_t d = 0;; ++d) {
-      const uint32_t ds = d & 1;
-      if (!mbar_wait_warp(&dempty[ds], ((d >> 1) & 1) ^ 1, a.status)) break;
+      const uint32_t ds = d % kDescs;
+      if (!mbar_wait_warp(&dempty[ds], ((d / kDescs) & 1) ^ 1, a.status)) break;
       int c = 0;
-      if (lane == 0) c = atomicAdd(&a.w.hdr->next, 1);
+      if (lane == 0) c = d == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(&a.w.hdr->next, 1);
       c = __shfl_sync(0xffffffffu, c, 0);
       ChunkDesc& cd = desc[ds];
       if (c >= n_chunks) {
@@ -882,8 +885,10 @@ template <int D, bool BF16>
 int launch_stream(StreamArgs& a, int grid, cudaStream_t stream) {
   constexpr size_t kStage = 2 * (size_t)kTile * D * 2;
   // alignment slack, query buffers, 2 merge buffers, then Q / merge barriers, hand-off
-  // records, the producer's page batch and the scheduler's 2 descriptors with barriers
-  const size_t fixed = 1024 + 2 * (size_t)kMaxG * D * 2 + 2 * (size_t)kCw * a.G * (D + 4) * 4 + 1024;
+  // records, the producer's page batch and the scheduler's descriptors with barriers
+  static_assert((2 * kQBufs + 4) * 8 + 16 + 32 * 8 + kDescs * (sizeof(ChunkDesc) + 16) <= 2048,
+                "decode: barrier and descriptor area");
+  const size_t fixed = 1024 + kQBufs * (size_t)a.G * D * 2 + 2 * (size_t)kCw * a.G * (D + 4) * 4 + 2048;
   const size_t per_stage = kStage + sizeof(TileMeta) + 16;
   const int stages = (int)std::min<size_t>(kMaxStages, (226 * 1024 - fixed) / per_stage);
   if (stages < 2) return fail(SA_EUNSUPPORTED, "decode: shared memory too small for the ring");
