@@ -48,7 +48,7 @@ constexpr int kMaxUnitChunks = 32;  // chunks per unit; bounds the final merge
 constexpr int kSelThreads = 256;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kSelTile = kSelThreads;  // pages per pass of the selection kernel
-constexpr int kSelSplitCtas = 320;     // selection CTAs aimed for (~2 per SM)
+constexpr int kSelSplitCtas = 296;     // selection CTAs at most: 2 resident per SM, one wave
 constexpr int kMaxParts = 16;          // parts per request
 constexpr int kMaxHeadWords = 4;       // query heads <= 128
 constexpr int kMaxHeads = kMaxHeadWords * 32;
@@ -67,8 +67,10 @@ struct DecHeader {
   int n_chunks;
   int chp;          // pages per chunk
   int next;         // queue counter of the stream kernel
-  int pad[60];
+  unsigned long long total;  // selected (unit, page) pairs, summed by the select CTAs
+  int pad[58];
 };
+static_assert(sizeof(DecHeader) == 256, "DecHeader");
 
 // A request's logical pages are selected in P parts of `seg` pages (one CTA each); part q of
 // unit bg writes its list at sel[bg][q * seg ...] and its length at count[bg][q].
@@ -114,7 +116,7 @@ inline size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // Parts per request: enough selection CTAs to cover the GPU, parts of >= 64 pages.
 int sel_parts(int64_t B, int64_t maxL) {
-  const int64_t want = (kSelSplitCtas + B - 1) / std::max<int64_t>(B, 1);
+  const int64_t want = kSelSplitCtas / std::max<int64_t>(B, 1);
   const int64_t cap = std::max<int64_t>(1, (maxL + 63) / 64);
   return (int)std::max<int64_t>(1, std::min<int64_t>({kMaxParts, want, cap}));
 }
@@ -157,6 +159,7 @@ __global__ void decode_init_kernel(DecHeader* hdr) {
   pdl_trigger();
   hdr->ticket = 0;
   hdr->next = 0;
+  hdr->total = 0;
 }
 
 // Exclusive prefix of v over the CTA (kSelThreads threads); *total gets the sum.
@@ -208,6 +211,17 @@ __global__ void __launch_bounds__(kSelThreads, 2) decode_select_kernel(const Dec
   __shared__ long long s_sum[kSelWarps];
   __shared__ int s_last;
   const int64_t ctx = p.ctx[b];
+  // Lanes run over the (head, level < r) pairs that are compared, KK words per lane and PP
+  // pages per step: the loads of one step (PP * KK per lane) are all in flight together.
+  constexpr int NST = 32 / PP;  // steps covered by one block-table load per lane
+  const int64_t lo = (int64_t)part * w.seg;
+  // Warp w takes a tile's pages s * 8PP + w * PP + [0, PP) in steps s < NST; one block-table
+  // load per lane covers all NST steps.  The first tile's load is issued with the context
+  // length's: it reads within the part and the table's width, and entries past the context
+  // are never used.
+  const int my_lt = (lane / PP) * (kSelWarps * PP) + warp * PP + (lane % PP);
+  int my_phys_next =
+      my_lt < min((int64_t)min(kSelTile, w.seg), p.maxL - lo) ? p.bt[b * p.bts[0] + (lo + my_lt) * p.bts[1]] : 0;
   for (int i = tid; i < H * r; i += kSelThreads) {
     const int h = i / r, lvl = i % r;
     s_qr[h][lvl] = (int32_t)load_any_i64(p.qrouter, p.qrouter_dtype,
@@ -217,19 +231,18 @@ __global__ void __launch_bounds__(kSelThreads, 2) decode_select_kernel(const Dec
   __syncthreads();
   // logical pages past the block table's width are not read (a consistent request has none)
   const int64_t nlog = ctx > 0 ? min((ctx + p.page - 1) / p.page, p.maxL) : 0;
-  // Lanes run over the (head, level < r) pairs that are compared, KK words per lane and PP
-  // pages per step: the loads of one step (PP * KK per lane) are all in flight together.
-  constexpr int NST = 32 / PP;  // steps covered by one block-table load per lane
   const int HR = H * r;
   uint8_t* mflag = s_miss[warp];
-  const int64_t lo = (int64_t)part * w.seg, hi = min(nlog, lo + w.seg);
+  const int64_t hi = min(nlog, lo + w.seg);
   const int64_t row = (int64_t)w.P * w.seg;  // one unit's list row
   for (int64_t t0 = lo; t0 < hi; t0 += kSelTile) {
     const int tn = (int)min((int64_t)kSelTile, hi - t0);
-    // ---- pass 1: head masks.  Warp w takes the tile's pages s * 8PP + w * PP + [0, PP) in
-    // steps s < NST; one block-table load per lane covers all NST steps.
-    const int my_lt = (lane / PP) * (kSelWarps * PP) + warp * PP + (lane % PP);
-    const int my_phys = my_lt < tn ? p.bt[b * p.bts[0] + (t0 + my_lt) * p.bts[1]] : 0;
+    // ---- pass 1: head masks
+    const int my_phys = my_phys_next;  // entries past tn are never used
+    if (t0 + kSelTile < hi) {
+      const int64_t nt = min((int64_t)kSelTile, hi - t0 - kSelTile);
+      my_phys_next = my_lt < nt ? p.bt[b * p.bts[0] + (t0 + kSelTile + my_lt) * p.bts[1]] : 0;
+    }
     for (int st = 0; st < NST; ++st) {
       const int lt = st * (kSelWarps * PP) + warp * PP;  // first page of this step
       if (lt >= tn) break;
@@ -318,27 +331,34 @@ __global__ void __launch_bounds__(kSelThreads, 2) decode_select_kernel(const Dec
     }
     __syncthreads();  // the tile's shared arrays are rewritten by the next tile
   }
-  for (int g = tid; g < Hkv; g += kSelThreads) w.count[(b * Hkv + g) * w.P + part] = s_run[g];
+  long long mine = 0;
+  for (int g = tid; g < Hkv; g += kSelThreads) {
+    w.count[(b * Hkv + g) * w.P + part] = s_run[g];
+    mine += s_run[g];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+  if (lane == 0) s_sum[warp] = mine;
 
-  // The last CTA to finish cuts the lists into chunks (the ticket was zeroed by the init
-  // kernel, which must have completed).
+  // The CTA adds its selected pairs to the header's total, then takes a ticket; the last CTA
+  // to finish cuts the lists into chunks (the header was zeroed by the init kernel, which
+  // must have completed).
   pdl_wait();
   __threadfence();
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&w.hdr->ticket, 1u) == gridDim.x * gridDim.y - 1;
+  if (tid == 0) {
+    long long cta = 0;
+    for (int i = 0; i < kSelWarps; ++i) cta += s_sum[i];
+    if (cta) atomicAdd(&w.hdr->total, (unsigned long long)cta);
+    __threadfence();
+    s_last = atomicAdd(&w.hdr->ticket, 1u) == gridDim.x * gridDim.y - 1;
+  }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   const int64_t BG = p.B * p.Hkv;
   const int P = w.P;
-  long long tot = 0;
-  for (int64_t i = tid; i < BG * P; i += kSelThreads) tot += __ldcg(w.count + i);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-  if ((tid & 31) == 0) s_sum[tid >> 5] = tot;
-  __syncthreads();
-  long long total = 0;
-  for (int i = 0; i < kSelThreads / 32; ++i) total += s_sum[i];
+  const long long total = (long long)__ldcg(&w.hdr->total);
   int chp = (int)std::max<long long>(ppt, (total + kChunkTarget - 1) / kChunkTarget);
   chp = (chp + ppt - 1) / ppt * ppt;
   int run = 0;
