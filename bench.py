@@ -553,8 +553,9 @@ def run_decode(dev, seed, steps, warmup, flush, peaks, world=1, barrier=None):
         "requests_per_gpu": B,
         "routed_gbs": round(gbs, 1), "routed_bytes": routed_bytes, "routed_pages": sel_pages,
         "dense_equivalent_bytes": dense_bytes,
-        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4)},
+        # per GPU (the slowest rank), against one GPU's measured copy bandwidth
+        "roofline": {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(gbs / world / peaks["hbm_gbs"], 4), "per": "GPU"},
         "gpu_launches_per_step": 4,
     }
 
