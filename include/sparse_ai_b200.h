@@ -59,6 +59,13 @@ SA_API int sa_abi_version(void);
  * reset != 0 clears it. */
 SA_API int sa_read_device_status(int reset, unsigned* value);
 
+/* Destroy the calling thread's side streams and events.  The backward's preparation phase
+ * runs its small kernels on a second, high-priority stream per host thread and device,
+ * created on first use and joined back into the caller's stream before each call returns;
+ * this releases them (e.g. before a worker thread exits).  Synchronises those streams.
+ * No counterpart in the reference (Triton keeps no such state). */
+SA_API int sa_release_thread_resources(void);
+
 /*
  * Routing vectors -> ascending active key-block lists.
  * Replaces: src/ultrametric/block_list.py:219-253 (mixed-radix prefix codes + launch of
@@ -256,7 +263,9 @@ SA_API int sa_ultrametric_decode(int dtype, int64_t B, int64_t H, int64_t Hkv, i
  * chunk table, partials) comes from a fixed 16 MiB device array inside the library (held by every GPU that loads it
  * until exit).  Requests needing more than 16 MiB of workspace return SA_EWORKSPACE.  The
  * first call on a device looks the array up (make it before any stream capture).  All
- * calls share the array: calls that overlap on the GPU race.  Allocates nothing.
+ * calls share the array: calls that overlap on the GPU race.  `stream` must belong to the
+ * current device, whose array is used (another device's stream: SA_EINVAL).  Allocates
+ * nothing.
  */
 SA_API int sa_ultrametric_decode_noalloc(int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t D,
                           int64_t page_size, int64_t num_pages,

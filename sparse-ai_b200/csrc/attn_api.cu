@@ -50,6 +50,7 @@ int fill_common(AttnParams& p, int dtype, int64_t Z, int64_t H, int64_t Hkv, int
   p.causal = causal;
   p.scale = scale;
   p.status = device_status_ptr();
+  if (!p.status) return fail(SA_ELAUNCH, std::string("attention: ") + sa_last_error());
   if (Z * H > 65535) return fail(SA_EUNSUPPORTED, "Z*H exceeds 65535");
   return SA_OK;
 }

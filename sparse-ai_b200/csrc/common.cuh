@@ -28,7 +28,16 @@ int check_launch(const char* what);
 enum : unsigned { kStatusWaitTimeout = 1u, kStatusBadIndex = 2u, kStatusSmemLayout = 4u };
 unsigned* device_status_ptr();
 
-__device__ __forceinline__ void raise_status(unsigned* st, unsigned bit) { atomicOr(st, bit); }
+// Launchers refuse to launch without a status word; the null check keeps a kernel that
+// got none anyway from faulting where it meant to report.
+__device__ __forceinline__ void raise_status(unsigned* st, unsigned bit) {
+  if (st) atomicOr(st, bit);
+}
+
+// SA_EINVAL unless `stream` (a cudaStream_t; NULL = legacy default stream) belongs to the
+// current device: per-device resources (status word, scratch) are looked up by the current
+// device, so the two must agree.
+int check_stream_device(void* stream, const char* what);
 
 // ---------------------------------------------------------------------------------------
 // element conversion

@@ -479,6 +479,8 @@ int sa_ultrametric_decode(int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t 
 //  * All calls share the one array: calls that overlap on the GPU (different streams, or
 //    different host threads) race on it.  The decode kernel rewrites every slot it reads
 //    in the same launch, so nothing needs clearing between calls.
+//  * `stream` must belong to the current device (the array is looked up for the current
+//    device); a stream of another device is rejected with SA_EINVAL.
 // ---------------------------------------------------------------------------------------
 #include <mutex>
 
@@ -499,6 +501,9 @@ void* decode_scratch_ptr() {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
     if (e != cudaSuccess) {
+      // clear the runtime's sticky last error, so that a later launch check does not
+      // report it against an unrelated kernel; the message is kept here
+      cudaGetLastError();
       set_error(std::string("decode scratch address: ") + cudaGetErrorString(e));
       return nullptr;
     }
@@ -525,6 +530,8 @@ int sa_ultrametric_decode_noalloc(int dtype, int64_t B, int64_t H, int64_t Hkv, 
                                   int64_t local_blocks, int sink_block, void* out,
                                   const int64_t* out_strides, void* stream) {
   using namespace sa;
+  // the scratch address is looked up for the current device, so the stream must be its own
+  if (int rc = check_stream_device(stream, "decode_noalloc")) return rc;
   if (H > 0 && Hkv > 0 && D > 0) {
     const int64_t need = sa_ultrametric_decode_workspace_bytes(B, H, Hkv, D, max_logical_pages);
     if (need > kNoAllocScratchBytes)

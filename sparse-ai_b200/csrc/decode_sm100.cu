@@ -948,6 +948,8 @@ int launch_decode_fast(const DecodeParams& p, int dtype, void* workspace, int64_
                                    " < " + std::to_string(need) + ")");
   if (p.B > 65535) return fail(SA_EUNSUPPORTED, "decode: more than 65535 requests");
   StreamArgs a{};
+  a.status = device_status_ptr();
+  if (!a.status) return fail(SA_ELAUNCH, std::string("decode: ") + sa_last_error());
   const uint32_t box_n = (uint32_t)std::min<int64_t>(p.page, kTile);
   int rc = make_tmap_4d(&a.tm_k, p.kc, dtype, p.num_pages, p.Hkv, p.page, p.D, p.ks, 64, box_n);
   if (!rc) rc = make_tmap_4d(&a.tm_v, p.vc, dtype, p.num_pages, p.Hkv, p.page, p.D, p.vs, 64, box_n);
@@ -985,7 +987,6 @@ int launch_decode_fast(const DecodeParams& p, int dtype, void* workspace, int64_
   a.ppt = ppt;
   a.scale2 = (1.0f / sqrtf((float)p.D)) * kLog2e;
   a.w = w;
-  a.status = device_status_ptr();
   const int grid = (int)std::min<int64_t>(device_sm_count(), max_chunks(BG, p.maxL, w.P));
   const bool bf = dtype == SA_BF16;
   if (p.D == 64)

@@ -34,26 +34,66 @@ unsigned* device_status_ptr() {
   static unsigned* ptrs[kMaxDevices] = {};
   static std::mutex mu;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("device status word: no current device");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("device status word: device index " + std::to_string(dev) + " out of range");
+    return nullptr;
+  }
   std::lock_guard<std::mutex> lock(mu);
   if (!ptrs[dev]) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_status_word) != cudaSuccess) return nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_device_status_word);
+    if (e != cudaSuccess) {
+      // keep the message, and clear the runtime's sticky last error so that a later
+      // check_launch does not report it against an unrelated kernel
+      cudaGetLastError();
+      set_error(std::string("device status word address: ") + cudaGetErrorString(e));
+      return nullptr;
+    }
     ptrs[dev] = static_cast<unsigned*>(p);
   }
   return ptrs[dev];
 }
 
+int check_stream_device(void* stream, const char* what) {
+  if (!stream) return SA_OK;  // the legacy default stream belongs to the current device
+  int dev = 0, sdev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SA_ELAUNCH, std::string(what) + ": no current device");
+  }
+  if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SA_EINVAL, std::string(what) + ": not a valid CUDA stream");
+  }
+  if (sdev != dev)
+    return fail(SA_EINVAL, std::string(what) + ": the stream belongs to device " +
+                               std::to_string(sdev) + " but the current device is " +
+                               std::to_string(dev) + "; make the stream's device current");
+  return SA_OK;
+}
+
 // A second stream (and a fork / join event pair) per host thread and device, created on
-// first use, for independent launches inside one entry point.  It has the highest stream
-// priority: its small latency-bound kernels get SM slots ahead of a wide kernel running
-// beside them on the caller's stream.
+// first use, for independent launches inside one entry point (the backward's preparation
+// phase).  It has the highest stream priority: its small latency-bound kernels get SM slots
+// ahead of a wide kernel running beside them on the caller's stream.  This is the library's
+// only host-side resource besides the read-only attribute caches; every entry point joins
+// the side stream back into the caller's stream before it returns, and
+// sa_release_thread_resources() destroys the calling thread's streams and events.
+namespace {
+struct Side {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+thread_local Side t_side[kMaxDevices];
+}  // namespace
+
 int side_stream(cudaStream_t* out, cudaEvent_t* fork, cudaEvent_t* join) {
-  struct Side {
-    cudaStream_t s = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
-  };
-  thread_local Side side[kMaxDevices];
+  Side* side = t_side;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(SA_ELAUNCH, "side stream: no current device");
@@ -136,6 +176,26 @@ extern "C" {
 const char* sa_last_error(void) { return sa::t_last_error.c_str(); }
 
 int sa_abi_version(void) { return 3; }
+
+// Destroy the side streams and events the calling thread created (one set per device it
+// used); the next backward call on this thread creates them again.  Synchronises each of
+// those streams first, so it must not be called while a capture uses them.
+int sa_release_thread_resources(void) {
+  int prev = 0;
+  const bool had_dev = cudaGetDevice(&prev) == cudaSuccess;
+  int rc = SA_OK;
+  for (int d = 0; d < sa::kMaxDevices; ++d) {
+    sa::Side& s = sa::t_side[d];
+    if (!s.s) continue;
+    if (cudaSetDevice(d) != cudaSuccess || cudaStreamSynchronize(s.s) != cudaSuccess ||
+        cudaStreamDestroy(s.s) != cudaSuccess || cudaEventDestroy(s.fork) != cudaSuccess ||
+        cudaEventDestroy(s.join) != cudaSuccess)
+      rc = sa::check_launch("release side stream");
+    s = sa::Side{};
+  }
+  if (had_dev) cudaSetDevice(prev);
+  return rc;
+}
 
 // Read (and optionally clear) the current device's status word.  Synchronises the device.
 int sa_read_device_status(int reset, unsigned* value) {

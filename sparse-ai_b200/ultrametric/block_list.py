@@ -21,6 +21,8 @@ own tiles.  There is no CPU or Triton path: non-CUDA tensors raise ``RuntimeErro
 
 from __future__ import annotations
 
+import warnings
+
 import math
 from typing import NamedTuple, Optional, Sequence, Union
 
@@ -194,8 +196,30 @@ def build_transposed_block_lists(
 # attention
 # ----------------------------------------------------------------------------------------
 
+_SIMT_WARNED = set()
+
+
+def _warn_if_simt(dtype, head_dim, route_block):
+    """The tensor-core (tcgen05) kernels take bf16/fp16 with head_dim 64 or 128 and a route
+    block that is a multiple of 128; other half-precision shapes run the CUDA-core kernels,
+    several times slower.  Say so once per shape instead of falling off that cliff quietly."""
+    if dtype not in (torch.float16, torch.bfloat16):
+        return
+    if head_dim in (64, 128) and route_block % 128 == 0:
+        return
+    key = (dtype, head_dim, route_block)
+    if key in _SIMT_WARNED:
+        return
+    _SIMT_WARNED.add(key)
+    warnings.warn(
+        f"block_list_attention: {str(dtype).replace('torch.', '')} with head_dim={head_dim} and "
+        f"route_block={route_block} runs on the CUDA-core kernels; the tensor-core path needs "
+        f"head_dim 64 or 128 and route_block a multiple of 128", RuntimeWarning, stacklevel=3)
+
+
 def _fwd(q, k, v, lists, counts, route_block, is_causal, scale, store_lse, soft_block_bias):
     Z, H, N, D = q.shape
+    _warn_if_simt(q.dtype, D, route_block)
     out = torch.empty_like(q)
     lse = torch.empty((Z, H, N), dtype=torch.float32, device=q.device) if store_lse else None
     sb = soft_block_bias

@@ -1,9 +1,14 @@
 """Routed sparse PagedAttention decode on B200 (sm_100a): the drop-in for sparse-ai's
 ``src/ultrametric/kernel_decode.py`` (``ultrametric_decode``, :188-247 there).
 
-One C-ABI call (``sa_ultrametric_decode``) runs a split-K kernel that gathers only the
-routed KV pages of each (request, KV head) with 16-byte loads, serves every query head of
-the GQA group from each loaded page, and merges the splits by log-sum-exp.  Differences
+One C-ABI call (``sa_ultrametric_decode``) selects the routed pages of every (request, KV
+head) and streams only those pages.  For bf16/fp16 caches with head_dim 64 or 128 (and page
+sizes 16, 32 or multiples of 64) it runs the sm_100a fast path (``csrc/decode_sm100.cu``):
+a selection kernel builds per-KV-head page lists and cuts them into balanced chunks, a
+persistent kernel streams each chunk's K/V tiles with TMA and serves every query head of
+the GQA group from each loaded tile, and a combine kernel merges the chunk partials by
+log-sum-exp.  Other shapes and fp32 take the general split-K kernel (``csrc/decode.cu``:
+16-byte ``cp.async`` loads, per-split online softmax, log-sum-exp merge).  Differences
 from the reference, all supersets: ``k_cache``/``v_cache`` may hold ``H // g`` KV heads
 (native GQA; the reference needs them expanded to H); a request with
 ``context_lens[b] == 0`` gets zeros (the reference kernel leaves ``torch.empty`` memory

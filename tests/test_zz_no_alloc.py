@@ -8,7 +8,9 @@ from a fixed device array inside the library instead.
 This file is collected last on purpose.  Both tests call the library through the C ABI
 (ctypes), the way such a caller would; the first compares the no-alloc entry point with
 ``sa_ultrametric_decode`` (caller workspace) on two calls in a row, which also checks that
-the shared array's leftover contents from the first call do not leak into the second.
+the shared array's leftover contents from the first call do not leak into the second.  It
+runs on the bf16 fast path (D=128, page 64) and on the general split-K path (fp32, and
+bf16 with D=32), both of which keep their partials in the shared array.
 """
 
 import ctypes
@@ -16,14 +18,14 @@ import ctypes
 import pytest
 import torch
 
-from helpers import assert_half_close
+from helpers import assert_fp32_close, assert_half_close
 from ultrametric import _native as nat
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def _inputs(seed, B=6, H=8, Hkv=2, D=128, page=64, TD=6):
+def _inputs(seed, B=6, H=8, Hkv=2, D=128, page=64, TD=6, dtype=torch.bfloat16):
     gen = torch.Generator().manual_seed(seed)
     ctx = torch.randint(1, 3000, (B,), generator=gen, dtype=torch.int32)
     ctx[0] = 0  # a request with no context
@@ -38,9 +40,9 @@ def _inputs(seed, B=6, H=8, Hkv=2, D=128, page=64, TD=6):
         bt[b, :n] = perm[off:off + n]
         off += n
     t = dict(
-        q=torch.randn(B, H, D, generator=gen).bfloat16(),
-        kc=torch.randn(total, Hkv, page, D, generator=gen).bfloat16(),
-        vc=torch.randn(total, Hkv, page, D, generator=gen).bfloat16(),
+        q=torch.randn(B, H, D, generator=gen).to(dtype),
+        kc=torch.randn(total, Hkv, page, D, generator=gen).to(dtype),
+        vc=torch.randn(total, Hkv, page, D, generator=gen).to(dtype),
         bt=bt, ctx=ctx,
         ri=torch.randint(0, 2, (total, H, TD), generator=gen, dtype=torch.int32),
         qri=torch.randint(0, 2, (B, H, TD), generator=gen, dtype=torch.int32),
@@ -52,7 +54,8 @@ def _common_args(t, out, req_depth=2, local_blocks=1, sink=1):
     q, kc, vc, bt, ctx, ri, qri = (t[k] for k in ("q", "kc", "vc", "bt", "ctx", "ri", "qri"))
     B, H, D = q.shape
     P, Hkv, page, _ = kc.shape
-    return [nat.SA_BF16, B, H, Hkv, D, page, P,
+    sa_dtype = {torch.bfloat16: nat.SA_BF16, torch.float16: nat.SA_F16, torch.float32: nat.SA_F32}[q.dtype]
+    return [sa_dtype, B, H, Hkv, D, page, P,
             q.data_ptr(), nat.strides(q), kc.data_ptr(), nat.strides(kc),
             vc.data_ptr(), nat.strides(vc), bt.data_ptr(), nat.strides(bt), bt.shape[1],
             ctx.data_ptr(), ri.data_ptr(), nat.SA_I32, nat.strides(ri),
@@ -78,13 +81,22 @@ def _no_alloc(t):
     return out
 
 
-def test_no_alloc_decode_matches_workspace_decode_twice():
+@pytest.mark.parametrize("dtype,D,page", [
+    (torch.bfloat16, 128, 64),  # fast path (decode_sm100.cu)
+    (torch.float32, 128, 64),   # general split-K path (decode.cu), fp32
+    (torch.bfloat16, 32, 16),   # general split-K path, a head_dim the fast path does not take
+])
+def test_no_alloc_decode_matches_workspace_decode_twice(dtype, D, page):
     for seed in (11, 12):  # two calls in a row, different inputs
-        t = _inputs(seed)
+        t = _inputs(seed, D=D, page=page, dtype=dtype)
         ref = _with_workspace(t)
         got = _no_alloc(t)
         torch.cuda.synchronize()
-        assert_half_close(got, ref.float(), f"no-alloc decode (call with seed {seed})")
+        what = f"no-alloc decode ({dtype}, D={D}, call with seed {seed})"
+        if dtype == torch.float32:
+            assert_fp32_close(got, ref, what)
+        else:
+            assert_half_close(got, ref.float(), what)
         assert (got[0] == 0).all()
     assert nat.read_device_status() == 0
 
