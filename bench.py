@@ -184,8 +184,10 @@ def cpu_reference_sample(heads=(0, 1), causal=True, sink=True, seed=0, t_heads=N
     return t1 - t0, len(heads)
 
 
-def kept_flops_c2(t_heads, causal, sink, fwd=True, bwd=True):
+def kept_flops_c2(t_heads, causal, sink, fwd=True, bwd=True, heads=None):
     bm = c2_masks(t_heads, causal, sink)
+    if heads is not None:
+        bm = bm[:, list(heads)]
     kept = int(bm.sum())
     RB, D = C2["RB"], C2["D"]
     per = (4 if fwd else 0) + (10 if bwd else 0)
@@ -193,6 +195,11 @@ def kept_flops_c2(t_heads, causal, sink, fwd=True, bwd=True):
 
 
 def run_reference_arm(args):
+    """The reference's CPU path of the headline step, timed on this box's host cores.  A step
+    is a bounded sample of C2 -- 2 of the 32 heads, full N=8192, masked dense fp32 forward +
+    autograd backward -- so every timed step is real work; value is the kept-block TFLOP/s
+    of that sample (the same rate the whole problem would run at, since the masked dense
+    path's cost is the same for every head)."""
     world, rank, _ = dist_setup(args.gpus)
     if rank != 0:
         return
@@ -200,14 +207,15 @@ def run_reference_arm(args):
     t_heads = c2_thresholds(0)
     kept, flops = kept_flops_c2(t_heads, True, True)
     heads = (0, 1)
+    kept_h, flops_h = kept_flops_c2(t_heads, True, True, heads=heads)
     for _ in range(args.warmup):
         cpu_reference_sample(heads, t_heads=t_heads)
     times = []
     for _ in range(args.steps):
         s, nh = cpu_reference_sample(heads, t_heads=t_heads)
-        times.append(s * C2["H"] / nh)
+        times.append(s)
     step = statistics.mean(times)
-    value = flops * args.gpus / step / 1e12
+    value = flops_h / step / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -215,9 +223,13 @@ def run_reference_arm(args):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_c2(args.gpus, t_heads, kept),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-                         "kind": "port",
-                         "sample": f"masked dense fp32 attention fwd+bwd (autograd) on {len(heads)} of "
-                                   f"{C2['H']} heads of C2, full N=8192, scaled x{C2['H'] // len(heads)}"},
+                         "kind": "port", "measured_s": round(step, 4), "scale": 1,
+                         "sample_heads": list(heads), "sample_kept_blocks": kept_h,
+                         "sample_flops": flops_h,
+                         "whole_step_s_extrapolated": round(step * flops / flops_h, 3),
+                         "sample": f"one step = masked dense fp32 attention fwd+bwd (autograd) on "
+                                   f"heads {list(heads)} of C2, full N=8192; value = the sample's "
+                                   f"kept-block FLOPs / its measured time"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -245,36 +257,49 @@ def config_c2(n_gpus, t_heads, kept):
 # ---------------------------------------------------------------------------------------
 
 class C2Problem:
-    """Device-resident C2 inputs and the direct C-ABI step (build, fwd, bwd phases)."""
+    """Device-resident C2 inputs and the direct C-ABI step (build, fwd, bwd phases).
 
-    def __init__(self, dev, seed, t_heads, causal=True, sink=True):
+    ``kv_groups`` (default: all 8) selects the KV heads this problem holds, with their 4
+    query heads each -- the strong-scaling split of C2's heads over GPUs.  The inputs are
+    always drawn for the whole C2 problem from the seed, then sliced, so every split sees
+    the same numbers."""
+
+    def __init__(self, dev, seed, t_heads, causal=True, sink=True, kv_groups=None):
         from ultrametric import _native as nat
         self.nat = nat
         self.dev = dev
         Z, H, Hkv, N, D, RB, TD = (C2[k] for k in ("Z", "H", "Hkv", "N", "D", "RB", "TD"))
+        G = H // Hkv
+        kv_groups = list(range(Hkv)) if kv_groups is None else list(kv_groups)
+        heads = [g * G + j for g in kv_groups for j in range(G)]
+        self.H, self.Hkv = len(heads), len(kv_groups)
         self.NB = N // RB
         gen = torch.Generator().manual_seed(seed)
-        self.h_q = torch.randn(Z, H, N, D, generator=gen).bfloat16().pin_memory()
-        self.h_k = torch.randn(Z, Hkv, N, D, generator=gen).bfloat16().pin_memory()
-        self.h_v = torch.randn(Z, Hkv, N, D, generator=gen).bfloat16().pin_memory()
-        self.h_do = torch.randn(Z, H, N, D, generator=gen).bfloat16().pin_memory()
+        h_q = torch.randn(Z, H, N, D, generator=gen).bfloat16()
+        h_k = torch.randn(Z, Hkv, N, D, generator=gen).bfloat16()
+        h_v = torch.randn(Z, Hkv, N, D, generator=gen).bfloat16()
+        h_do = torch.randn(Z, H, N, D, generator=gen).bfloat16()
+        if self.H != H:
+            h_q, h_do = h_q[:, heads].contiguous(), h_do[:, heads].contiguous()
+            h_k, h_v = h_k[:, kv_groups].contiguous(), h_v[:, kv_groups].contiguous()
+        self.h_q, self.h_k, self.h_v, self.h_do = (t.pin_memory() for t in (h_q, h_k, h_v, h_do))
         self.q, self.k, self.v, self.do = (t.to(dev) for t in (self.h_q, self.h_k, self.h_v, self.h_do))
-        self.router = tree_router(Z, H, self.NB, TD).to(dev)
-        self.t_heads = list(t_heads)
+        self.router = tree_router(Z, self.H, self.NB, TD).to(dev)
+        self.t_heads = [t_heads[h] for h in heads]
         self.depth = torch.tensor(self.t_heads, dtype=torch.int32, device=dev)
         self.causal, self.sink = causal, sink
         self.scale = 1.0 / math.sqrt(D)
         NB = self.NB
-        self.lists = torch.empty(Z, H, NB, NB, dtype=torch.int32, device=dev)
-        self.counts = torch.empty(Z, H, NB, dtype=torch.int32, device=dev)
+        self.lists = torch.empty(Z, self.H, NB, NB, dtype=torch.int32, device=dev)
+        self.counts = torch.empty(Z, self.H, NB, dtype=torch.int32, device=dev)
         self.out = torch.empty_like(self.q)
-        self.lse = torch.empty(Z, H, N, dtype=torch.float32, device=dev)
+        self.lse = torch.empty(Z, self.H, N, dtype=torch.float32, device=dev)
         self.dq = torch.empty_like(self.q)
         self.dk = torch.empty_like(self.k)
         self.dv = torch.empty_like(self.v)
-        wsb = int(nat.lib().sa_block_list_attention_bwd_workspace_bytes(Z, H, Hkv, N, D, RB))
+        wsb = int(nat.lib().sa_block_list_attention_bwd_workspace_bytes(Z, self.H, self.Hkv, N, D, RB))
         self.ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        fwb = int(nat.lib().sa_block_list_attention_fwd_workspace_bytes(Z, H, N, D, RB))
+        fwb = int(nat.lib().sa_block_list_attention_fwd_workspace_bytes(Z, self.H, N, D, RB))
         self.fws = torch.empty(max(fwb, 256), dtype=torch.uint8, device=dev)
         self.build()
         torch.cuda.synchronize()
@@ -284,29 +309,26 @@ class C2Problem:
                       "dkdv": self.kept * 8 * RB2D}
         self.flops_alg = self.kept * 14 * RB2D
         # compulsory bytes of the forward: Q, O, LSE and each referenced K/V block once per KV head
-        NBK = NB
-        ref_kv = torch.zeros(Z, Hkv, NBK, dtype=torch.bool, device=dev)
-        group = H // Hkv
-        for h in range(H):
+        ref_kv = torch.zeros(Z, self.Hkv, NB, dtype=torch.bool, device=dev)
+        for h in range(self.H):
             c = self.counts[0, h]
             m = torch.arange(NB, device=dev).view(1, -1) < c.view(-1, 1)
-            ref_kv[0, h // group].index_put_((self.lists[0, h][m].long(),), torch.tensor(True, device=dev))
+            ref_kv[0, h // G].index_put_((self.lists[0, h][m].long(),), torch.tensor(True, device=dev))
         self.fwd_bytes = (2 * self.q.numel() * 2 + self.lse.numel() * 4 +
                           int(ref_kv.sum()) * RB * D * 2 * 2)
 
     def build(self):
         nat, s = self.nat, torch.cuda.current_stream().cuda_stream
-        Z, H, NB = 1, C2["H"], self.NB
         nat.check(nat.lib().sa_build_block_lists(
-            self.router.data_ptr(), nat.SA_I32, nat.strides(self.router), Z, H, NB, C2["TD"],
+            self.router.data_ptr(), nat.SA_I32, nat.strides(self.router), 1, self.H, self.NB, C2["TD"],
             self.depth.data_ptr(), 2, 1, int(self.causal), int(self.sink), 0,
-            self.lists.data_ptr(), NB, self.counts.data_ptr(), s), "build")
+            self.lists.data_ptr(), self.NB, self.counts.data_ptr(), s), "build")
 
     def fwd(self):
         nat, s = self.nat, torch.cuda.current_stream().cuda_stream
-        Z, H, Hkv, N, D, RB = (C2[k] for k in ("Z", "H", "Hkv", "N", "D", "RB"))
+        N, D, RB = C2["N"], C2["D"], C2["RB"]
         nat.check(nat.lib().sa_block_list_attention_fwd(
-            nat.SA_BF16, Z, H, Hkv, N, D, RB, self.q.data_ptr(), nat.strides(self.q),
+            nat.SA_BF16, 1, self.H, self.Hkv, N, D, RB, self.q.data_ptr(), nat.strides(self.q),
             self.k.data_ptr(), nat.strides(self.k), self.v.data_ptr(), nat.strides(self.v),
             self.out.data_ptr(), nat.strides(self.out), self.lse.data_ptr(),
             self.lists.data_ptr(), self.NB, self.counts.data_ptr(), None, 0, None,
@@ -314,9 +336,9 @@ class C2Problem:
 
     def bwd(self, phase):
         nat, s = self.nat, torch.cuda.current_stream().cuda_stream
-        Z, H, Hkv, N, D, RB = (C2[k] for k in ("Z", "H", "Hkv", "N", "D", "RB"))
+        N, D, RB = C2["N"], C2["D"], C2["RB"]
         nat.check(nat.lib().sa_block_list_attention_bwd_phase(
-            phase, nat.SA_BF16, Z, H, Hkv, N, D, RB, self.q.data_ptr(), nat.strides(self.q),
+            phase, nat.SA_BF16, 1, self.H, self.Hkv, N, D, RB, self.q.data_ptr(), nat.strides(self.q),
             self.k.data_ptr(), nat.strides(self.k), self.v.data_ptr(), nat.strides(self.v),
             self.out.data_ptr(), nat.strides(self.out), self.do.data_ptr(), nat.strides(self.do),
             self.lse.data_ptr(), self.lists.data_ptr(), self.NB, self.counts.data_ptr(),
@@ -341,6 +363,13 @@ class C2Problem:
         evs[4].record()
         self.bwd(3)
         evs[5].record()
+
+    def step_plain(self):
+        self.build()
+        self.fwd()
+        self.bwd(1)
+        self.bwd(2)
+        self.bwd(3)
 
 
 def flush_l2(buf):
@@ -370,6 +399,39 @@ def time_c2(prob, steps, warmup, flush, barrier=None):
             parts[p].append(e[j].elapsed_time(e[j + 1]))
         totals.append(e[0].elapsed_time(e[5]))
     return sum(totals), {p: statistics.mean(v) for p, v in parts.items()}
+
+
+def time_c2_graph(prob, steps, warmup, flush):
+    """The same step captured once in a CUDA graph and replayed (L2 flushed between
+    replays, outside the events): what is left when host launch work is taken away.  The
+    difference from the eager step is the launch and host overhead of the C-ABI calls."""
+    try:
+        for _ in range(2):
+            prob.step_plain()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            prob.step_plain()
+        torch.cuda.synchronize()
+        for _ in range(warmup):
+            flush_l2(flush)
+            g.replay()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(steps):
+            flush_l2(flush)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        del g
+        return {"ms_per_step": round(statistics.mean(times), 4),
+                "ms_median": round(statistics.median(times), 4)}
+    except Exception as ex:  # capture is a diagnostic; report why it did not run
+        torch.cuda.synchronize()
+        return {"error": f"{type(ex).__name__}: {str(ex)[:160]}"}
 
 
 def time_e2e(prob, steps, warmup):
@@ -479,14 +541,19 @@ def run_sweep(dev, flush, steps):
     return rows
 
 
-def run_decode(dev, seed, steps, warmup, flush, peaks, world=1, barrier=None):
-    """C3: 64 requests, H=32/8, D=128, page 64, ctx ~U[2048, 32768], shuffled pool,
-    tree routes on the logical page index (depth 9), random query leaf, req_depth 4,
-    sink + most recent page."""
-    from ultrametric import ultrametric_decode
-    B, H, Hkv, D, page, TD = 64, 32, 8, 128, 64, 9
+C3 = dict(B=64, H=32, Hkv=8, D=128, page=64, TD=9, req_depth=4, local_blocks=1, sink_block=True,
+          ctx_lo=2048, ctx_hi=32768)
+
+
+def make_c3(dev, seed=0):
+    """The C3 decode batch: 64 requests, H=32/8, D=128, page 64, ctx ~U[2048, 32768] (seeded),
+    a shuffled physical page pool with random block tables, tree routes of the LOGICAL page
+    index (depth 9) stored at the physical page id, a random query leaf per request (routes
+    shared by all heads), req_depth 4, sink + most recent page.  Host-side metadata is kept
+    for byte counts and the CPU oracle; the caches are drawn on the device."""
+    B, H, Hkv, D, page, TD = (C3[k] for k in ("B", "H", "Hkv", "D", "page", "TD"))
     gen = torch.Generator().manual_seed(10 + seed)
-    ctx = torch.randint(2048, 32769, (B,), generator=gen, dtype=torch.int32)
+    ctx = torch.randint(C3["ctx_lo"], C3["ctx_hi"] + 1, (B,), generator=gen, dtype=torch.int32)
     n_log = (ctx + page - 1) // page
     maxL = int(n_log.max())
     total = int(n_log.sum()) + 16
@@ -508,49 +575,107 @@ def run_decode(dev, seed, steps, warmup, flush, peaks, world=1, barrier=None):
     kc = torch.randn(total, Hkv, page, D, generator=g, device=dev, dtype=torch.bfloat16)
     vc = torch.randn(total, Hkv, page, D, generator=g, device=dev, dtype=torch.bfloat16)
     q = torch.randn(B, H, D, generator=g, device=dev, dtype=torch.bfloat16)
-    btd, ctxd, rid, qrid = bt.to(dev), ctx.to(dev), ri.to(dev), qri.to(dev)
-    # routed bytes (routes are shared by the heads of a group): selected pages x valid tokens
-    rd, local = 4, 1
-    sel_tokens = 0
-    sel_pages = 0
-    for b in range(B):
-        n = int(n_log[b])
+    return {"q": q, "kc": kc, "vc": vc, "bt": bt.to(dev), "ctx": ctx.to(dev), "ri": ri.to(dev),
+            "qri": qri.to(dev), "h_bt": bt, "h_ctx": ctx, "h_ri": ri, "h_qri": qri,
+            "bits": bits, "qbits": qbits, "n_log": n_log, "total_pages": total}
+
+
+def c3_routed_bytes(c3, requests):
+    """Algorithmic bytes of a decode over ``requests``: the selected pages' valid tokens x
+    Hkv x D x 2 B for K and V (each KV byte once per KV head; the routes are shared by the
+    heads of a group) + Q and O.  Returns (bytes, selected pages)."""
+    Hkv, D, page, H = C3["Hkv"], C3["D"], C3["page"], C3["H"]
+    rd, local = C3["req_depth"], C3["local_blocks"]
+    tokens = pages = 0
+    for b in requests:
+        n = int(c3["n_log"][b])
         lp = torch.arange(n)
-        match = (bits[lp][:, :rd] == qbits[b, :rd]).all(-1)
+        match = (c3["bits"][lp][:, :rd] == c3["qbits"][b, :rd]).all(-1)
         match[0] = True
         match[max(0, n - local):] = True
-        valid = torch.clamp(int(ctx[b]) - lp * page, max=page)
-        sel_tokens += int(valid[match].sum())
-        sel_pages += int(match.sum())
-    kv_bytes = sel_tokens * Hkv * D * 2 * 2
-    qo_bytes = 2 * B * H * D * 2
-    routed_bytes = kv_bytes + qo_bytes
+        valid = torch.clamp(int(c3["h_ctx"][b]) - lp * page, max=page)
+        tokens += int(valid[match].sum())
+        pages += int(match.sum())
+    return tokens * Hkv * D * 2 * 2 + 2 * len(requests) * H * D * 2, pages
 
-    def one():
-        return ultrametric_decode(q, kc, vc, btd, ctxd, rid, qrid, rd, local_blocks=local, sink_block=True)
 
-    for _ in range(warmup):
-        one()
-    torch.cuda.synchronize()
-    if barrier:
-        barrier()
-    tot = 0.0
-    for _ in range(steps):
-        flush_l2(flush)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        one()
-        e1.record()
-        e1.synchronize()
-        tot += e0.elapsed_time(e1)
-    # each rank decodes its own batch (weak scaling): whole-job rates over the slowest rank
-    ms = max_over_ranks([tot / steps], world, dev)[0]
+def c3_host_subset(c3, requests):
+    """CPU copies of what the decode of ``requests`` reads: their pages in a compacted pool,
+    with block tables and page routes re-indexed to it (for the CPU oracle)."""
+    n_log = c3["n_log"]
+    phys = torch.cat([c3["h_bt"][b, :int(n_log[b])].long() for b in requests])
+    remap = {int(p): i for i, p in enumerate(phys.tolist())}
+    maxL = max(int(n_log[b]) for b in requests)
+    bt = torch.zeros(len(requests), maxL, dtype=torch.int32)
+    for i, b in enumerate(requests):
+        n = int(n_log[b])
+        bt[i, :n] = torch.tensor([remap[int(p)] for p in c3["h_bt"][b, :n].tolist()], dtype=torch.int32)
+    idx = phys.to(c3["kc"].device)
+    return {"q": c3["q"][list(requests)].cpu(), "kc": c3["kc"][idx].cpu(), "vc": c3["vc"][idx].cpu(),
+            "bt": bt, "ctx": c3["h_ctx"][list(requests)].clone(), "ri": c3["h_ri"][phys].clone(),
+            "qri": c3["h_qri"][list(requests)].clone()}
+
+
+def c3_decode(c3, requests=None):
+    """One C3 decode through the public API (``requests``: a contiguous slice, for strong
+    scaling; default all 64)."""
+    from ultrametric import ultrametric_decode
+    sl = slice(None) if requests is None else slice(requests[0], requests[-1] + 1)
+    return ultrametric_decode(c3["q"][sl], c3["kc"], c3["vc"], c3["bt"][sl], c3["ctx"][sl],
+                              c3["ri"], c3["qri"][sl], C3["req_depth"],
+                              local_blocks=C3["local_blocks"], sink_block=C3["sink_block"])
+
+
+def cpu_decode_baseline(c3, requests=(0, 21, 42, 63)):
+    """The reference's CPU decode (_ultrametric_decode_reference, kernel_decode.py:129-185,
+    restated in oracle/) on a request sample, scaled to the 64-request batch by routed bytes.
+    The port reads the GQA cache head of each query head, which is what the reference's
+    expanded cache gives it.  Returns (seconds for 64 requests, sample seconds, sample)."""
+    from oracle import decode_oracle as dor
+    sub = c3_host_subset(c3, list(requests))
+    t0 = time.perf_counter()
+    dor.ultrametric_decode_reference(sub["q"].float(), sub["kc"].float(), sub["vc"].float(), sub["bt"],
+                                     sub["ctx"], sub["ri"], sub["qri"], C3["req_depth"],
+                                     local_blocks=C3["local_blocks"], sink_block=C3["sink_block"],
+                                     compute_dtype=torch.float32)
+    s = time.perf_counter() - t0
+    b_all, _ = c3_routed_bytes(c3, range(C3["B"]))
+    b_sub, _ = c3_routed_bytes(c3, list(requests))
+    return s * b_all / b_sub, s, list(requests)
+
+
+def run_decode(dev, seed, steps, warmup, flush, peaks, world=1, rank=0, barrier=None, cpu=False):
+    """C3 routed paged decode.  Weak scaling: every rank decodes its own 64-request batch.
+    Strong scaling (world > 1): the one 64-request batch is split into contiguous request
+    slices, one per rank, as the C3 config defines it.  Times are the max over ranks."""
+    B = C3["B"]
+    c3 = make_c3(dev, seed)
+    routed_bytes, sel_pages = c3_routed_bytes(c3, range(B))
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        tot = 0.0
+        for _ in range(steps):
+            flush_l2(flush)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+        return max_over_ranks([tot / steps], world, dev)[0]
+
+    ms = timed(lambda: c3_decode(c3))
     gbs = world * routed_bytes / (ms * 1e-3) / 1e9
-    dense_bytes = int(n_log.sum()) * page * Hkv * D * 2 * 2
-    return {
+    dense_bytes = int(c3["n_log"].sum()) * C3["page"] * C3["Hkv"] * C3["D"] * 2 * 2
+    res = {
         "config": "C3: 64 req x 1 token, H=32/8, D=128, page 64, ctx~U[2048,32768], req_depth 4, sink+last page",
         "ms_per_step": round(ms, 4), "tok_per_s": round(world * B / (ms * 1e-3), 1),
-        "requests_per_gpu": B,
+        "requests_per_gpu": B, "scaling": "weak",
         "routed_gbs": round(gbs, 1), "routed_bytes": routed_bytes, "routed_pages": sel_pages,
         "dense_equivalent_bytes": dense_bytes,
         # per GPU (the slowest rank), against one GPU's measured copy bandwidth
@@ -558,29 +683,84 @@ def run_decode(dev, seed, steps, warmup, flush, peaks, world=1, barrier=None):
                      "unit": "GB/s", "frac": round(gbs / world / peaks["hbm_gbs"], 4), "per": "GPU"},
         "gpu_launches_per_step": 4,
     }
+    if world > 1:
+        per = B // world
+        mine = list(range(rank * per, (rank + 1) * per))
+        if seed != 0:  # every rank takes its slice of the same (seed 0) batch
+            del c3
+            torch.cuda.empty_cache()
+            c3 = make_c3(dev, 0)
+        ms_s = timed(lambda: c3_decode(c3, mine))
+        res["strong"] = {"requests_per_gpu": per, "ms_per_step": round(ms_s, 4),
+                         "tok_per_s": round(B / (ms_s * 1e-3), 1),
+                         "routed_gbs": round(routed_bytes / (ms_s * 1e-3) / 1e9, 1),
+                         "scaling": "strong: the one 64-request batch split over the ranks"}
+    if cpu and rank == 0 and world == 1:
+        torch.set_num_threads(os.cpu_count() or 1)
+        cpu_s, sample_s, reqs = cpu_decode_baseline(c3)
+        res["cpu_baseline"] = {"value": round(B / cpu_s, 3), "unit": "tok/s",
+                               "ms_per_step": round(cpu_s * 1e3, 1),
+                               "cores": torch.get_num_threads(), "kind": "port",
+                               "measured_s": round(sample_s, 3), "scale": round(cpu_s / sample_s, 2),
+                               "sample": f"_ultrametric_decode_reference (fp32, per query head) on "
+                                         f"requests {reqs}, scaled to the 64-request batch by routed bytes"}
+    del c3
+    torch.cuda.empty_cache()
+    return res
 
 
 C5 = dict(Z=1, H=16, Hkv=8, N=131072, D=128, RB=128, TD=10, t=7)
 
 
-def run_c5(dev, rank, world, steps, warmup, flush, barrier=None):
+def make_c5(dev, rank=0, world=1):
+    """C5 inputs: N=131072, H=16/8, D=128, RB=128 (NB=1024), tree routes TD=10, threshold 7,
+    causal + sink (5624 kept blocks per head), lists built on the device.  q/k/v hold this
+    rank's contiguous chunk of N / world rows, drawn on the device (seed 40 + rank)."""
+    from ultrametric import build_block_lists
+    Z, H, Hkv, N, D, RB = (C5[k] for k in ("Z", "H", "Hkv", "N", "D", "RB"))
+    router = tree_router(Z, H, N // RB, C5["TD"])
+    bl = build_block_lists(router.to(dev), C5["t"], is_causal=True, sink_block=True, arity=2)
+    Nl = N // world
+    g = torch.Generator(device=dev).manual_seed(40 + rank)
+    q = torch.randn(Z, H, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(Z, Hkv, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(Z, Hkv, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
+    return {"q": q, "k": k, "v": v, "bl": bl, "router": router, "rows_per_rank": Nl}
+
+
+def cpu_c5_baseline(c5, rows=1024):
+    """The reference's CPU path for C5 cannot run whole (70 TFLOP of masked dense attention):
+    time a slice of it -- head 0, the last ``rows`` query rows against all 131072 keys,
+    masked dense fp32 in the query-chunked form of benchmarks/benchmark_block_list.py:106-123
+    -- and scale by the rows and heads it stands for (every query chunk of that form scores
+    all N keys).  Returns (seconds for the whole forward, sample seconds, scale)."""
+    from oracle import attention_oracle as ao
+    from oracle import block_list_oracle as blo
+    N, H, RB = C5["N"], C5["H"], C5["RB"]
+    bm = torch.from_numpy(blo.block_mask(c5["router"][:, :1].numpy(), C5["t"], is_causal=True,
+                                         sink_block=True))
+    q = c5["q"][:, :1].float().cpu()
+    k = c5["k"][:, :1].float().cpu()
+    v = c5["v"][:, :1].float().cpu()
+    t0 = time.perf_counter()
+    ao.masked_attention_chunked(q, k, v, bm, RB, True, chunk=rows, compute_dtype=torch.float32,
+                                row_ranges=[(N - rows, N)])
+    s = time.perf_counter() - t0
+    scale = H * N / rows
+    return s * scale, s, scale
+
+
+def run_c5(dev, rank, world, steps, warmup, flush, barrier=None, cpu=False):
     """C5 very long prefill forward: N=131072, H=16/8, D=128, RB=128 (NB=1024), tree routes
     TD=10, threshold 7, causal + sink (5624 kept blocks per head).  One GPU: the whole
     sequence.  N GPUs: the sequence sharded contiguously, K/V chunks rotating over NCCL
     (ultrametric.ring), time = max over ranks."""
-    from ultrametric import build_block_lists
     from ultrametric.block_list import _fwd
     from ultrametric.ring import RingPlan, ring_block_list_attention
     Z, H, Hkv, N, D, RB = (C5[k] for k in ("Z", "H", "Hkv", "N", "D", "RB"))
-    NB = N // RB
-    router = tree_router(Z, H, NB, C5["TD"]).to(dev)
-    bl = build_block_lists(router, C5["t"], is_causal=True, sink_block=True, arity=2)
+    c5 = make_c5(dev, rank, world)
+    q, k, v, bl, Nl = c5["q"], c5["k"], c5["v"], c5["bl"], c5["rows_per_rank"]
     kept = int(bl.counts.sum())
-    Nl = N // world
-    g = torch.Generator(device=dev).manual_seed(40 + rank)  # this rank's chunk of the sequence
-    q = torch.randn(Z, H, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
-    k = torch.randn(Z, Hkv, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
-    v = torch.randn(Z, Hkv, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(D)
     # the ring's schedule depends only on the lists: planned once, like the lists themselves
     plan = RingPlan(bl, world, rank, Nl, RB, True) if world > 1 else None
@@ -617,6 +797,17 @@ def run_c5(dev, rank, world, steps, warmup, flush, barrier=None):
                        "kv_bytes_sent_by_rank0": 2 * Z * Hkv * sent * D * 2,
                        "dense_ring_bytes_per_hop": 2 * Z * Hkv * Nl * D * 2,
                        "transport": "NCCL send/recv (torch.distributed) of the referenced K/V blocks only"}
+    if cpu and rank == 0 and world == 1:
+        torch.set_num_threads(os.cpu_count() or 1)
+        cpu_s, sample_s, sc = cpu_c5_baseline(c5)
+        res["cpu_baseline"] = {"value": round(flops / cpu_s / 1e12, 6), "unit": "TFLOP/s",
+                               "ms": round(cpu_s * 1e3, 1), "cores": torch.get_num_threads(),
+                               "kind": "port", "measured_s": round(sample_s, 3), "scale": sc,
+                               "sample": "masked dense fp32 forward, head 0, the last 1024 query rows "
+                                         "against all 131072 keys (query-chunked form), scaled by "
+                                         "16 heads x 131072 rows / 1024 rows; rate on kept-block FLOPs"}
+    del c5
+    torch.cuda.empty_cache()
     return res
 
 
@@ -680,6 +871,160 @@ def run_c4(dev, rank, world, warmup, flush, barrier=None):
             "timed": "per layer: list build + forward (router projection not included)"}
 
 
+# ---------------------------------------------------------------------------------------
+# the reference's own Triton kernels on this GPU (the bar this build has to beat)
+# ---------------------------------------------------------------------------------------
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def run_reference_triton_subprocess(timeout_s=900):
+    """Time the reference's Triton kernels in a child process (its ``ultrametric`` package
+    would shadow ours in this one).  The reference is installed, unmodified, into
+    baseline/_ref (``pip install --no-index --no-deps --target baseline/_ref`` of its
+    source); without it the entry says unavailable."""
+    if not os.path.isdir(os.path.join(REF_DIR, "ultrametric")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    cmd = [sys.executable, os.path.abspath(__file__), "--reference-triton-worker"]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"reference Triton timing exceeded {timeout_s} s"}
+    for line in reversed(r.stdout.strip().splitlines()):
+        if line.startswith("{"):
+            try:
+                return json.loads(line)
+            except json.JSONDecodeError:
+                break
+    return {"unavailable": f"reference Triton worker rc={r.returncode}: "
+                           f"{(r.stderr or r.stdout).strip().splitlines()[-1:] }"}
+
+
+def _bench_ms(fn, flush, reps=20, warmup=3):
+    """do_bench-style median over ``reps`` CUDA-event-timed calls, L2 flushed before each."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        flush_l2(flush)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return statistics.median(times)
+
+
+def reference_triton_worker(args):
+    """Child process: import the reference's ``ultrametric`` from baseline/_ref (never this
+    repository's) and time, on the same inputs as our arm:
+      * build_block_lists(arity=2) (its fused Triton compaction, block_list.py:127-167);
+      * block_list_attention forward and forward+backward (block_list.py:387-681) at C2 for
+        the seeded threshold mix and the 50 / 90 / 98.4 % sweep points -- with K/V
+        repeat-interleaved to the 32 query heads, since the reference has no GQA;
+      * ultrametric_decode (kernel_decode.py:23-124) on the C3 batch, caches expanded to 32
+        heads likewise.
+    Prints one JSON line."""
+    ours = os.path.join(ROOT, "sparse-ai_b200")
+    sys.path[:] = [p for p in sys.path if os.path.abspath(p) != ours]
+    sys.path.insert(0, REF_DIR)
+    import importlib
+    rbl = importlib.import_module("ultrametric.block_list")
+    rkd = importlib.import_module("ultrametric.kernel_decode")
+    assert os.path.abspath(rbl.__file__).startswith(REF_DIR), rbl.__file__
+    import triton
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    res = {"source": "sparse-ai installed unmodified in baseline/_ref", "triton": triton.__version__,
+           "timing": "median of 20 CUDA-event-timed calls, L2 flushed (256 MiB write) before each"}
+    Z, H, Hkv, N, D, RB, TD = (C2[k] for k in ("Z", "H", "Hkv", "N", "D", "RB", "TD"))
+    G = H // Hkv
+    gen = torch.Generator().manual_seed(0)
+    q = torch.randn(Z, H, N, D, generator=gen).bfloat16().to(dev)
+    k = torch.randn(Z, Hkv, N, D, generator=gen).bfloat16().to(dev)
+    v = torch.randn(Z, Hkv, N, D, generator=gen).bfloat16().to(dev)
+    do = torch.randn(Z, H, N, D, generator=gen).bfloat16().to(dev)
+    k = k.repeat_interleave(G, dim=1).contiguous()
+    v = v.repeat_interleave(G, dim=1).contiguous()
+    router = tree_router(Z, H, N // RB, TD).to(dev)
+    cases = [("headline", c2_thresholds(0), True, True), ("50%", [1] * H, True, True),
+             ("90%", [4] * H, True, True), ("98.4%", [6] * H, False, False)]
+    rows = []
+    for name, t_heads, causal, sink in cases:
+        row = {"case": name}
+        try:
+            depth = torch.tensor(t_heads, dtype=torch.int64, device=dev)
+            build = lambda: rbl.build_block_lists(router, depth, is_causal=causal, sink_block=sink, arity=2)
+            row["build_ms"] = round(_bench_ms(build, flush), 4)
+            bl = build()
+            kept = int(bl.counts.sum())
+            row["kept_blocks"] = kept
+            with torch.no_grad():
+                fwd = lambda: rbl.block_list_attention(q, k, v, bl, route_block=RB, is_causal=causal)
+                row["fwd_ms"] = round(_bench_ms(fwd, flush), 4)
+            qg, kg, vg = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+
+            def fwd_bwd():
+                out = rbl.block_list_attention(qg, kg, vg, bl, route_block=RB, is_causal=causal)
+                out.backward(do)
+            row["fwd_bwd_ms"] = round(_bench_ms(fwd_bwd, flush, reps=10), 4)
+            f = RB * RB * D
+            row["fwd_kept_tflops"] = round(kept * 4 * f / (row["fwd_ms"] * 1e-3) / 1e12, 2)
+            row["fwd_bwd_kept_tflops"] = round(kept * 14 * f / (row["fwd_bwd_ms"] * 1e-3) / 1e12, 2)
+            row["step_ms_with_build"] = round(row["fwd_bwd_ms"] + row["build_ms"], 4)
+            del qg, kg, vg
+        except Exception as ex:
+            row["error"] = f"{type(ex).__name__}: {str(ex)[:200]}"
+        rows.append(row)
+        torch.cuda.empty_cache()
+    res["c2"] = rows
+    del q, k, v, do
+    torch.cuda.empty_cache()
+    try:
+        c3 = make_c3(dev, 0)
+        kc = c3["kc"].repeat_interleave(C3["H"] // C3["Hkv"], dim=1).contiguous()
+        vc = c3["vc"].repeat_interleave(C3["H"] // C3["Hkv"], dim=1).contiguous()
+        del c3["kc"], c3["vc"]
+        dec = lambda: rkd.ultrametric_decode(c3["q"], kc, vc, c3["bt"], c3["ctx"], c3["ri"], c3["qri"],
+                                             C3["req_depth"], local_blocks=C3["local_blocks"],
+                                             sink_block=C3["sink_block"])
+        ms = _bench_ms(dec, flush)
+        rb, _ = c3_routed_bytes(c3, range(C3["B"]))
+        res["c3_decode"] = {"ms": round(ms, 4), "tok_per_s": round(C3["B"] / (ms * 1e-3), 1),
+                            "routed_gbs_gqa_bytes": round(rb / (ms * 1e-3) / 1e9, 1),
+                            "note": "caches expanded to 32 heads (no GQA in the reference); "
+                                    "GB/s counts each KV byte once per KV head, as ours does"}
+    except Exception as ex:
+        res["c3_decode"] = {"error": f"{type(ex).__name__}: {str(ex)[:200]}"}
+    print(json.dumps(res), flush=True)
+
+
+def _merge_reference_triton(line, ref, ms_step):
+    """Put the reference's Triton times beside ours: headline step, sweep rows, decode."""
+    rows = {r.get("case"): r for r in ref.get("c2", [])}
+    h = rows.get("headline", {})
+    if "step_ms_with_build" in h:
+        line["vs_reference_triton"] = {
+            "reference_step_ms": h["step_ms_with_build"], "ours_step_ms": round(ms_step, 4),
+            "speedup": round(h["step_ms_with_build"] / ms_step, 2),
+            "note": "same inputs; the reference step = its build_block_lists(arity=2) + "
+                    "block_list_attention fwd+bwd (K/V expanded to 32 heads)"}
+    for r in line.get("sweep", []):
+        t = rows.get(r["target"], {})
+        if "fwd_ms" in t:
+            r["reference_triton_ms"] = {"fwd": t["fwd_ms"], "fwd_bwd": t["fwd_bwd_ms"], "build": t["build_ms"]}
+            r["speedup_fwd_vs_reference_triton"] = round(t["fwd_ms"] / r["fwd_ms"], 2)
+            r["speedup_step_vs_reference_triton"] = round(t["step_ms_with_build"] / r["step_ms"], 2)
+    d = line.get("decode")
+    t = ref.get("c3_decode", {})
+    if d is not None and "ms" in t:
+        d["reference_triton_ms"] = t["ms"]
+        d["speedup_vs_reference_triton"] = round(t["ms"] / d["ms_per_step"], 2)
+
+
 def run_ours(args):
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -696,7 +1041,7 @@ def run_ours(args):
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
     if args.decode_only:  # profiling aid: the C3 decode alone, one JSON line
-        d = run_decode(dev, rank, args.steps, args.warmup, flush, peaks, world, barrier)
+        d = run_decode(dev, rank, args.steps, args.warmup, flush, peaks, world, rank, barrier)
         if rank == 0:
             print(json.dumps({"decode": d}), flush=True)
         if world > 1:
@@ -724,6 +1069,29 @@ def run_ours(args):
         with open(tf) as f:
             traffic = json.load(f).get(kern)
 
+    graph = time_c2_graph(prob, args.steps, args.warmup, flush)
+    if "ms_per_step" in graph:
+        graph["ms_per_step"] = round(max_over_ranks([graph["ms_per_step"]], world, dev)[0], 4)
+        graph["kept_tflops_whole_job"] = round(prob.flops_alg * world / (graph["ms_per_step"] * 1e-3) / 1e12, 2)
+    graph["eager_ms_per_step"] = round(ms_step, 4)
+
+    strong = None
+    if world > 1 and C2["Hkv"] % world == 0:
+        # strong scaling: C2's 8 KV groups (and their 32 query heads) split over the ranks
+        per = C2["Hkv"] // world
+        sub = C2Problem(dev, seed=0, t_heads=t_heads, kv_groups=range(rank * per, (rank + 1) * per))
+        tot_s, parts_s = time_c2(sub, args.steps, args.warmup, flush, barrier)
+        ms_s = max_over_ranks([tot_s / args.steps], world, dev)[0]
+        kept_all = torch.tensor([sub.kept], dtype=torch.float64, device=dev)
+        import torch.distributed as dist
+        dist.all_reduce(kept_all)
+        flops_all = float(kept_all.item()) * 14 * C2["RB"] ** 2 * C2["D"]
+        strong = {"kv_groups_per_gpu": per, "q_heads_per_gpu": sub.H, "ms_per_step": round(ms_s, 4),
+                  "kept_tflops_whole_job": round(flops_all / (ms_s * 1e-3) / 1e12, 2),
+                  "scaling": "strong: C2's heads split over the ranks by KV group, no collective"}
+        del sub
+        torch.cuda.empty_cache()
+
     if barrier:
         barrier()
     e2e_ms, h2d, d2h = time_e2e(prob, max(3, args.steps // 2), 2)
@@ -733,9 +1101,11 @@ def run_ours(args):
     extras = {}
     if not args.quick:
         extras["sweep"] = run_sweep(dev, flush, steps=5)  # per GPU (rank 0's numbers)
-        extras["c5"] = run_c5(dev, rank, world, max(3, args.steps // 2), args.warmup, flush, barrier)
+        extras["c5"] = run_c5(dev, rank, world, max(3, args.steps // 2), args.warmup, flush, barrier,
+                              cpu=not args.no_cpu)
         extras["c4"] = run_c4(dev, rank, world, 1, flush, barrier)
-        extras["decode"] = run_decode(dev, rank, args.steps, args.warmup, flush, peaks, world, barrier)
+        extras["decode"] = run_decode(dev, rank, args.steps, args.warmup, flush, peaks, world, rank,
+                                      barrier, cpu=not args.no_cpu)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -743,12 +1113,21 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         torch.set_num_threads(os.cpu_count() or 1)
-        s, nh = cpu_reference_sample((0, 1), t_heads=t_heads)
-        cpu_step = s * C2["H"] / nh
-        cpu = {"value": prob.flops_alg / cpu_step / 1e12, "unit": "TFLOP/s",
-               "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"masked dense fp32 attention fwd+bwd (autograd), 2 of 32 heads of C2 at "
-                         f"N=8192, {s:.2f} s, scaled x16 to {cpu_step:.1f} s per step"}
+        heads = (0, 1)
+        s, nh = cpu_reference_sample(heads, t_heads=t_heads)
+        _, flops_h = kept_flops_c2(t_heads, True, True, heads=heads)
+        cpu = {"value": flops_h / s / 1e12, "unit": "TFLOP/s",
+               "cores": torch.get_num_threads(), "kind": "port", "measured_s": round(s, 3),
+               "scale": round(prob.flops_alg / flops_h, 3),
+               "whole_step_s_extrapolated": round(s * prob.flops_alg / flops_h, 2),
+               "sample": f"masked dense fp32 attention fwd+bwd (autograd) on heads {list(heads)} of "
+                         f"C2 at N=8192; value = the sample's kept-block FLOPs / its time"}
+
+    ref_triton = None
+    if rank == 0 and world == 1 and not args.quick and not args.no_reference_triton:
+        del prob
+        torch.cuda.empty_cache()
+        ref_triton = run_reference_triton_subprocess()
 
     if rank == 0:
         line = {
@@ -772,8 +1151,14 @@ def run_ours(args):
                     "path": "ultrametric.block_list_attention autograd (ctypes -> C ABI)"},
             "clocks": clk.summary(),
             "gpu_launches": sum(C2Problem.LAUNCHES.values()) * args.steps,
+            "cuda_graph": graph,
             **extras,
         }
+        if strong is not None:
+            line["c2_strong"] = strong
+        if ref_triton is not None:
+            line["reference_triton"] = ref_triton
+            _merge_reference_triton(line, ref_triton, ms_step)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -790,12 +1175,17 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--decode-only", action="store_true",
                     help="profiling aid: time only the C3 routed decode")
+    ap.add_argument("--no-reference-triton", action="store_true",
+                    help="skip timing the reference's own Triton kernels on this GPU")
+    ap.add_argument("--reference-triton-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--threshold", type=int, default=None,
                     help="profiling aid: every head uses this LCA threshold instead of the seeded mix")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.reference_triton_worker:
+        reference_triton_worker(args)
+    elif args.impl == "reference":
         run_reference_arm(args)
     else:
         run_ours(args)

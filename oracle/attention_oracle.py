@@ -12,6 +12,8 @@ Restates the reference's ground truth for the prefill path of sparse-ai:
   shared by ``H // Hkv`` query heads (the reference repeat-interleaves them).
 * ``masked_attention_grads`` -- dQ, dK, dV and the soft-block-bias gradient by autograd of
   the masked reference (tests/test_block_list.py:287-292, 330-348 of the reference).
+* ``masked_attention_grads_chunked`` -- the same gradients written out explicitly and
+  query-chunked per GQA group, so the full N=8192 backward fits in host memory.
 """
 
 from __future__ import annotations
@@ -76,24 +78,27 @@ def masked_attention(q, k, v, mask, sm_scale: Optional[float] = None, bias=None,
 
 def masked_attention_chunked(q, k, v, block_mask, route_block: int, is_causal: bool,
                              sm_scale: Optional[float] = None, chunk: int = 1024,
-                             compute_dtype=torch.float32, heads=None):
+                             compute_dtype=torch.float32, heads=None, row_ranges=None):
     """Query-chunked masked attention over (Z, H, N, D) q and (Z, Hkv, N, D) k/v
-    (benchmarks/benchmark_block_list.py:106-123).  ``heads`` restricts to a head subset.
-    Returns (out, lse) in ``compute_dtype`` for the selected heads."""
+    (benchmarks/benchmark_block_list.py:106-123).  ``heads`` restricts to a head subset,
+    ``row_ranges`` (a list of [start, end) query-row ranges) to some query rows; rows
+    outside them are left zero.  Returns (out, lse) in ``compute_dtype`` for the selected
+    heads."""
     Z, H, N, D = q.shape
     group = H // k.shape[1]
     scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(D)
     hs = list(range(H)) if heads is None else list(heads)
-    out = torch.empty(Z, len(hs), N, D, dtype=compute_dtype)
-    lse = torch.empty(Z, len(hs), N, dtype=compute_dtype)
+    out = torch.zeros(Z, len(hs), N, D, dtype=compute_dtype)
+    lse = torch.zeros(Z, len(hs), N, dtype=compute_dtype)
     col_blk = torch.arange(N) // route_block
     cols = torch.arange(N)
     for z in range(Z):
         for hi, h in enumerate(hs):
             kf = k[z, h // group].to(compute_dtype)
             vf = v[z, h // group].to(compute_dtype)
-            for s0 in range(0, N, chunk):
-                e0 = min(N, s0 + chunk)
+            spans = row_ranges if row_ranges is not None else [(0, N)]
+            starts = [(s0, min(e, s0 + chunk)) for b, e in spans for s0 in range(b, e, chunk)]
+            for s0, e0 in starts:
                 rows = torch.arange(s0, e0)
                 sc = torch.matmul(q[z, h, s0:e0].to(compute_dtype), kf.T) * scale
                 m = block_mask[z, h][rows // route_block][:, col_blk]
@@ -171,3 +176,78 @@ def block_list_backward_lowp(q, k, v, out, dout, lse, mask, sm_scale=None, io_dt
         dk = dk.view(Z, k.shape[1], g, N, D).sum(2)
         dv = dv.view(Z, k.shape[1], g, N, D).sum(2)
     return {"dq": dq, "dk": dk, "dv": dv}
+
+
+def masked_attention_grads_chunked(q, k, v, block_mask, route_block: int, is_causal: bool,
+                                   dout, kv_heads, sm_scale: Optional[float] = None,
+                                   chunk: int = 1024, io_dtype=None,
+                                   compute_dtype=torch.float64):
+    """Backward of the masked attention for whole GQA groups, query-chunked so N=8192 fits
+    in host memory (the chunking of benchmarks/benchmark_block_list.py:106-123, applied to
+    the gradients of block_list.py:494-681).
+
+    For each KV head in ``kv_heads`` and its ``H // Hkv`` query heads: a forward pass per
+    query chunk gives out and lse, then a second pass gives
+        P = exp(S - lse), dP = dO V^T, Delta = rowsum(dO * O), dS = P * (dP - Delta),
+        dQ = scale * dS K,  dK = scale * sum_heads dS^T Q,  dV = sum_heads P^T dO,
+    and the unscaled per-block sums of dS (the soft-block-bias gradient before the slot
+    gather, block_list.py:571-584).  With ``io_dtype`` set, P and scale*dS are rounded to it
+    before their products and Delta uses O rounded to it, as the reference kernels do
+    (block_list.py:565-580, 652-680, 785).  Returns a dict of tensors over the selected heads:
+    out/lse/dq (Z, G*len(kv_heads), N, .), dk/dv (Z, len(kv_heads), N, D), dbias_blocks
+    (Z, G*len(kv_heads), NB, NB), and ``heads``, the query heads in order."""
+    Z, H, N, D = q.shape
+    Hkv = k.shape[1]
+    G = H // Hkv
+    NB = -(-N // route_block)
+    scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(D)
+    f = compute_dtype
+    heads = [g * G + j for g in kv_heads for j in range(G)]
+    nh, nk = len(heads), len(kv_heads)
+    res = {"heads": heads,
+           "out": torch.zeros(Z, nh, N, D, dtype=f), "lse": torch.zeros(Z, nh, N, dtype=f),
+           "dq": torch.zeros(Z, nh, N, D, dtype=f), "dk": torch.zeros(Z, nk, N, D, dtype=f),
+           "dv": torch.zeros(Z, nk, N, D, dtype=f),
+           "dbias_blocks": torch.zeros(Z, nh, NB, NB, dtype=f)}
+    col_blk = torch.arange(N) // route_block
+    cols = torch.arange(N)
+
+    def rnd(x):
+        return x.to(io_dtype).to(f) if io_dtype is not None else x
+
+    for z in range(Z):
+        for gi, g in enumerate(kv_heads):
+            kf = k[z, g].to(f)
+            vf = v[z, g].to(f)
+            for j in range(G):
+                hi = gi * G + j
+                h = heads[hi]
+                for s0 in range(0, N, chunk):
+                    e0 = min(N, s0 + chunk)
+                    rows = torch.arange(s0, e0)
+                    qc = q[z, h, s0:e0].to(f)
+                    doc = dout[z, h, s0:e0].to(f)
+                    m = block_mask[z, h][rows // route_block][:, col_blk]
+                    if is_causal:
+                        m = m & (rows[:, None] >= cols[None, :])
+                    s = (qc @ kf.T) * scale
+                    s = s.masked_fill(~m, float("-inf"))
+                    lse = torch.logsumexp(s, dim=-1)
+                    lse_safe = torch.where(torch.isinf(lse), torch.zeros_like(lse), lse)
+                    p = torch.where(m, torch.exp(s - lse_safe[:, None]), torch.zeros_like(s))
+                    o = p @ vf
+                    res["out"][z, hi, s0:e0] = o
+                    res["lse"][z, hi, s0:e0] = lse
+                    dp = doc @ vf.T
+                    delta = (doc * rnd(o)).sum(-1, keepdim=True)
+                    ds = torch.where(m, p * (dp - delta), torch.zeros_like(p))
+                    ds_s = rnd(ds * scale)
+                    res["dq"][z, hi, s0:e0] = ds_s @ kf
+                    res["dk"][z, gi] += ds_s.T @ qc
+                    res["dv"][z, gi] += rnd(p).T @ doc
+                    # per-block sums of the unscaled dS: rows -> query blocks, cols -> key blocks
+                    qb = rows // route_block
+                    blk = torch.zeros(NB, N, dtype=f).index_add_(0, qb, ds)
+                    res["dbias_blocks"][z, hi] += torch.zeros(NB, NB, dtype=f).index_add_(
+                        1, col_blk, blk)
+    return res
