@@ -364,6 +364,13 @@ class C2Problem:
         self.bwd(3)
         evs[5].record()
 
+    def free_device(self):
+        """Drop the device tensors (the counts and host copies stay) to make room for
+        another process on this GPU."""
+        for name in ("q", "k", "v", "do", "router", "depth", "lists", "out", "lse", "dq", "dk",
+                     "dv", "ws", "fws"):
+            setattr(self, name, None)
+
     def step_plain(self):
         self.build()
         self.fwd()
@@ -811,19 +818,56 @@ def run_c5(dev, rank, world, steps, warmup, flush, barrier=None, cpu=False):
     return res
 
 
-C4 = dict(Z=4, H=4, Hkv=1, N=32768, D=128, RB=128, levels=8, depth=(3, 4, 4, 4), layers=32)
+C4 = dict(Z=4, H=4, Hkv=1, N=32768, D=128, RB=128, levels=8, p=2, r=4, depth=(3, 4, 4, 4),
+          local_blocks=1, layers=32)
 
 
-def run_c4(dev, rank, world, warmup, flush, barrier=None):
-    """C4 Llama-3.1-8B-shaped surgery prefill, the attention sublayer on one GPU's KV group:
-    batch 4, N=32768, 4 query heads / 1 KV head, D=128, route_block 128 (NB=256), 32 layers,
-    bf16, random init.  Per layer: that layer's Q/K/V and fresh random block routes (levels 8,
-    arity 2: a stand-in for the random-init router's per-block majority vote), then
-    build_block_lists(per-head depth 3/4/4/4, causal, sink, one local block) and the
-    block-list forward.  Depth r keeps ~2^-r of the causal triangle (plus sink and diagonal),
-    ~10 % on average over the four heads.  One step = all 32 layers; time = max over ranks."""
+def _torch_vote_glue(assign, r, rb):
+    """The reference's torch glue for the block vote (surgery.py:543-547), restated for a
+    same-GPU comparison: token argmax, one-hot, sum over each route block, argmax."""
+    B, H, S, _, p = assign.shape
+    nb = -(-S // rb)
+    idx = assign[:, :, :S, :r, :].argmax(dim=-1)
+    votes = torch.nn.functional.one_hot(idx, p).to(torch.float32)
+    if nb * rb != S:
+        votes = torch.nn.functional.pad(votes, (0, 0, 0, 0, 0, nb * rb - S))
+    return votes.view(B, H, nb, rb, r, p).sum(3).argmax(-1).to(torch.int32)
+
+
+def cpu_c4_baseline(q, k, v, bl, rows=1024):
+    """The reference's CPU path for one C4 layer slice: query head 0 of sequence 0, the last
+    ``rows`` query rows against all 32768 keys, masked dense fp32 (query-chunked form),
+    scaled by rows x heads x sequences x layers.  Returns (seconds per layer, sample s, scale)."""
+    from oracle import attention_oracle as ao
+    N, RB = C4["N"], C4["RB"]
+    lists, counts = bl.lists[:1, :1].cpu(), bl.counts[:1, :1].cpu()
+    bm = torch.zeros(1, 1, N // RB, N // RB, dtype=torch.bool)
+    for i in range(N // RB):
+        c = int(counts[0, 0, i])
+        bm[0, 0, i, lists[0, 0, i, :c].long()] = True
+    qs, ks, vs = (t[:1, :1].float().cpu() for t in (q, k, v))
+    t0 = time.perf_counter()
+    ao.masked_attention_chunked(qs, ks, vs, bm, RB, True, chunk=rows, compute_dtype=torch.float32,
+                                row_ranges=[(N - rows, N)])
+    s = time.perf_counter() - t0
+    scale = C4["Z"] * C4["H"] * N / rows
+    return s * scale, s, scale
+
+
+def run_c4(dev, rank, world, warmup, flush, barrier=None, cpu=False):
+    """C4 Llama-3.1-8B-shaped surgery prefill, the attention sublayer on one GPU's KV group
+    (the 8-GPU job splits the 32 heads by KV group): batch 4, N=32768, 4 query heads / 1 KV
+    head, D=128, route_block 128 (NB=256), 32 layers, bf16, random init.  Per layer: that
+    layer's Q/K/V and its router's per-token outputs (levels 8, p=2), then
+    build_block_lists_from_assignments -- per-block majority vote of the first r=4 levels,
+    per-head match depth 3/4/4/4, causal + sink + one local block -- and the block-list
+    forward.  Depth d keeps ~2^-d of the causal triangle (plus sink, diagonal and local
+    band), ~10 % on average over the four heads.  One step = all 32 layers; time = max over
+    ranks.  The router's projection is not part of this library: a random-init router's
+    argmax branches are uniformly random, so its outputs are drawn at random."""
     from ultrametric import build_block_lists
     from ultrametric.block_list import _fwd
+    from ultrametric.surgery_routing import build_block_lists_from_assignments
     Z, H, Hkv, N, D, RB, L = (C4[k] for k in ("Z", "H", "Hkv", "N", "D", "RB", "layers"))
     NB = N // RB
     g = torch.Generator(device=dev).manual_seed(400 + rank)
@@ -832,43 +876,79 @@ def run_c4(dev, rank, world, warmup, flush, barrier=None):
         layers.append((torch.randn(Z, H, N, D, generator=g, device=dev, dtype=torch.bfloat16),
                        torch.randn(Z, Hkv, N, D, generator=g, device=dev, dtype=torch.bfloat16),
                        torch.randn(Z, Hkv, N, D, generator=g, device=dev, dtype=torch.bfloat16),
-                       torch.randint(0, 2, (Z, H, NB, C4["levels"]), generator=g, device=dev,
-                                     dtype=torch.int32)))
+                       torch.randn(Z, H, N, C4["levels"], C4["p"], generator=g, device=dev,
+                                   dtype=torch.bfloat16)))
     scale = 1.0 / math.sqrt(D)
     depth = torch.tensor(C4["depth"], dtype=torch.int32, device=dev)
+    kw = dict(route_block=RB, req_depth=depth, is_causal=True, sink_block=True,
+              local_blocks=C4["local_blocks"], arity=C4["p"])
+
+    def lists_of(assign):
+        return build_block_lists_from_assignments(assign, C4["r"], **kw)
 
     def step(collect=None):
-        for q, k, v, routes in layers:
-            bl = build_block_lists(routes, depth, is_causal=True, sink_block=True,
-                                   local_blocks=1, arity=2)
+        for q, k, v, assign in layers:
+            bl = lists_of(assign)
             _fwd(q, k, v, bl.lists, bl.counts, RB, True, scale, True, None)
             if collect is not None:
                 collect.append(bl.counts.sum())
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        flush_l2(flush)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        return max_over_ranks([e0.elapsed_time(e1)], world, dev)[0]
 
     counts = []
     for _ in range(max(1, warmup)):
         step(counts if not counts else None)
     kept = int(torch.stack(counts).sum())
-    torch.cuda.synchronize()
-    if barrier:
-        barrier()
-    flush_l2(flush)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    step()
-    e1.record()
-    e1.synchronize()
-    ms = max_over_ranks([e0.elapsed_time(e1)], world, dev)[0]
+    ms = timed(step)
+    # the routing part alone, fused vs the reference's torch glue + builder on this GPU
+    ms_lists = timed(lambda: [lists_of(a) for *_, a in layers])
+
+    def glue():
+        for *_, a in layers:
+            route = _torch_vote_glue(a, C4["r"], RB)
+            build_block_lists(route, depth, is_causal=True, sink_block=True,
+                              local_blocks=C4["local_blocks"], arity=C4["p"])
+    glue()
+    ms_glue = timed(glue)
     causal_pairs = Z * H * NB * (NB + 1) // 2 * L
-    return {"config": "C4: Llama-3.1-8B-shaped attention sublayer per GPU, batch 4, N=32768, "
-                      "H=4/1 per GPU, D=128, RB=128, 32 layers, random block routes, per-head "
-                      "depth 3/4/4/4, causal + sink + local",
-            "layers": L, "ms_all_layers": round(ms, 3), "ms_per_layer": round(ms / L, 4),
-            "kept_blocks_all_layers": kept,
-            "density_causal": round(kept / causal_pairs, 4),
-            "kept_tflops": round(kept * 4 * RB * RB * D / (ms * 1e-3) / 1e12, 2),
-            "whole_job_kept_tflops": round(world * kept * 4 * RB * RB * D / (ms * 1e-3) / 1e12, 2),
-            "timed": "per layer: list build + forward (router projection not included)"}
+    flops = kept * 4 * RB * RB * D
+    res = {"config": "C4: Llama-3.1-8B-shaped attention sublayer per GPU (1 of 8 KV groups), "
+                     "batch 4, N=32768, H=4/1 per GPU, D=128, RB=128, 32 layers, router outputs "
+                     "levels 8 p 2 -> majority vote r=4, per-head depth 3/4/4/4, causal + sink + local",
+           "layers": L, "ms_all_layers": round(ms, 3), "ms_per_layer": round(ms / L, 4),
+           "kept_blocks_all_layers": kept,
+           "density_causal": round(kept / causal_pairs, 4),
+           "kept_tflops": round(flops / (ms * 1e-3) / 1e12, 2),
+           "whole_job_kept_tflops": round(world * flops / (ms * 1e-3) / 1e12, 2),
+           "routing_ms_per_layer": {"fused_vote_and_lists": round(ms_lists / L, 4),
+                                    "torch_vote_glue_plus_builder": round(ms_glue / L, 4)},
+           "timed": "per layer: router outputs -> vote + lists (one C-ABI call) -> forward; "
+                    "router projection not included"}
+    if cpu and rank == 0 and world == 1:
+        torch.set_num_threads(os.cpu_count() or 1)
+        q, k, v, a = layers[0]
+        cpu_layer_s, sample_s, sc = cpu_c4_baseline(q, k, v, lists_of(a))
+        res["cpu_baseline"] = {"value": round(flops / L / cpu_layer_s / 1e12, 6), "unit": "TFLOP/s",
+                               "ms_per_layer": round(cpu_layer_s * 1e3, 1),
+                               "cores": torch.get_num_threads(), "kind": "port",
+                               "measured_s": round(sample_s, 3), "scale": sc,
+                               "sample": "masked dense fp32 forward of layer 0, sequence 0, head 0: "
+                                         "the last 1024 query rows against all 32768 keys, scaled "
+                                         "by 4 sequences x 4 heads x 32768 rows / 1024 rows per "
+                                         "layer; rate on kept-block FLOPs"}
+    del layers
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------------------------------------------
@@ -1103,7 +1183,7 @@ def run_ours(args):
         extras["sweep"] = run_sweep(dev, flush, steps=5)  # per GPU (rank 0's numbers)
         extras["c5"] = run_c5(dev, rank, world, max(3, args.steps // 2), args.warmup, flush, barrier,
                               cpu=not args.no_cpu)
-        extras["c4"] = run_c4(dev, rank, world, 1, flush, barrier)
+        extras["c4"] = run_c4(dev, rank, world, 1, flush, barrier, cpu=not args.no_cpu)
         extras["decode"] = run_decode(dev, rank, args.steps, args.warmup, flush, peaks, world, rank,
                                       barrier, cpu=not args.no_cpu)
     if world > 1:
@@ -1125,7 +1205,7 @@ def run_ours(args):
 
     ref_triton = None
     if rank == 0 and world == 1 and not args.quick and not args.no_reference_triton:
-        del prob
+        prob.free_device()
         torch.cuda.empty_cache()
         ref_triton = run_reference_triton_subprocess()
 

@@ -107,6 +107,35 @@ SA_API int sa_build_transposed_block_lists(const int32_t* lists, int64_t list_st
                                     int32_t* k_slots, void* stream);
 
 /*
+ * Router outputs -> block routes -> ascending block lists, all on the device.
+ * Replaces: src/llama_surgery/surgery.py:533-547 (token argmax, per-block majority vote by
+ * one-hot sums and argmax, or the argmax of block-level assignments) followed by the
+ * build_block_lists(block_route, r, ..., arity=p) call of :562-564.
+ *
+ * assignments       (Z, H, S, levels, num_branches) of dtype (SA_F32/F16/BF16), any strides.
+ * tokens_per_block  route block length in rows of `assignments`: route_block for
+ *                   token-level outputs, 1 for block-level ones.  NB = ceil(S / it).
+ * r                 levels that vote (0..min(levels, 32)); num_branches <= 16.
+ *                   A block's branch per level is the majority of its rows' argmax branches
+ *                   (first maximum wins within a row; vote ties go to the lowest branch id;
+ *                   rows at or past S do not vote).
+ * req_depth         device int32 (H,): levels that must agree per head (<= r).
+ * arity             branch count; prefix codes use base max(2, arity) (the sync-free path).
+ * block_route       (Z, H, NB, r) int32 out, contiguous (written only when r > 0).
+ * lists/counts      as sa_build_block_lists.
+ * Two launches on `stream` (vote, then compaction as its programmatic dependent); no
+ * host synchronisation.
+ */
+SA_API int sa_build_block_lists_from_assignments(const void* assignments, int dtype,
+                                          const int64_t* strides, int64_t Z, int64_t H,
+                                          int64_t S, int64_t levels, int64_t num_branches,
+                                          int64_t tokens_per_block, int64_t r,
+                                          const int32_t* req_depth, int64_t arity,
+                                          int is_causal, int sink_block, int64_t local_blocks,
+                                          int32_t* block_route, int32_t* lists,
+                                          int64_t list_stride, int32_t* counts, void* stream);
+
+/*
  * Block-list attention forward.
  * Replaces: src/ultrametric/block_list.py:688-757 (_block_list_attention_fwd, kernel
  * :387-470).  Semantics: for each query row, online softmax over the keys of the route

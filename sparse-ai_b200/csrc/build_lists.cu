@@ -50,6 +50,9 @@ __device__ __forceinline__ bool levels_equal(const BuildParams& p, int64_t oa, i
 // match = equal prefix OR |i-j| <= local OR (sink and j == 0); AND j <= i when causal.
 __global__ void __launch_bounds__(kBuildThreads) build_lists_kernel(BuildParams p) {
   extern __shared__ uint64_t s_codes[];
+  // launched as a programmatic dependent (after the route vote), the routes are complete
+  // only past this point; otherwise a no-op
+  pdl_wait();
   const int64_t zh = blockIdx.y;
   const int64_t z = zh / p.H, h = zh % p.H;
   const int d = p.depth[h];
@@ -170,22 +173,11 @@ int launch_transpose_lists(const int32_t* lists, int64_t list_stride, const int3
   return check_launch("transpose_lists_kernel");
 }
 
-}  // namespace sa
-
-extern "C" {
-
-int sa_build_block_lists(const void* router, int router_dtype, const int64_t* router_strides,
-                         int64_t Z, int64_t H, int64_t NB, int64_t TD, const int32_t* req_depth,
-                         int64_t base, int use_codes, int is_causal, int sink_block,
-                         int64_t local_blocks, int32_t* lists, int64_t list_stride,
-                         int32_t* counts, void* stream) {
-  using namespace sa;
-  if (Z < 0 || H < 0 || NB < 0 || TD < 0) return fail(SA_EINVAL, "negative size");
-  if (Z * H * NB == 0) return SA_OK;
-  if (!router || !req_depth || !lists || !counts || !router_strides)
-    return fail(SA_EINVAL, "null pointer argument");
-  if (router_dtype != SA_I32 && router_dtype != SA_I64)
-    return fail(SA_EUNSUPPORTED, "router_indices must be int32 or int64");
+int launch_build_lists(const void* router, int router_dtype, const int64_t* router_strides,
+                       int64_t Z, int64_t H, int64_t NB, int64_t TD, const int32_t* req_depth,
+                       int64_t base, int use_codes, int is_causal, int sink_block,
+                       int64_t local_blocks, int32_t* lists, int64_t list_stride,
+                       int32_t* counts, cudaStream_t stream, bool dependent) {
   if (list_stride < 1) return fail(SA_EINVAL, "list_stride must be >= 1");
   if (use_codes && NB > 16384)
     return fail(SA_EUNSUPPORTED, "more than 16384 route blocks per head");
@@ -211,8 +203,32 @@ int sa_build_block_lists(const void* router, int router_dtype, const int64_t* ro
     cudaFuncSetAttribute(build_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
   dim3 grid((unsigned)((NB + kBuildRowsPerCta - 1) / kBuildRowsPerCta), (unsigned)(Z * H));
-  build_lists_kernel<<<grid, kBuildThreads, smem, (cudaStream_t)stream>>>(p);
+  if (dependent)
+    return launch_dependent(build_lists_kernel, grid, dim3(kBuildThreads), smem, stream,
+                            "build_lists_kernel", p);
+  build_lists_kernel<<<grid, kBuildThreads, smem, stream>>>(p);
   return check_launch("build_lists_kernel");
+}
+
+}  // namespace sa
+
+extern "C" {
+
+int sa_build_block_lists(const void* router, int router_dtype, const int64_t* router_strides,
+                         int64_t Z, int64_t H, int64_t NB, int64_t TD, const int32_t* req_depth,
+                         int64_t base, int use_codes, int is_causal, int sink_block,
+                         int64_t local_blocks, int32_t* lists, int64_t list_stride,
+                         int32_t* counts, void* stream) {
+  using namespace sa;
+  if (Z < 0 || H < 0 || NB < 0 || TD < 0) return fail(SA_EINVAL, "negative size");
+  if (Z * H * NB == 0) return SA_OK;
+  if (!router || !req_depth || !lists || !counts || !router_strides)
+    return fail(SA_EINVAL, "null pointer argument");
+  if (router_dtype != SA_I32 && router_dtype != SA_I64)
+    return fail(SA_EUNSUPPORTED, "router_indices must be int32 or int64");
+  return launch_build_lists(router, router_dtype, router_strides, Z, H, NB, TD, req_depth, base,
+                            use_codes, is_causal, sink_block, local_blocks, lists, list_stride,
+                            counts, (cudaStream_t)stream, false);
 }
 
 int sa_build_transposed_block_lists(const int32_t* lists, int64_t list_stride,
