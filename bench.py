@@ -264,7 +264,7 @@ class C2Problem:
     always drawn for the whole C2 problem from the seed, then sliced, so every split sees
     the same numbers."""
 
-    def __init__(self, dev, seed, t_heads, causal=True, sink=True, kv_groups=None):
+    def __init__(self, dev, seed, t_heads, causal=True, sink=True, kv_groups=None, fused=True):
         from ultrametric import _native as nat
         self.nat = nat
         self.dev = dev
@@ -305,8 +305,12 @@ class C2Problem:
         torch.cuda.synchronize()
         self.kept = int(self.counts.sum())
         RB2D = RB * RB * D
-        self.flops = {"fwd": self.kept * 4 * RB2D, "dq": self.kept * 6 * RB2D,
-                      "dkdv": self.kept * 8 * RB2D}
+        # per-kernel tensor work: the fused backward does S^T, dP^T, dV, dK, dQ (10 RB^2 D per
+        # kept pair); the two-kernel path recomputes S and dP in both kernels (6 + 8)
+        self.fused = fused
+        self.flops = {"fwd": self.kept * 4 * RB2D, "bwd": self.kept * 10 * RB2D,
+                      "dq": self.kept * 6 * RB2D, "dkdv": self.kept * 8 * RB2D}
+        self.parts = ("build", "fwd", "prep", "bwd") if fused else ("build", "fwd", "prep", "dq", "dkdv")
         self.flops_alg = self.kept * 14 * RB2D
         # compulsory bytes of the forward: Q, O, LSE and each referenced K/V block once per KV head
         ref_kv = torch.zeros(Z, self.Hkv, NB, dtype=torch.bool, device=dev)
@@ -347,9 +351,14 @@ class C2Problem:
             self.dv.data_ptr(), nat.strides(self.dv), None, self.ws.data_ptr(), self.ws.numel(), s),
             f"bwd phase {phase}")
 
-    PARTS = ("build", "fwd", "prep", "dq", "dkdv")
-    # fwd: planner + kernel; prep: delta, transposed lists, 2 planners; dkdv: kernel + split reduce
-    LAUNCHES = {"build": 1, "fwd": 2, "prep": 4, "dq": 1, "dkdv": 2}
+    # our kernels per part.  fwd: planner + kernel.  Fused path -- prep: Delta (+ zeroing of
+    # the dQ accumulator), transposed lists, dK/dV planner; bwd: fused kernel + split reduce.
+    # Two-kernel path -- prep: Delta, transposed lists, planner; dq: planner + kernel; dkdv:
+    # kernel + split reduce.
+    LAUNCHES = {"build": 1, "fwd": 2, "prep": 3, "bwd": 2, "dq": 2, "dkdv": 2}
+
+    def launches(self):
+        return sum(self.LAUNCHES[p] for p in self.parts)
 
     def step(self, evs):
         evs[0].record()
@@ -357,12 +366,18 @@ class C2Problem:
         evs[1].record()
         self.fwd()
         evs[2].record()
-        self.bwd(1)
-        evs[3].record()
-        self.bwd(2)
-        evs[4].record()
-        self.bwd(3)
-        evs[5].record()
+        if self.fused:
+            self.bwd(4)
+            evs[3].record()
+            self.bwd(5)
+            evs[4].record()
+        else:
+            self.bwd(1)
+            evs[3].record()
+            self.bwd(2)
+            evs[4].record()
+            self.bwd(3)
+            evs[5].record()
 
     def free_device(self):
         """Drop the device tensors (the counts and host copies stay) to make room for
@@ -374,9 +389,8 @@ class C2Problem:
     def step_plain(self):
         self.build()
         self.fwd()
-        self.bwd(1)
-        self.bwd(2)
-        self.bwd(3)
+        for ph in ((4, 5) if self.fused else (1, 2, 3)):
+            self.bwd(ph)
 
 
 def flush_l2(buf):
@@ -384,10 +398,11 @@ def flush_l2(buf):
 
 
 def time_c2(prob, steps, warmup, flush, barrier=None):
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
+    ne = len(prob.parts) + 1
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(ne)] for _ in range(steps)]
     for _ in range(warmup):
         flush_l2(flush)
-        prob.step([torch.cuda.Event(enable_timing=True) for _ in range(6)])
+        prob.step([torch.cuda.Event(enable_timing=True) for _ in range(ne)])
     torch.cuda.synchronize()
     if barrier:
         barrier()
@@ -399,12 +414,12 @@ def time_c2(prob, steps, warmup, flush, barrier=None):
     if barrier:
         barrier()
     torch.cuda.synchronize()
-    parts = {p: [] for p in C2Problem.PARTS}
+    parts = {p: [] for p in prob.parts}
     totals = []
     for e in evs:
-        for j, p in enumerate(C2Problem.PARTS):
+        for j, p in enumerate(prob.parts):
             parts[p].append(e[j].elapsed_time(e[j + 1]))
-        totals.append(e[0].elapsed_time(e[5]))
+        totals.append(e[0].elapsed_time(e[ne - 1]))
     return sum(totals), {p: statistics.mean(v) for p, v in parts.items()}
 
 
@@ -528,7 +543,7 @@ def run_sweep(dev, flush, steps):
         ms = total / steps
         kept = prob.kept
         fwd_tf = prob.flops["fwd"] / (parts["fwd"] * 1e-3) / 1e12
-        bwd_ms = parts["prep"] + parts["dq"] + parts["dkdv"]
+        bwd_ms = sum(v for k, v in parts.items() if k not in ("build", "fwd"))
         sd = time_sdpa(prob, causal)
         rows.append({
             "target": name, "threshold": t, "causal": causal, "sink": sink, "kept_blocks": kept,
@@ -1141,6 +1156,7 @@ def run_ours(args):
 
     t_heads = c2_thresholds(0) if args.threshold is None else [args.threshold] * C2["H"]
     prob = C2Problem(dev, seed=rank, t_heads=t_heads)
+    prob_launches = prob.launches()
     with ClockSampler(local) as clk:
         total_ms, parts = time_c2(prob, args.steps, args.warmup, flush, barrier)
     keys = list(parts)
@@ -1151,13 +1167,25 @@ def run_ours(args):
     value = prob.flops_alg * world / (ms_step * 1e-3) / 1e12
 
     # dominant kernel roofline (tensor-bound kernels of the step)
-    kern = max(("fwd", "dq", "dkdv"), key=lambda p: parts[p])
+    kern = max((p for p in prob.parts if p in prob.flops), key=lambda p: parts[p])
     achieved = prob.flops[kern] / (parts[kern] * 1e-3) / 1e12
     traffic = None
     tf = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tf):
         with open(tf) as f:
             traffic = json.load(f).get(kern)
+
+    # the reproducible two-kernel backward (deterministic=True) on the same problem, for scale
+    det = C2Problem(dev, seed=rank, t_heads=t_heads, fused=False)
+    tot_d, parts_d = time_c2(det, args.steps, args.warmup, flush, barrier)
+    keys_d = list(parts_d)
+    red_d = max_over_ranks([tot_d] + [parts_d[k] for k in keys_d], world, dev)
+    two_kernel = {"ms_per_step": round(red_d[0] / args.steps, 4),
+                  "breakdown_ms": {k: round(v, 4) for k, v in zip(keys_d, red_d[1:])},
+                  "note": "deterministic=True: separate dQ and dK/dV kernels (14 RB^2 D of MMA "
+                          "work per kept pair against the fused kernel's 10)"}
+    del det
+    torch.cuda.empty_cache()
 
     graph = time_c2_graph(prob, args.steps, args.warmup, flush)
     if "ms_per_step" in graph:
@@ -1240,8 +1268,9 @@ def run_ours(args):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "ultrametric.block_list_attention autograd (ctypes -> C ABI)"},
             "clocks": clk.summary(),
-            "gpu_launches": sum(C2Problem.LAUNCHES.values()) * args.steps,
+            "gpu_launches": prob_launches * args.steps,
             "cuda_graph": graph,
+            "two_kernel_backward": two_kernel,
             **extras,
         }
         if strong is not None:

@@ -58,6 +58,10 @@ int fill_common(AttnParams& p, int dtype, int64_t Z, int64_t H, int64_t Hkv, int
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace
+
+// Shapes the fused single-pass backward can take (dtype and alignment are checked at launch);
+// their workspace carries its fp32 dQ accumulator.
+bool fused_shape(int64_t D, int64_t RB) { return D == 128 && RB % 128 == 0; }
 }  // namespace sa
 
 extern "C" {
@@ -153,6 +157,11 @@ int64_t sa_block_list_attention_bwd_workspace_bytes(int64_t Z, int64_t H, int64_
   b += align256((size_t)Z * H * ((N + 63) / 64) * 128 * sizeof(float));  // row stats
   b += align256((size_t)sa::bwd_plan_bytes(sa::kPlanDq, Z, H, Hkv, N, D));
   b += align256((size_t)sa::bwd_plan_bytes(sa::kPlanDkdv, Z, H, Hkv, N, D));
+  if (sa::fused_shape(D, route_block)) {
+    b += align256((size_t)Z * H * N * D * sizeof(float));        // fp32 dQ accumulator
+    b += align256((size_t)Z * H * ((N + 63) / 64) * sizeof(int32_t));  // sub-tile counters
+    b += align256((size_t)Z * H * NB * sizeof(int32_t));           // contributions per block
+  }
   return (int64_t)b;
 }
 
@@ -217,12 +226,29 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
   p.plan_dq = w;
   w += align256((size_t)bwd_plan_bytes(kPlanDq, Z, H, Hkv, N, D));
   p.plan_dkdv = w;
+  w += align256((size_t)bwd_plan_bytes(kPlanDkdv, Z, H, Hkv, N, D));
   p.k_lists = k_lists;
   p.k_slots = k_slots;
   p.q_counts = q_counts;
 
-  if (phase < 0 || phase > 3) return fail(SA_EINVAL, "backward phase must be 0..3");
-  if (phase == 0 || phase == 1) {
+  if (phase < 0 || phase > 5) return fail(SA_EINVAL, "backward phase must be 0..5");
+  // phase 0 = the whole backward, fused when the shape allows; 1-3 = the two-kernel path
+  // (prep, dQ, dK/dV: reproducible dQ sums); 4-5 = the fused path (prep, fused kernel)
+  const bool fused = (phase == 0 || phase >= 4) && fused_shape(D, route_block) && bwd_fused_eligible(p);
+  if (fused) {
+    p.dq_acc = reinterpret_cast<float*>(w);
+    w += align256((size_t)Z * H * N * D * sizeof(float));
+    p.dq_cnt = reinterpret_cast<int32_t*>(w);
+    w += align256((size_t)Z * H * ((N + 63) / 64) * sizeof(int32_t));
+    p.dq_expect = reinterpret_cast<int32_t*>(w);
+  }
+  if (phase == 4 && !fused) phase = 1;  // shapes without the fused kernel: two-kernel path
+  if (phase == 5 && !fused) {
+    rc = launch_bwd_sm100(p, s, kBwdDq | kBwdDkDv);
+    if (rc != SA_EUNSUPPORTED) return rc;
+    return launch_bwd_simt(p, s, kBwdDq | kBwdDkDv);
+  }
+  if (phase == 0 || phase == 1 || phase == 4) {
     // Delta (HBM-bound, a wide grid) runs on the caller's stream; the transposition and the
     // dK/dV planner (small, latency-bound, independent of Delta) on a high-priority second
     // stream beside it.  The caller's stream waits for both.  (The dQ planner runs with the
@@ -233,8 +259,11 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
     if (rc) return rc;
     if (cudaEventRecord(fork, s) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
       return check_launch("backward fork");
-    rc = launch_transpose_lists(lists, list_stride, counts, Z * H, NB, NB, k_lists, NB,
-                                q_counts, k_slots, 0, side);
+    if (fused && cudaMemsetAsync(p.dq_expect, 0, (size_t)Z * H * NB * sizeof(int32_t), side) != cudaSuccess)
+      rc = check_launch("memset dQ contribution counts");
+    if (!rc)
+      rc = launch_transpose_lists(lists, list_stride, counts, Z * H, NB, NB, k_lists, NB,
+                                  q_counts, k_slots, 0, side, fused ? p.dq_expect : nullptr);
     if (!rc) rc = plan_bwd_sm100(p, side, kBwdDkDv);
     if (cudaEventRecord(join, side) != cudaSuccess) return check_launch("backward join");
     if (!rc) rc = launch_delta(p, s);
@@ -247,7 +276,8 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
         return check_launch("memset d_soft_bias");
     }
   }
-  const int parts = phase == 0 ? (kBwdDq | kBwdDkDv) : phase == 2 ? kBwdDq : phase == 3 ? kBwdDkDv : 0;
+  int parts = phase == 0 ? (kBwdDq | kBwdDkDv) : phase == 2 ? kBwdDq : phase == 3 ? kBwdDkDv : 0;
+  if (fused && (phase == 0 || phase == 5)) parts = kBwdFused;
   if (!parts) return SA_OK;
   rc = launch_bwd_sm100(p, s, parts);
   if (rc != SA_EUNSUPPORTED) return rc;

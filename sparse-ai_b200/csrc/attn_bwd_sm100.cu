@@ -72,6 +72,13 @@ struct BwdArgs {
   unsigned* status;
   SchedArgs sched;
   float* partials;  // dK/dV: fp32 [slot][128][dV D | dK D] for split chunks
+  // fused kernel: fp32 dQ accumulator (Z*H, N, D) contiguous, per 64-row query sub-tile
+  // arrival counters (Z*H, ceil(N/64)), and the number of key blocks whose transposed list
+  // holds each query block (Z*H, NB): a sub-tile is complete after that many x RB/128
+  // arrivals
+  float* dq_acc;
+  int32_t* dq_cnt;
+  const int32_t* dq_expect;
 };
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
@@ -799,6 +806,435 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
   }
 }
 
+// =======================================================================================
+// fused dK / dV / dQ kernel (head_dim 128): one pass over the transposed lists
+// =======================================================================================
+//
+// The dK/dV kernel's pipeline plus, per streamed 64-row query sub-tile,
+//    dQ^T[b] = K^T dS^T   (M=128 head-dim rows, N=64 query rows, K=128 keys)
+// with K^T read MN-major from the resident K tile, dS^T (bf16) written by the elementwise
+// warps into shared memory as well as TMEM, and the accumulator in the dP^T[b] columns, which
+// are free once the elementwise warps have read dP^T.  P^T and dS^T (bf16 pairs) both go into
+// the S^T[b] columns: half hc of the 64 query columns puts P^T at [32 hc, 32 hc + 16) and dS^T
+// at [32 hc + 16, 32 hc + 32).  The owning elementwise group then reads the dQ^T tile out of
+// TMEM, releases the columns and adds it into an fp32 dQ accumulator in global memory
+// (red.global.add.f32: per warp and query row one coalesced 128-byte reduction at L2).  The
+// group that brings a query sub-tile's last contribution (an arrival counter per 64-row
+// sub-tile) converts its 64 accumulated rows to dQ.  Tensor work per kept pair is 10 RB^2 D
+// (S^T, dP^T, dV, dK, dQ) against 14 for the separate dQ and dK/dV kernels, and there is one
+// elementwise pass instead of two.  dQ's summation order depends on timing (atomics), so it is
+// not bitwise reproducible from run to run; the two-kernel path is.
+//
+// The MMA thread polls its barriers instead of following a fixed order: it issues S^T/dP^T of
+// the next sub-tile as soon as its stage is loaded and its TMEM buffer drained, and the
+// accumulating MMAs of the oldest pending sub-tile as soon as its P^T/dS^T are written, so the
+// tensor pipe is fed whichever way the elementwise and drain latencies fall.  The
+// accumulating MMAs stay in sub-tile order (dV and dK sums are reproducible).
+
+constexpr int kFuStages = 3;
+
+struct FuLayout {
+  static constexpr int D = 128;
+  static constexpr uint32_t kK = 0;                      // [128][128] (2 boxes of 64 columns)
+  static constexpr uint32_t kV = kRows * D * 2;
+  static constexpr uint32_t kQD = 2 * kRows * D * 2;     // stages x (Q, dO, stats)
+  static constexpr uint32_t kStats = 2 * kSub * D * 2;
+  static constexpr uint32_t kStage = kStats + 1024;
+  static constexpr uint32_t kDsT = kQD + kFuStages * kStage;  // 2 x dS^T [128 keys][64 q] bf16
+  static constexpr uint32_t kDsTBytes = kRows * kSub * 2;
+  static constexpr uint32_t kBars = kDsT + 2 * kDsTBytes;
+  static constexpr uint32_t kMeta = kBars + 256;  // FuMeta[kFuStages]
+  static constexpr uint32_t kFlag = kMeta + 128;  // per group: "this sub-tile is complete"
+  static constexpr uint32_t kRingOff = kFlag + 64;
+  static constexpr uint32_t kAlloc = kRingOff + 128 + 1024;
+  static_assert(kDsT % 1024 == 0 && kStage % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+  static_assert(kAlloc <= 232448, "fused backward shared-memory layout too large");
+};
+
+struct FuMeta {
+  int64_t start;     // first query row of the sub-tile
+  int64_t zh;        // z * H + h of its query head
+  int64_t bias_idx;  // d_soft_bias element of the block pair, or -1
+  float b2;          // soft bias * log2(e)
+  int qb;            // query block
+};
+static_assert(sizeof(FuMeta) == 32, "FuMeta layout");
+
+enum { FU_KVFULL = 0, FU_KVEMPTY, FU_QFULL0, FU_QEMPTY0 = FU_QFULL0 + kFuStages,
+       FU_SFULL0 = FU_QEMPTY0 + kFuStages, FU_PFULL0 = FU_SFULL0 + 2, FU_DQFULL0 = FU_PFULL0 + 2,
+       FU_DQEMPTY0 = FU_DQFULL0 + 2, FU_DONE = FU_DQEMPTY0 + 2, FU_EPI, FU_GSYNC0,
+       FU_WFULL0 = FU_GSYNC0 + 2, FU_WEMPTY0 = FU_WFULL0 + kRing, FU_NUM = FU_WEMPTY0 + kRing };
+static_assert(FU_NUM * 8 <= 256, "fused backward barriers");
+
+template <bool BF16>
+__global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const __grid_constant__ BwdArgs a) {
+  using L = FuLayout;
+  constexpr int D = L::D;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
+  FuMeta* meta = reinterpret_cast<FuMeta*>(sm + L::kMeta);
+  volatile int* flag = reinterpret_cast<volatile int*>(sm + L::kFlag);
+  WorkEntry* ring = reinterpret_cast<WorkEntry*>(sm + L::kRingOff);
+  __shared__ uint32_t s_tmem;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    uint32_t cnt[FU_NUM];
+    for (int i = 0; i < FU_NUM; ++i) cnt[i] = 1;
+    for (int b = 0; b < 2; ++b) {
+      cnt[FU_PFULL0 + b] = kEwThreads / 2;   // the owning group
+      cnt[FU_DQEMPTY0 + b] = kEwThreads / 2;
+      cnt[FU_GSYNC0 + b] = kEwThreads / 2;   // group-wide sync of group b
+    }
+    cnt[FU_EPI] = kEwThreads;  // both groups have read the dV / dK accumulators
+    for (int i = 0; i < kRing; ++i) cnt[FU_WEMPTY0 + i] = 1 + kEwThreads;
+    init_bars(bars, cnt, FU_NUM);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&a.tm_q);
+      prefetch_tmap(&a.tm_do);
+      prefetch_tmap(&a.tm_k);
+      prefetch_tmap(&a.tm_v);
+      uint32_t qd = 0, jk = 0;
+      bool ok = true;
+      auto weight = [&](int64_t i) { return kv_item_tiles(a, kv_item(a, i)); };
+      WorkFetcher fetch;
+      fetch.init(&a.sched, weight);
+      for (uint32_t w = 0; ok; ++w) {
+        const WorkEntry e = fetch.next(weight);
+        if (!(ok = ring_put(ring, &bars[FU_WFULL0], &bars[FU_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const KvItem it = kv_item(a, e.item);
+        if (e.end == e.begin) {
+          fetch.reserve(weight);
+          continue;
+        }
+        if (!(ok = mbar_wait(&bars[FU_KVEMPTY], (jk & 1) ^ 1, a.status))) break;
+        ++jk;
+        mbar_arrive_expect_tx(&bars[FU_KVFULL], 2 * kRows * D * 2);
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(sm + L::kK + c * kRows * 128, &a.tm_k, &bars[FU_KVFULL], c * 64, (int)it.k0,
+                      (int)it.hk, (int)it.z);
+          tma_load_4d(sm + L::kV + c * kRows * 128, &a.tm_v, &bars[FU_KVFULL], c * 64, (int)it.k0,
+                      (int)it.hk, (int)it.z);
+        }
+        uint32_t done = 0;
+        ok = for_each_qtile(a, it, e.begin, e.end,
+                            [&](int64_t h, int64_t qb, int64_t slot, int64_t q0) -> bool {
+          const uint32_t st = qd % kFuStages, ph = (qd / kFuStages) & 1;
+          if (!mbar_wait(&bars[FU_QEMPTY0 + st], ph ^ 1, a.status)) return false;
+          unsigned char* stage = sm + L::kQD + st * L::kStage;
+          const int64_t zh = it.z * a.H + h;
+          meta[st].start = q0;
+          meta[st].zh = zh;
+          meta[st].bias_idx = a.dbias ? (zh * a.NB + qb) * a.list_stride + slot : -1;
+          meta[st].b2 = bias_log2(a, it.z, h, qb, slot);
+          meta[st].qb = (int)qb;
+          mbar_arrive_expect_tx(&bars[FU_QFULL0 + st], L::kStats + 2 * kSub * 4);
+          for (int c = 0; c < D / 64; ++c) {
+            tma_load_4d(stage + c * kSub * 128, &a.tm_q, &bars[FU_QFULL0 + st], c * 64, (int)q0,
+                        (int)h, (int)it.z);
+            tma_load_4d(stage + kSub * D * 2 + c * kSub * 128, &a.tm_do, &bars[FU_QFULL0 + st],
+                        c * 64, (int)q0, (int)h, (int)it.z);
+          }
+          bulk_load(stage + L::kStats, a.stats + (zh * ((a.N + kSub - 1) / kSub) + q0 / kSub) * 2 * kSub,
+                    2 * kSub * 4, &bars[FU_QFULL0 + st]);
+          ++qd;
+          if ((int)++done == e.end - e.begin) fetch.reserve(weight);
+          return true;
+        });
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_f16(kRows, kSub, BF16, false, false);
+      constexpr uint32_t id_acc = idesc_f16(kRows, D, BF16, false, true);
+      // dQ^T = K^T dS^T: A (head dim x keys) and B (keys x query rows) both MN-major
+      constexpr uint32_t id_dq = idesc_f16(kRows, kSub, BF16, true, true);
+      const uint32_t k_addr = smem_u32(sm + L::kK), v_addr = smem_u32(sm + L::kV);
+      const uint32_t ds_addr = smem_u32(sm + L::kDsT);
+      uint32_t ga = 0, gb = 0, jk = 0, n_items = 0;  // sub-tiles with A / B issued (all items)
+      bool ok = true;
+      for (uint32_t w = 0; ok; ++w) {
+        WorkEntry e;
+        if (!(ok = ring_get(ring, &bars[FU_WFULL0], &bars[FU_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const int n = e.end - e.begin;
+        if (n == 0) continue;
+        if (!(ok = mbar_wait(&bars[FU_KVFULL], jk & 1, a.status))) break;
+        ++jk;
+        int ia = 0, ib = 0;
+        long long idle_since = clock64();
+        while (ib < n) {
+          bool progressed = false;
+          // A: S^T / dP^T of sub-tile ga into TMEM buffer ga & 1.  The buffer's S^T columns
+          // are free once the accumulating MMAs of sub-tile ga - 2 are issued (ia - ib < 2;
+          // MMAs execute in issue order), its dP^T columns once that sub-tile's dQ^T tile
+          // was read out (DQEMPTY).
+          if (ia < n && ia - ib < 2) {
+            const uint32_t st = ga % kFuStages, ph = (ga / kFuStages) & 1, sb = ga & 1;
+            const bool drained = ga < 2 || mbar_try_wait(&bars[FU_DQEMPTY0 + sb], ((ga >> 1) - 1) & 1);
+            if (drained && mbar_try_wait(&bars[FU_QFULL0 + st], ph)) {
+              tc_fence_after();
+              const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
+              const uint32_t do_addr = q_addr + kSub * D * 2;
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t oa = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+                const uint32_t ob = (kk >> 2) * (kSub * 128) + (kk & 3) * 32;
+                tc_mma_f16(tmem + kColS + sb * kSub, smem_desc(k_addr + oa, 16, 1024),
+                           smem_desc(q_addr + ob, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+                tc_mma_f16(tmem + kColP + sb * kSub, smem_desc(v_addr + oa, 16, 1024),
+                           smem_desc(do_addr + ob, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+              }
+              tc_commit(&bars[FU_SFULL0 + sb]);
+              ++ga;
+              ++ia;
+              progressed = true;
+            }
+          }
+          // B: dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T of the oldest pending sub-tile.  The
+          // item's first one overwrites the dV / dK accumulators: the previous item's epilogue
+          // must have read them (EPI).
+          if (ib < ia) {
+            const uint32_t pb = gb & 1;
+            const bool epi_ok = ib > 0 || n_items == 0 || mbar_try_wait(&bars[FU_EPI], (n_items - 1) & 1);
+            if (epi_ok && mbar_try_wait(&bars[FU_PFULL0 + pb], (gb >> 1) & 1)) {
+              tc_fence_after();
+              const uint32_t st = gb % kFuStages;
+              const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
+              const uint32_t do_addr = q_addr + kSub * D * 2;
+              const uint32_t colS = kColS + pb * kSub;
+#pragma unroll
+              for (int kk = 0; kk < kSub / 16; ++kk) {
+                const uint32_t acc = (ib > 0 || kk > 0) ? 1u : 0u;
+                const uint32_t pcol = colS + (kk >> 1) * 32 + (kk & 1) * 8;  // P^T, then dS^T + 16
+                tc_mma_f16_ts(tmem + kColAcc, tmem + pcol,
+                              smem_desc(do_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
+                tc_mma_f16_ts(tmem + kColAcc + D, tmem + pcol + 16,
+                              smem_desc(q_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
+              }
+              const uint32_t dsb = ds_addr + pb * L::kDsTBytes;
+#pragma unroll
+              for (int kk = 0; kk < kRows / 16; ++kk)
+                tc_mma_f16(tmem + kColP + pb * kSub,
+                           smem_desc(k_addr + kk * 16 * 128, kRows * 128, 1024),
+                           smem_desc(dsb + kk * 16 * 128, kSub * 128, 1024), id_dq, kk > 0 ? 1u : 0u);
+              tc_commit(&bars[FU_QEMPTY0 + st]);
+              tc_commit(&bars[FU_DQFULL0 + pb]);
+              ++gb;
+              ++ib;
+              progressed = true;
+            }
+          }
+          if (progressed) {
+            idle_since = clock64();
+          } else if (clock64() - idle_since > (1ll << 31)) {
+            raise_status(a.status, kStatusWaitTimeout);
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&bars[FU_KVEMPTY]);  // the last dQ^T MMA has read K
+        tc_commit(&bars[FU_DONE]);
+        ++n_items;
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int grp = (warp - 2) >> 2;
+    const int half = grp;
+    const int rl = quarter * 32 + lane;  // key row (S^T, dP^T, dV, dK) / head-dim row (dQ^T)
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float scale2 = a.scale * kLog2e;
+    const int64_t n64 = (a.N + kSub - 1) / kSub;
+    const int rb_tiles = (int)(a.RB / kRows);
+    const bool leader = (warp & 3) == 2 && lane == 0;  // one thread per group (warps 2 and 6)
+    uint32_t s_it = 0, done_it = 0, qd = 0, gsync = 0;
+    bool ok = true;
+    // Sync of this group's 4 warps on an mbarrier with a bounded wait (a named barrier would
+    // wait forever on a warp that gave up); warp-uniform result.
+    auto group_sync = [&]() -> bool {
+      mbar_arrive(&bars[FU_GSYNC0 + grp]);
+      return mbar_wait_warp(&bars[FU_GSYNC0 + grp], gsync++ & 1, a.status);
+    };
+    for (uint32_t w = 0; ok; ++w) {
+      WorkEntry e;
+      if (!(ok = ring_get_warp(ring, &bars[FU_WFULL0], &bars[FU_WEMPTY0], w, e, a.status))) break;
+      if (e.item < 0) break;
+      const KvItem it = kv_item(a, e.item);
+      const int n = e.end - e.begin;
+      const int64_t key = it.k0 + rl;
+      for (int i = 0; i < n && ok; ++i, ++qd, ++s_it) {
+        const uint32_t sb = s_it & 1, sph = (s_it >> 1) & 1;
+        if ((int)sb != grp) continue;
+        const uint32_t st = qd % kFuStages, ph = (qd / kFuStages) & 1;
+        if (!(ok = mbar_wait_warp(&bars[FU_QFULL0 + st], ph, a.status))) break;
+        const float* stats = reinterpret_cast<const float*>(sm + L::kQD + st * L::kStage + L::kStats);
+        const FuMeta m = meta[st];
+        const int64_t q0 = m.start;
+        if (!(ok = mbar_wait_warp(&bars[FU_SFULL0 + sb], sph, a.status))) break;
+        tc_fence_after();
+        const int64_t cmin = a.causal ? key - q0 : 0;
+        const int lo = (int)max((int64_t)0, min((int64_t)kSub, cmin));
+        const int hi = key < a.N ? (int)max((int64_t)0, min((int64_t)kSub, a.N - q0)) : 0;
+        const bool full = lo == 0 && hi == kSub;
+        unsigned char* dsrow = sm + L::kDsT + sb * L::kDsTBytes + rl * 128;
+        float rs = 0.f;
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          float s[32], dp[32];
+          tmem_ld32(lane_addr + kColS + sb * kSub + hc * 32, s);
+          tmem_ld32(lane_addr + kColP + sb * kSub + hc * 32, dp);
+          tmem_wait_ld();
+          const float4* l2v = reinterpret_cast<const float4*>(stats + hc * 32);
+          const float4* dlv = reinterpret_cast<const float4*>(stats + kSub + hc * 32);
+          uint32_t pk[16], dk[16];
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 l4 = l2v[c4], d4 = dlv[c4];
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+            float p[4], d[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int c = c4 * 4 + u;
+              p[u] = fast_exp2(fmaf(s[c], scale2, m.b2) - lv[u]);
+              d[u] = p[u] * (dp[c] - dv[u]);
+              if (!full) {
+                const int cc = hc * 32 + c;
+                const bool vis = cc >= lo && cc < hi;
+                p[u] = vis ? p[u] : 0.f;
+                d[u] = vis ? d[u] : 0.f;
+              }
+              rs += d[u];
+              d[u] *= a.scale;
+            }
+            pk[c4 * 2] = pack2(p[0], p[1], BF16);
+            pk[c4 * 2 + 1] = pack2(p[2], p[3], BF16);
+            dk[c4 * 2] = pack2(d[0], d[1], BF16);
+            dk[c4 * 2 + 1] = pack2(d[2], d[3], BF16);
+          }
+          // P^T and dS^T (bf16 pairs) into this half's 32 S^T columns, which this thread has read
+          tmem_st16(lane_addr + kColS + sb * kSub + hc * 32, pk);
+          tmem_st16(lane_addr + kColS + sb * kSub + hc * 32 + 16, dk);
+          // dS^T row `rl`, query columns [32 hc, 32 hc + 32), into the dQ MMA's B tile
+          // (128-byte rows, 16-byte units swizzled by the row's low 3 bits)
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int unit = hc * 4 + v;
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                             smem_u32(dsrow + ((unit ^ (rl & 7)) << 4))),
+                         "r"(dk[v * 4 + 0]), "r"(dk[v * 4 + 1]), "r"(dk[v * 4 + 2]), "r"(dk[v * 4 + 3])
+                         : "memory");
+          }
+        }
+        tmem_wait_st();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars[FU_PFULL0 + sb]);
+        if (m.bias_idx >= 0) {
+#pragma unroll
+          for (int o = 16; o; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+          if (lane == 0) atomicAdd(&a.dbias[m.bias_idx], rs);
+        }
+        // dQ^T of this sub-tile: out of TMEM, release the columns, add into the accumulator
+        if (!(ok = mbar_wait_warp(&bars[FU_DQFULL0 + sb], sph, a.status))) break;
+        tc_fence_after();
+        float dq[64];
+        tmem_ld32(lane_addr + kColP + sb * kSub, *reinterpret_cast<float(*)[32]>(dq));
+        tmem_ld32(lane_addr + kColP + sb * kSub + 32, *reinterpret_cast<float(*)[32]>(dq + 32));
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[FU_DQEMPTY0 + sb]);
+        float* acc = a.dq_acc + (m.zh * a.N + q0) * D + rl;
+        const int rows = (int)min((int64_t)kSub, a.N - q0);
+#pragma unroll
+        for (int c = 0; c < kSub; ++c)
+          if (c < rows) atomicAdd(acc + (int64_t)c * D, dq[c]);
+        // the sub-tile's last contribution converts it (the classic last-arrival pattern:
+        // every thread's reductions are ordered before the group leader's counter update)
+        __threadfence();
+        if (!(ok = group_sync())) break;
+        if (leader) {
+          const int64_t t64 = m.zh * n64 + q0 / kSub;
+          const int want = a.dq_expect[m.zh * a.NB + m.qb] * rb_tiles;
+          const int prev = atomicAdd(&a.dq_cnt[t64], 1);
+          flag[grp] = prev == want - 1;
+          __threadfence();
+        }
+        if (!(ok = group_sync())) break;
+        if (flag[grp]) {
+          const int64_t z = m.zh / a.H, h = m.zh % a.H;
+          using T = __nv_bfloat16;  // both half types are 2 bytes; pack2 picks the format
+          T* dst = static_cast<T*>(a.dq) + z * a.dqs[0] + h * a.dqs[1] + q0 * a.dqs[2] + rl;
+          const float* src = a.dq_acc + (m.zh * a.N + q0) * D + rl;
+          for (int c = 0; c < rows; c += 2) {
+            const float v0 = __ldcg(src + (int64_t)c * D);
+            const float v1 = c + 1 < rows ? __ldcg(src + (int64_t)(c + 1) * D) : 0.f;
+            const uint32_t pr = pack2(v0, v1, BF16);
+            *reinterpret_cast<uint16_t*>(dst + c * a.dqs[2]) = (uint16_t)(pr & 0xffffu);
+            if (c + 1 < rows) *reinterpret_cast<uint16_t*>(dst + (c + 1) * a.dqs[2]) = (uint16_t)(pr >> 16);
+          }
+        }
+      }
+      if (!ok) break;
+      if (n > 0) {
+        if (!(ok = mbar_wait_warp(&bars[FU_DONE], done_it & 1, a.status))) break;
+        ++done_it;
+        tc_fence_after();
+      }
+      const int c0 = half * (D / 2);
+      if (e.slot < 0) {
+        store_cols<D / 2>(a.dv, a.dvs, it.z, it.hk, key, c0, lane_addr + kColAcc + c0, BF16,
+                          key < a.N, n == 0);
+        store_cols<D / 2>(a.dk, a.dks, it.z, it.hk, key, c0, lane_addr + kColAcc + D + c0, BF16,
+                          key < a.N, n == 0);
+      } else {
+        float* prow = a.partials + ((int64_t)e.slot * kRows + rl) * (2 * D);
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+#pragma unroll
+          for (int c = 0; c < D / 2; c += 32) {
+            float o[32];
+            if (n > 0) {
+              tmem_ld32(lane_addr + kColAcc + part * D + c0 + c, o);
+              tmem_wait_ld();
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(prow + part * D + c0 + c + i) =
+                  make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      if (n > 0) mbar_arrive(&bars[FU_EPI]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 template <int D, bool BF16>
 int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
   BwdArgs a{};
@@ -892,7 +1328,75 @@ int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
   return SA_OK;
 }
 
+template <bool BF16>
+int launch_fused_t(const AttnParams& p, cudaStream_t stream) {
+  constexpr int D = 128;
+  BwdArgs a{};
+  a.Z = p.Z;
+  a.H = p.H;
+  a.Hkv = p.Hkv;
+  a.N = p.N;
+  a.RB = p.RB;
+  a.NB = p.NB;
+  a.lists = p.lists;
+  a.list_stride = p.list_stride;
+  a.counts = p.counts;
+  a.k_lists = p.k_lists;
+  a.k_slots = p.k_slots;
+  a.q_counts = p.q_counts;
+  a.lse = p.lse;
+  a.delta = p.delta;
+  a.bias = p.bias;
+  a.bias_dtype = p.bias_dtype;
+  for (int i = 0; i < 4; ++i) {
+    a.bs[i] = p.bs[i];
+    a.dqs[i] = p.dqs[i];
+    a.dks[i] = p.dks[i];
+    a.dvs[i] = p.dvs[i];
+  }
+  a.dbias = p.dbias;
+  a.stats = p.stats;
+  a.dq = p.dq;
+  a.dk = p.dk;
+  a.dv = p.dv;
+  a.causal = p.causal;
+  a.scale = p.scale;
+  a.status = p.status;
+  a.dq_acc = p.dq_acc;
+  a.dq_cnt = p.dq_cnt;
+  a.dq_expect = p.dq_expect;
+  if (!a.dq_acc || !a.dq_cnt || !a.dq_expect || !p.plan_dkdv)
+    return fail(SA_EINVAL, "fused backward: missing dQ accumulator / counters / plan");
+  int rc = make_tmap_4d(&a.tm_q, p.q, p.dtype, p.Z, p.H, p.N, D, p.qs, 64, kSub);
+  if (!rc) rc = make_tmap_4d(&a.tm_do, p.dout, p.dtype, p.Z, p.H, p.N, D, p.dos, 64, kSub);
+  if (!rc) rc = make_tmap_4d(&a.tm_k, p.k, p.dtype, p.Z, p.Hkv, p.N, D, p.ks, 64, kRows);
+  if (!rc) rc = make_tmap_4d(&a.tm_v, p.v, p.dtype, p.Z, p.Hkv, p.N, D, p.vs, 64, kRows);
+  if (rc) return fail(SA_ELAUNCH, std::string("fused backward tensor maps: ") + sa_last_error());
+  a.tiles = (p.N + kRows - 1) / kRows;
+  const int64_t items = a.Z * a.Hkv * a.tiles;
+  const int ctas = (int)std::min<int64_t>(items, device_sm_count());
+  const PlanPtrs pp = plan_carve(p.plan_dkdv, kPlanDkdv, items, ctas, D);
+  a.sched = SchedArgs{pp.header, pp.queue, items, 0};
+  a.partials = pp.partials;
+  auto kern = bwd_fused_sm100_kernel<BF16>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FuLayout::kAlloc);
+  kern<<<(unsigned)ctas, kBwdThreads, FuLayout::kAlloc, stream>>>(a);
+  rc = check_launch("bwd_fused_sm100_kernel");
+  if (rc) return rc;
+  return launch_dkdv_reduce(p, pp, ctas, stream);
+}
+
 }  // namespace
+
+bool bwd_sm100_eligible(const AttnParams& p);
+
+bool bwd_fused_eligible(const AttnParams& p) {
+  // the prep's vectorised Delta kernel zeroes the dQ accumulator: O must suit it too
+  if (reinterpret_cast<uintptr_t>(p.out) % 16) return false;
+  for (int i = 0; i < 3; ++i)
+    if (p.os[i] % 8) return false;
+  return bwd_sm100_eligible(p) && p.D == 128 && p.RB % kRows == 0;
+}
 
 bool bwd_sm100_eligible(const AttnParams& p) {
   if (p.dtype != SA_BF16 && p.dtype != SA_F16) return false;
@@ -954,6 +1458,10 @@ int launch_bwd_sm100(const AttnParams& p, cudaStream_t stream, int parts) {
       return SA_EUNSUPPORTED;
   if (p.N > INT32_MAX) return SA_EUNSUPPORTED;
   const bool bf = p.dtype == SA_BF16;
+  if (parts & kBwdFused) {
+    if (!bwd_fused_eligible(p)) return SA_EUNSUPPORTED;
+    return bf ? launch_fused_t<true>(p, stream) : launch_fused_t<false>(p, stream);
+  }
   if (p.D == 64) return bf ? launch_t<64, true>(p, stream, parts) : launch_t<64, false>(p, stream, parts);
   return bf ? launch_t<128, true>(p, stream, parts) : launch_t<128, false>(p, stream, parts);
 }

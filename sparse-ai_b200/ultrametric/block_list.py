@@ -237,7 +237,8 @@ def _fwd(q, k, v, lists, counts, route_block, is_causal, scale, store_lse, soft_
     return out, lse
 
 
-def _bwd(do, q, k, v, out, lse, lists, counts, route_block, is_causal, scale, soft_block_bias):
+def _bwd(do, q, k, v, out, lse, lists, counts, route_block, is_causal, scale, soft_block_bias,
+         deterministic=False):
     Z, H, N, D = q.shape
     do = do.contiguous() if do.stride(-1) != 1 else do
     dq = torch.empty_like(q)
@@ -250,16 +251,20 @@ def _bwd(do, q, k, v, out, lse, lists, counts, route_block, is_causal, scale, so
     ws_bytes = int(nat.lib().sa_block_list_attention_bwd_workspace_bytes(Z, H, k.shape[1], N, D,
                                                                           route_block))
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)
-    nat.check(nat.lib().sa_block_list_attention_bwd(
-        nat.float_code(q.dtype), Z, H, k.shape[1], N, D, route_block,
-        q.data_ptr(), nat.strides(q), k.data_ptr(), nat.strides(k), v.data_ptr(), nat.strides(v),
-        out.data_ptr(), nat.strides(out), do.data_ptr(), nat.strides(do), lse.data_ptr(),
-        lists.data_ptr(), lists.shape[-1], counts.data_ptr(),
-        nat.ptr(sb), nat.float_code(sb.dtype) if sb is not None else 0,
-        nat.strides(sb) if sb is not None else None,
-        int(bool(is_causal)), float(scale),
-        dq.data_ptr(), nat.strides(dq), dk.data_ptr(), nat.strides(dk), dv.data_ptr(), nat.strides(dv),
-        nat.ptr(d_sb), ws.data_ptr(), ws.numel(), nat.stream_of(q)), "block_list_attention backward")
+    # phase 0: the whole backward (the fused single-pass kernel where the shape allows);
+    # deterministic: the dQ and dK/dV kernels (phases 1-3), whose sums are reproducible
+    for phase in ((1, 2, 3) if deterministic else (0,)):
+        nat.check(nat.lib().sa_block_list_attention_bwd_phase(
+            phase, nat.float_code(q.dtype), Z, H, k.shape[1], N, D, route_block,
+            q.data_ptr(), nat.strides(q), k.data_ptr(), nat.strides(k), v.data_ptr(), nat.strides(v),
+            out.data_ptr(), nat.strides(out), do.data_ptr(), nat.strides(do), lse.data_ptr(),
+            lists.data_ptr(), lists.shape[-1], counts.data_ptr(),
+            nat.ptr(sb), nat.float_code(sb.dtype) if sb is not None else 0,
+            nat.strides(sb) if sb is not None else None,
+            int(bool(is_causal)), float(scale),
+            dq.data_ptr(), nat.strides(dq), dk.data_ptr(), nat.strides(dk), dv.data_ptr(),
+            nat.strides(dv), nat.ptr(d_sb), ws.data_ptr(), ws.numel(), nat.stream_of(q)),
+            "block_list_attention backward")
     if d_sb is not None:
         d_sb = d_sb.to(sb.dtype)
     return dq, dk, dv, d_sb
@@ -271,8 +276,9 @@ class _BlockListAttentionFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, k, v, lists, counts, route_block, is_causal, scale, return_lse,
-                soft_block_bias):
+                soft_block_bias, deterministic=False):
         out, lse = _fwd(q, k, v, lists, counts, route_block, is_causal, scale, True, soft_block_bias)
+        ctx.deterministic = deterministic
         saved = [q, k, v, out, lse, lists, counts]
         if soft_block_bias is not None:
             saved.append(soft_block_bias)
@@ -293,12 +299,12 @@ class _BlockListAttentionFn(torch.autograd.Function):
         q, k, v, out, lse, lists, counts = saved[:7]
         sb = saved[7] if ctx.has_bias else None
         dq, dk, dv, d_sb = _bwd(do, q, k, v, out, lse, lists, counts, ctx.route_block,
-                                ctx.is_causal, ctx.scale, sb)
+                                ctx.is_causal, ctx.scale, sb, ctx.deterministic)
         return (dq if ctx.needs_input_grad[0] else None,
                 dk if ctx.needs_input_grad[1] else None,
                 dv if ctx.needs_input_grad[2] else None,
                 None, None, None, None, None, None,
-                d_sb if (ctx.has_bias and ctx.needs_input_grad[9]) else None)
+                d_sb if (ctx.has_bias and ctx.needs_input_grad[9]) else None, None)
 
 
 def block_list_attention(
@@ -316,6 +322,7 @@ def block_list_attention(
     num_stages: int = 3,
     return_lse: bool = False,
     soft_block_bias: Optional[torch.Tensor] = None,
+    deterministic: bool = False,
 ):
     """Block-sparse attention over precomputed block lists, with sparse autograd.
 
@@ -325,6 +332,11 @@ def block_list_attention(
     adds the (Z, H, N) fp32 natural-log LSE (-inf for rows with no visible key);
     ``soft_block_bias`` (Z, H, NB, max_count) is an additive logit bias per (row block, slot)
     with an exact gradient (for STE router training).
+
+    The backward of bf16/fp16 with head_dim 128 and route_block a multiple of 128 runs one
+    fused kernel (dK, dV and dQ in one pass; dQ summed in fp32 by atomics, so its last bits
+    can differ from run to run).  ``deterministic=True`` (an addition to the reference's
+    signature) runs the separate dQ and dK/dV kernels instead, whose sums are reproducible.
     """
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4 or k.shape != v.shape or \
             q.shape[0] != k.shape[0] or q.shape[2:] != k.shape[2:] or \
@@ -370,7 +382,7 @@ def block_list_attention(
     if needs_grad:
         return _BlockListAttentionFn.apply(q, k, v, lists, counts, int(route_block),
                                            bool(is_causal), float(scale), bool(return_lse),
-                                           soft_block_bias)
+                                           soft_block_bias, bool(deterministic))
     out, lse = _fwd(q, k, v, lists, counts, int(route_block), bool(is_causal), float(scale),
                     bool(return_lse), soft_block_bias)
     return (out, lse) if return_lse else out

@@ -315,3 +315,63 @@ def test_backward_split_heavy_sink_column():
     for name, t in (("dq", qq), ("dk", kk), ("dv", vv)):
         assert_half_close(t.grad, lowp[name], name + " vs reference rounding")
         assert_half_close(t.grad, res[name], name + " vs exact", abs_tol=4e-2, rel_tol=2e-2)
+
+
+# ---------------------------------------------------------------------------------------
+# the fused single-pass backward (head_dim 128) against the oracle and the two-kernel path
+# ---------------------------------------------------------------------------------------
+
+FUSED_CASES = [
+    # Z, H, Hkv, N, RB, depth, causal, sink, local, with_bias, empty_rows
+    (1, 4, 1, 1024, 128, 1, True, True, 0, False, False),
+    (2, 4, 2, 1000, 256, 1, True, True, 1, True, False),   # route block of two key tiles, tail
+    (1, 2, 2, 320, 128, 2, False, False, 0, False, True),  # partial last sub-tile, empty rows
+    (1, 8, 2, 768, 128, [0, 1, 2, 3, 1, 1, 2, 0], True, False, 0, True, False),
+]
+
+
+@pytest.mark.parametrize("Z,H,Hkv,N,RB,depth,causal,sink,local,with_bias,empty_rows", FUSED_CASES)
+def test_fused_backward(Z, H, Hkv, N, RB, depth, causal, sink, local, with_bias, empty_rows):
+    D = 128
+    gen = torch.Generator().manual_seed(100 + N)
+    q = randn((Z, H, N, D), gen).bfloat16()
+    k = randn((Z, Hkv, N, D), gen).bfloat16()
+    v = randn((Z, Hkv, N, D), gen).bfloat16()
+    do = randn((Z, H, N, D), gen).bfloat16()
+    NB = -(-N // RB)
+    router = random_router(Z, H, NB, 6, 2, seed=N + 1).to(DEV)
+    bl = build_block_lists(router, depth, is_causal=causal, sink_block=sink, local_blocks=local)
+    if empty_rows:  # some query blocks list no key block: their dQ rows must come out zero
+        counts = bl.counts.clone()
+        counts[:, :, 1] = 0
+        bl = BlockLists(bl.lists, counts, bl.max_count)
+    grads = {}
+    for det in (False, True):
+        qq, kk, vv = (t.to(DEV).requires_grad_(True) for t in (q, k, v))
+        raw = torch.zeros(bl.lists.shape, device=DEV, requires_grad=True) if with_bias else None
+        ste = (raw - raw.detach()) if with_bias else None
+        out = block_list_attention(qq, kk, vv, bl, route_block=RB, is_causal=causal,
+                                   soft_block_bias=ste, deterministic=det)
+        out.backward(do.to(DEV))
+        grads[det] = {"out": out.detach(), "dq": qq.grad, "dk": kk.grad, "dv": vv.grad,
+                      "db": raw.grad if with_bias else None}
+    mask = ao.token_mask(block_mask_from_lists(bl.lists, bl.counts), RB, N, causal)
+    res = ao.masked_attention_grads(q.float(), k.float(), v.float(), mask, do.float(),
+                                    block_bias=torch.zeros(bl.lists.shape) if with_bias else None,
+                                    lists=bl.lists.cpu(), counts=bl.counts.cpu(), route_block=RB)
+    g = grads[False]
+    for name in ("dq", "dk", "dv"):
+        assert_half_close(g[name], res[name], f"fused {name}")
+        # same math as the two-kernel path, up to bf16 rounding of the stored gradients
+        assert_half_close(g[name], grads[True][name].float(), f"fused vs two-kernel {name}")
+    if empty_rows:
+        assert (g["dq"][:, :, RB:2 * RB] == 0).all()
+    if with_bias:
+        err = (g["db"].cpu().double() - res["d_bias"]).abs().max().item()
+        assert err <= 2e-2 * max(1.0, res["d_bias"].abs().max().item()), f"d_bias err {err}"
+    assert _native_status() == 0
+
+
+def _native_status():
+    from ultrametric import _native as nat
+    return nat.read_device_status()

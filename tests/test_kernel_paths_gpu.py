@@ -32,15 +32,22 @@ def test_forward_uses_tcgen05_kernel(D, dtype):
     assert _native.read_device_status() == 0
 
 
-def test_backward_uses_tcgen05_kernels():
+@pytest.mark.parametrize("D,deterministic", [(128, False), (128, True), (64, False)])
+def test_backward_uses_tcgen05_kernels(D, deterministic):
+    """head_dim 128 runs the fused single-pass kernel unless deterministic sums are asked
+    for; the two-kernel path (dQ, dK/dV) serves deterministic=True and head_dim 64."""
     gen = torch.Generator().manual_seed(2)
-    q, k, v = (randn((1, 4, 512, 128), gen).bfloat16().to(DEV).requires_grad_(True) for _ in range(3))
+    q, k, v = (randn((1, 4, 512, D), gen).bfloat16().to(DEV).requires_grad_(True) for _ in range(3))
     bl = build_block_lists(random_router(1, 4, 4, 4, 2).to(DEV), 1, is_causal=True, sink_block=True, arity=2)
-    out = block_list_attention(q, k, v, bl, route_block=128, is_causal=True)
+    out = block_list_attention(q, k, v, bl, route_block=128, is_causal=True, deterministic=deterministic)
     g = torch.ones_like(out)
     names = kernel_names(lambda: out.backward(g))
-    assert any("bwd_dq_sm100_kernel" in n for n in names), names
-    assert any("bwd_dkdv_sm100_kernel" in n for n in names), names
+    if D == 128 and not deterministic:
+        assert any("bwd_fused_sm100_kernel" in n for n in names), names
+        assert not any("bwd_dq_sm100_kernel" in n for n in names), names
+    else:
+        assert any("bwd_dq_sm100_kernel" in n for n in names), names
+        assert any("bwd_dkdv_sm100_kernel" in n for n in names), names
     assert not any("simt" in n for n in names), names
     assert _native.read_device_status() == 0
 
