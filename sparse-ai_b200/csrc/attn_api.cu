@@ -157,11 +157,8 @@ int64_t sa_block_list_attention_bwd_workspace_bytes(int64_t Z, int64_t H, int64_
   b += align256((size_t)Z * H * ((N + 63) / 64) * 128 * sizeof(float));  // row stats
   b += align256((size_t)sa::bwd_plan_bytes(sa::kPlanDq, Z, H, Hkv, N, D));
   b += align256((size_t)sa::bwd_plan_bytes(sa::kPlanDkdv, Z, H, Hkv, N, D));
-  if (sa::fused_shape(D, route_block)) {
-    b += align256((size_t)Z * H * N * D * sizeof(float));        // fp32 dQ accumulator
-    b += align256((size_t)Z * H * ((N + 63) / 64) * sizeof(int32_t));  // sub-tile counters
-    b += align256((size_t)Z * H * NB * sizeof(int32_t));           // contributions per block
-  }
+  if (sa::fused_shape(D, route_block))
+    b += align256((size_t)Z * H * N * D * sizeof(float));  // fp32 dQ accumulator
   return (int64_t)b;
 }
 
@@ -235,13 +232,7 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
   // phase 0 = the whole backward, fused when the shape allows; 1-3 = the two-kernel path
   // (prep, dQ, dK/dV: reproducible dQ sums); 4-5 = the fused path (prep, fused kernel)
   const bool fused = (phase == 0 || phase >= 4) && fused_shape(D, route_block) && bwd_fused_eligible(p);
-  if (fused) {
-    p.dq_acc = reinterpret_cast<float*>(w);
-    w += align256((size_t)Z * H * N * D * sizeof(float));
-    p.dq_cnt = reinterpret_cast<int32_t*>(w);
-    w += align256((size_t)Z * H * ((N + 63) / 64) * sizeof(int32_t));
-    p.dq_expect = reinterpret_cast<int32_t*>(w);
-  }
+  if (fused) p.dq_acc = reinterpret_cast<float*>(w);
   if (phase == 4 && !fused) phase = 1;  // shapes without the fused kernel: two-kernel path
   if (phase == 5 && !fused) {
     rc = launch_bwd_sm100(p, s, kBwdDq | kBwdDkDv);
@@ -259,11 +250,8 @@ int sa_block_list_attention_bwd_phase(int phase, int dtype, int64_t Z, int64_t H
     if (rc) return rc;
     if (cudaEventRecord(fork, s) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
       return check_launch("backward fork");
-    if (fused && cudaMemsetAsync(p.dq_expect, 0, (size_t)Z * H * NB * sizeof(int32_t), side) != cudaSuccess)
-      rc = check_launch("memset dQ contribution counts");
-    if (!rc)
-      rc = launch_transpose_lists(lists, list_stride, counts, Z * H, NB, NB, k_lists, NB,
-                                  q_counts, k_slots, 0, side, fused ? p.dq_expect : nullptr);
+    rc = launch_transpose_lists(lists, list_stride, counts, Z * H, NB, NB, k_lists, NB,
+                                q_counts, k_slots, 0, side);
     if (!rc) rc = plan_bwd_sm100(p, side, kBwdDkDv);
     if (cudaEventRecord(join, side) != cudaSuccess) return check_launch("backward join");
     if (!rc) rc = launch_delta(p, s);

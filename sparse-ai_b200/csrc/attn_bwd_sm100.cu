@@ -72,13 +72,7 @@ struct BwdArgs {
   unsigned* status;
   SchedArgs sched;
   float* partials;  // dK/dV: fp32 [slot][128][dV D | dK D] for split chunks
-  // fused kernel: fp32 dQ accumulator (Z*H, N, D) contiguous, per 64-row query sub-tile
-  // arrival counters (Z*H, ceil(N/64)), and the number of key blocks whose transposed list
-  // holds each query block (Z*H, NB): a sub-tile is complete after that many x RB/128
-  // arrivals
-  float* dq_acc;
-  int32_t* dq_cnt;
-  const int32_t* dq_expect;
+  float* dq_acc;  // fused kernel: fp32 dQ accumulator (Z*H, N, D) contiguous, zeroed
 };
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
@@ -844,8 +838,7 @@ struct FuLayout {
   static constexpr uint32_t kDsTBytes = kRows * kSub * 2;
   static constexpr uint32_t kBars = kDsT + 2 * kDsTBytes;
   static constexpr uint32_t kMeta = kBars + 256;  // FuMeta[kFuStages]
-  static constexpr uint32_t kFlag = kMeta + 128;  // per group: "this sub-tile is complete"
-  static constexpr uint32_t kRingOff = kFlag + 64;
+  static constexpr uint32_t kRingOff = kMeta + 128;
   static constexpr uint32_t kAlloc = kRingOff + 128 + 1024;
   static_assert(kDsT % 1024 == 0 && kStage % 1024 == 0, "swizzled tiles need 1024-byte alignment");
   static_assert(kAlloc <= 232448, "fused backward shared-memory layout too large");
@@ -875,7 +868,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
   FuMeta* meta = reinterpret_cast<FuMeta*>(sm + L::kMeta);
-  volatile int* flag = reinterpret_cast<volatile int*>(sm + L::kFlag);
   WorkEntry* ring = reinterpret_cast<WorkEntry*>(sm + L::kRingOff);
   __shared__ uint32_t s_tmem;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1060,8 +1052,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
     const int rl = quarter * 32 + lane;  // key row (S^T, dP^T, dV, dK) / head-dim row (dQ^T)
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const float scale2 = a.scale * kLog2e;
-    const int64_t n64 = (a.N + kSub - 1) / kSub;
-    const int rb_tiles = (int)(a.RB / kRows);
     const bool leader = (warp & 3) == 2 && lane == 0;  // one thread per group (warps 2 and 6)
     uint32_t s_it = 0, done_it = 0, qd = 0, gsync = 0;
     bool ok = true;
@@ -1159,36 +1149,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars[FU_DQEMPTY0 + sb]);
-        float* acc = a.dq_acc + (m.zh * a.N + q0) * D + rl;
+        // dQ^T -> fp32 rows [q][d] in this group's dS^T buffer (free: the dQ^T MMA that read it
+        // has completed), 32 query rows = 16 KB at a time, each added into the accumulator by
+        // one bulk reduction (cp.reduce.async.bulk .add.f32, performed at L2)
         const int rows = (int)min((int64_t)kSub, a.N - q0);
+        float* stg = reinterpret_cast<float*>(sm + L::kDsT + sb * L::kDsTBytes);
+        float* gdst = a.dq_acc + (m.zh * a.N + q0) * D;
 #pragma unroll
-        for (int c = 0; c < kSub; ++c)
-          if (c < rows) atomicAdd(acc + (int64_t)c * D, dq[c]);
-        // the sub-tile's last contribution converts it (the classic last-arrival pattern:
-        // every thread's reductions are ordered before the group leader's counter update)
-        __threadfence();
-        if (!(ok = group_sync())) break;
-        if (leader) {
-          const int64_t t64 = m.zh * n64 + q0 / kSub;
-          const int want = a.dq_expect[m.zh * a.NB + m.qb] * rb_tiles;
-          const int prev = atomicAdd(&a.dq_cnt[t64], 1);
-          flag[grp] = prev == want - 1;
-          __threadfence();
-        }
-        if (!(ok = group_sync())) break;
-        if (flag[grp]) {
-          const int64_t z = m.zh / a.H, h = m.zh % a.H;
-          using T = __nv_bfloat16;  // both half types are 2 bytes; pack2 picks the format
-          T* dst = static_cast<T*>(a.dq) + z * a.dqs[0] + h * a.dqs[1] + q0 * a.dqs[2] + rl;
-          const float* src = a.dq_acc + (m.zh * a.N + q0) * D + rl;
-          for (int c = 0; c < rows; c += 2) {
-            const float v0 = __ldcg(src + (int64_t)c * D);
-            const float v1 = c + 1 < rows ? __ldcg(src + (int64_t)(c + 1) * D) : 0.f;
-            const uint32_t pr = pack2(v0, v1, BF16);
-            *reinterpret_cast<uint16_t*>(dst + c * a.dqs[2]) = (uint16_t)(pr & 0xffffu);
-            if (c + 1 < rows) *reinterpret_cast<uint16_t*>(dst + (c + 1) * a.dqs[2]) = (uint16_t)(pr >> 16);
+        for (int hf = 0; hf < 2; ++hf) {
+          if (hf == 1) {
+            if (leader) bulk_wait_read();  // the first half's reduction has read the buffer
+            if (!(ok = group_sync())) break;
           }
+#pragma unroll
+          for (int r = 0; r < 32; ++r) stg[r * D + rl] = dq[hf * 32 + r];
+          fence_proxy_async_smem();
+          if (!(ok = group_sync())) break;
+          const int rows_h = min(32, rows - hf * 32);
+          if (leader && rows_h > 0)
+            bulk_reduce_add_f32(gdst + (int64_t)hf * 32 * D, stg, (uint32_t)rows_h * D * 4);
         }
+        if (!ok) break;
+        // the buffer is this group's dS^T again at its next sub-tile
+        if (leader) bulk_wait_read();
+        if (!(ok = group_sync())) break;
       }
       if (!ok) break;
       if (n > 0) {
@@ -1227,6 +1211,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
       if (n > 0) mbar_arrive(&bars[FU_EPI]);
     }
   }
+  // bulk reductions still in flight complete before the CTA (and its shared memory) ends
+  if ((warp == 2 || warp == 6) && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -1328,6 +1314,26 @@ int launch_t(const AttnParams& p, cudaStream_t stream, int parts) {
   return SA_OK;
 }
 
+// dQ (Z, H, N, 128) with strides <- fp32 accumulator (Z*H, N, 128) contiguous; HBM-bound,
+// 16-byte stores (rows 16-byte aligned, as the fused kernel's eligibility requires).
+template <bool BF16>
+__global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict__ acc, void* dq,
+                                                         int64_t s0, int64_t s1, int64_t s2,
+                                                         int64_t H, int64_t N, int64_t n8) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const int64_t row = i / 16, c8 = i % 16;  // 16 groups of 8 columns per row
+  const int64_t zh = row / N, q = row % N, z = zh / H, h = zh % H;
+  const float4 a0 = __ldcs(reinterpret_cast<const float4*>(acc) + i * 2);
+  const float4 a1 = __ldcs(reinterpret_cast<const float4*>(acc) + i * 2 + 1);
+  uint4 o;
+  o.x = pack2(a0.x, a0.y, BF16);
+  o.y = pack2(a0.z, a0.w, BF16);
+  o.z = pack2(a1.x, a1.y, BF16);
+  o.w = pack2(a1.z, a1.w, BF16);
+  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(dq) + z * s0 + h * s1 + q * s2 + c8 * 8) = o;
+}
+
 template <bool BF16>
 int launch_fused_t(const AttnParams& p, cudaStream_t stream) {
   constexpr int D = 128;
@@ -1363,10 +1369,7 @@ int launch_fused_t(const AttnParams& p, cudaStream_t stream) {
   a.scale = p.scale;
   a.status = p.status;
   a.dq_acc = p.dq_acc;
-  a.dq_cnt = p.dq_cnt;
-  a.dq_expect = p.dq_expect;
-  if (!a.dq_acc || !a.dq_cnt || !a.dq_expect || !p.plan_dkdv)
-    return fail(SA_EINVAL, "fused backward: missing dQ accumulator / counters / plan");
+  if (!a.dq_acc || !p.plan_dkdv) return fail(SA_EINVAL, "fused backward: missing dQ accumulator / plan");
   int rc = make_tmap_4d(&a.tm_q, p.q, p.dtype, p.Z, p.H, p.N, D, p.qs, 64, kSub);
   if (!rc) rc = make_tmap_4d(&a.tm_do, p.dout, p.dtype, p.Z, p.H, p.N, D, p.dos, 64, kSub);
   if (!rc) rc = make_tmap_4d(&a.tm_k, p.k, p.dtype, p.Z, p.Hkv, p.N, D, p.ks, 64, kRows);
@@ -1383,7 +1386,13 @@ int launch_fused_t(const AttnParams& p, cudaStream_t stream) {
   kern<<<(unsigned)ctas, kBwdThreads, FuLayout::kAlloc, stream>>>(a);
   rc = check_launch("bwd_fused_sm100_kernel");
   if (rc) return rc;
-  return launch_dkdv_reduce(p, pp, ctas, stream);
+  rc = launch_dkdv_reduce(p, pp, ctas, stream);
+  if (rc) return rc;
+  // dQ = the fp32 accumulator rounded to bf16 / fp16 (8 elements per thread)
+  const int64_t n8 = p.Z * p.H * p.N * (D / 8);
+  dq_convert_kernel<BF16><<<(unsigned)((n8 + 255) / 256), 256, 0, stream>>>(
+      p.dq_acc, p.dq, p.dqs[0], p.dqs[1], p.dqs[2], p.H, p.N, n8);
+  return check_launch("dq_convert_kernel");
 }
 
 }  // namespace

@@ -41,12 +41,8 @@ struct AttnParams {
   void* dv;
   int64_t dvs[4];
   float* dbias;  // (Z, H, NB, list_stride) contiguous fp32, or null
-  // fused backward: fp32 dQ accumulator (Z*H, N, D), arrival counters per 64-row query
-  // sub-tile (Z*H, ceil(N/64)), and per query block the number of key blocks listing it
-  // (Z*H, NB).  Null on the two-kernel path.
+  // fused backward: fp32 dQ accumulator (Z*H, N, D) contiguous (null on the two-kernel path)
   float* dq_acc;
-  int32_t* dq_cnt;
-  int32_t* dq_expect;
   unsigned* status;
   // planner workspaces of the tcgen05 kernels (null: static round-robin scheduling)
   void* plan_fwd;
@@ -60,12 +56,10 @@ constexpr int kBwdDq = 1, kBwdDkDv = 2, kBwdFused = 4;
 int launch_fwd_simt(const AttnParams& p, cudaStream_t stream);
 int launch_bwd_simt(const AttnParams& p, cudaStream_t stream, int parts);
 int launch_delta(const AttnParams& p, cudaStream_t stream);
-// q_member (optional, zeroed by the caller): per query block, add the number of key blocks
-// whose transposed list holds it.
 int launch_transpose_lists(const int32_t* lists, int64_t list_stride, const int32_t* counts,
                            int64_t ZH, int64_t NBQ, int64_t NBK, int32_t* k_lists,
                            int64_t k_list_stride, int32_t* q_counts, int32_t* k_slots, int pad,
-                           cudaStream_t stream, int32_t* q_member = nullptr);
+                           cudaStream_t stream);
 // The fused backward takes bf16/fp16, head_dim 128, route_block a multiple of 128.
 bool bwd_fused_eligible(const AttnParams& p);
 // tcgen05 kernels: return SA_EUNSUPPORTED (without launching) for shapes they do not take.

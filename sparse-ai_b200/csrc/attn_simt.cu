@@ -195,17 +195,12 @@ __global__ void __launch_bounds__(256) delta_vec_kernel(AttnParams p) {
       st[row % 64] = l2;
       st[64 + row % 64] = a;
     }
-    if (p.dq_acc && row < p.N && row % 64 == 0) p.dq_cnt[zh * (npad / 64) + row / 64] = 0;
   }
   if (p.dq_acc && in_range && row < p.N) {
-    // fused backward: zero this row of the fp32 dQ accumulator, and write dQ = 0 now for rows
-    // whose query block lists no key block (no contribution will ever convert them)
+    // fused backward: zero this row of the fp32 dQ accumulator
     float4* acc = reinterpret_cast<float4*>(p.dq_acc + (zh * p.N + row) * D) + li * (D / LPR / 4);
 #pragma unroll
     for (int i = 0; i < D / LPR / 4; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p.counts[zh * p.NB + row / p.RB] == 0)
-      *reinterpret_cast<uint4*>(static_cast<T*>(p.dq) + z * p.dqs[0] + h * p.dqs[1] + row * p.dqs[2] +
-                                li * VEC) = make_uint4(0u, 0u, 0u, 0u);
   }
 }
 

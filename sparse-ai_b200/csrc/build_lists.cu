@@ -102,7 +102,6 @@ struct TransParams {
   int32_t* q_counts;
   int32_t* k_slots;
   int pad;
-  int32_t* q_member;
 };
 
 // grid (ceil(NBK / kTransRows), ZH).  Phase 1 scatters every (qb, t) entry whose key block
@@ -126,15 +125,7 @@ __global__ void __launch_bounds__(256) transpose_lists_kernel(TransParams p) {
     }
   }
   __syncthreads();
-  if (p.q_member) {
-    // per query block: how many of this CTA's key blocks list it (the fused backward's
-    // count of dQ contributions)
-    for (int64_t qb = threadIdx.x; qb < p.NBQ; qb += blockDim.x) {
-      int c = 0;
-      for (int64_t r = 0; r < nrows; ++r) c += s_slot[r * p.NBQ + qb] >= 0;
-      if (c) atomicAdd(&p.q_member[zh * p.NBQ + qb], c);
-    }
-  }
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int r = warp; r < nrows; r += blockDim.x >> 5) {
     const int64_t kb = kb0 + r;
@@ -168,14 +159,13 @@ __global__ void __launch_bounds__(256) transpose_lists_kernel(TransParams p) {
 int launch_transpose_lists(const int32_t* lists, int64_t list_stride, const int32_t* counts,
                            int64_t ZH, int64_t NBQ, int64_t NBK, int32_t* k_lists,
                            int64_t k_list_stride, int32_t* q_counts, int32_t* k_slots, int pad,
-                           cudaStream_t stream, int32_t* q_member) {
+                           cudaStream_t stream) {
   if (ZH <= 0 || NBK <= 0) return SA_OK;
   const size_t smem = (size_t)kTransRows * NBQ * sizeof(int32_t);
   if (smem > 200 * 1024)
     return fail(SA_EUNSUPPORTED, "transposed lists: too many query blocks (" +
                                      std::to_string(NBQ) + ") for the shared slot table");
-  TransParams p{lists, list_stride, counts, NBQ, NBK, k_lists, k_list_stride, q_counts, k_slots, pad,
-                q_member};
+  TransParams p{lists, list_stride, counts, NBQ, NBK, k_lists, k_list_stride, q_counts, k_slots, pad};
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(transpose_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
@@ -254,7 +244,7 @@ int sa_build_transposed_block_lists(const int32_t* lists, int64_t list_stride,
   if (k_list_stride < 1 || list_stride < 0) return fail(SA_EINVAL, "bad list stride");
   if (ZH > 65535) return fail(SA_EUNSUPPORTED, "Z*H exceeds 65535");
   return launch_transpose_lists(lists, list_stride, counts, ZH, NBQ, NBK, k_lists, k_list_stride,
-                                q_counts, k_slots, 1, (cudaStream_t)stream, nullptr);
+                                q_counts, k_slots, 1, (cudaStream_t)stream);
 }
 
 }  // extern "C"
