@@ -831,17 +831,25 @@ struct FuLayout {
   static constexpr int D = 128;
   static constexpr uint32_t kK = 0;                      // [128][128] (2 boxes of 64 columns)
   static constexpr uint32_t kV = kRows * D * 2;
-  static constexpr uint32_t kQD = 2 * kRows * D * 2;     // stages x (Q, dO, stats)
-  static constexpr uint32_t kStats = 2 * kSub * D * 2;
-  static constexpr uint32_t kStage = kStats + 1024;
+  static constexpr uint32_t kQD = 2 * kRows * D * 2;     // stages x (Q [64][D], dO [64][D])
+  static constexpr uint32_t kStage = 2 * kSub * D * 2;
   static constexpr uint32_t kDsT = kQD + kFuStages * kStage;  // 2 x dS^T [128 keys][64 q] bf16
   static constexpr uint32_t kDsTBytes = kRows * kSub * 2;
-  static constexpr uint32_t kBars = kDsT + 2 * kDsTBytes;
+  static constexpr uint32_t kStg = kDsT + 2 * kDsTBytes;  // per group: dQ rows [32][D] fp32
+  static constexpr uint32_t kStgBytes = 32 * D * 4;
+  static constexpr uint32_t kStats = kStg + 2 * kStgBytes;  // stages x {lse*log2e[64], delta[64]}
+  static constexpr uint32_t kBars = kStats + kFuStages * 512;
   static constexpr uint32_t kMeta = kBars + 256;  // FuMeta[kFuStages]
   static constexpr uint32_t kRingOff = kMeta + 128;
-  static constexpr uint32_t kAlloc = kRingOff + 128 + 1024;
-  static_assert(kDsT % 1024 == 0 && kStage % 1024 == 0, "swizzled tiles need 1024-byte alignment");
-  static_assert(kAlloc <= 232448, "fused backward shared-memory layout too large");
+  static constexpr uint32_t kTmemSlot = kRingOff + 64;
+  static constexpr uint32_t kBytes = kTmemSlot + 16;
+  // alignment slack for the 1024-byte aligned tiles, as far as the opt-in limit allows; the
+  // kernel checks the padding it needs against %dynamic_smem_size
+  static constexpr uint32_t kAlloc = kBytes + 1024 <= 232448 ? kBytes + 1024 : 232448;
+  static_assert(kDsT % 1024 == 0 && kStage % 1024 == 0 && kStg % 1024 == 0,
+                "swizzled tiles need 1024-byte alignment");
+  static_assert(kDsTBytes == kStgBytes, "a dS^T buffer doubles as a dQ staging buffer");
+  static_assert(kBytes <= 232448, "fused backward shared-memory layout too large");
 };
 
 struct FuMeta {
@@ -864,12 +872,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
   using L = FuLayout;
   constexpr int D = L::D;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
+  {
+    const uint32_t base = smem_u32(smem_raw);
+    uint32_t dyn;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    if ((((base + 1023u) & ~1023u) - base) + L::kBytes > dyn) {  // uniform over the CTA
+      if (threadIdx.x == 0) raise_status(a.status, kStatusSmemLayout);
+      return;
+    }
+  }
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
   FuMeta* meta = reinterpret_cast<FuMeta*>(sm + L::kMeta);
   WorkEntry* ring = reinterpret_cast<WorkEntry*>(sm + L::kRingOff);
-  __shared__ uint32_t s_tmem;
+  uint32_t& s_tmem = *reinterpret_cast<uint32_t*>(sm + L::kTmemSlot);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -934,15 +951,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
           meta[st].bias_idx = a.dbias ? (zh * a.NB + qb) * a.list_stride + slot : -1;
           meta[st].b2 = bias_log2(a, it.z, h, qb, slot);
           meta[st].qb = (int)qb;
-          mbar_arrive_expect_tx(&bars[FU_QFULL0 + st], L::kStats + 2 * kSub * 4);
+          mbar_arrive_expect_tx(&bars[FU_QFULL0 + st], L::kStage + 2 * kSub * 4);
           for (int c = 0; c < D / 64; ++c) {
             tma_load_4d(stage + c * kSub * 128, &a.tm_q, &bars[FU_QFULL0 + st], c * 64, (int)q0,
                         (int)h, (int)it.z);
             tma_load_4d(stage + kSub * D * 2 + c * kSub * 128, &a.tm_do, &bars[FU_QFULL0 + st],
                         c * 64, (int)q0, (int)h, (int)it.z);
           }
-          bulk_load(stage + L::kStats, a.stats + (zh * ((a.N + kSub - 1) / kSub) + q0 / kSub) * 2 * kSub,
-                    2 * kSub * 4, &bars[FU_QFULL0 + st]);
+          bulk_load(sm + L::kStats + st * 512,
+                    a.stats + (zh * ((a.N + kSub - 1) / kSub) + q0 / kSub) * 2 * kSub, 2 * kSub * 4,
+                    &bars[FU_QFULL0 + st]);
           ++qd;
           if ((int)++done == e.end - e.begin) fetch.reserve(weight);
           return true;
@@ -1073,11 +1091,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
         if ((int)sb != grp) continue;
         const uint32_t st = qd % kFuStages, ph = (qd / kFuStages) & 1;
         if (!(ok = mbar_wait_warp(&bars[FU_QFULL0 + st], ph, a.status))) break;
-        const float* stats = reinterpret_cast<const float*>(sm + L::kQD + st * L::kStage + L::kStats);
+        const float* stats = reinterpret_cast<const float*>(sm + L::kStats + st * 512);
         const FuMeta m = meta[st];
         const int64_t q0 = m.start;
         if (!(ok = mbar_wait_warp(&bars[FU_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
+        // this group's bulk reductions of its previous sub-tile have read their sources (its
+        // staging buffer and this dS^T buffer) before either is written again
+        if (leader) bulk_wait_read();
+        if (!(ok = group_sync())) break;
         const int64_t cmin = a.causal ? key - q0 : 0;
         const int lo = (int)max((int64_t)0, min((int64_t)kSub, cmin));
         const int hi = key < a.N ? (int)max((int64_t)0, min((int64_t)kSub, a.N - q0)) : 0;
@@ -1149,30 +1171,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars[FU_DQEMPTY0 + sb]);
-        // dQ^T -> fp32 rows [q][d] in this group's dS^T buffer (free: the dQ^T MMA that read it
-        // has completed), 32 query rows = 16 KB at a time, each added into the accumulator by
-        // one bulk reduction (cp.reduce.async.bulk .add.f32, performed at L2)
+        // dQ^T -> fp32 rows [q][d]: query rows 0-31 into this group's staging buffer, 32-63
+        // into this dS^T buffer (free: the dQ^T MMA that read it has completed); each half is
+        // added into the accumulator by one bulk reduction (cp.reduce.async.bulk .add.f32,
+        // performed at L2).  Nobody waits for them here: the next sub-tile of this group
+        // waits for their reads before it writes either buffer.
         const int rows = (int)min((int64_t)kSub, a.N - q0);
-        float* stg = reinterpret_cast<float*>(sm + L::kDsT + sb * L::kDsTBytes);
-        float* gdst = a.dq_acc + (m.zh * a.N + q0) * D;
+        float* stg0 = reinterpret_cast<float*>(sm + L::kStg + grp * L::kStgBytes);
+        float* stg1 = reinterpret_cast<float*>(sm + L::kDsT + sb * L::kDsTBytes);
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          if (hf == 1) {
-            if (leader) bulk_wait_read();  // the first half's reduction has read the buffer
-            if (!(ok = group_sync())) break;
-          }
-#pragma unroll
-          for (int r = 0; r < 32; ++r) stg[r * D + rl] = dq[hf * 32 + r];
-          fence_proxy_async_smem();
-          if (!(ok = group_sync())) break;
-          const int rows_h = min(32, rows - hf * 32);
-          if (leader && rows_h > 0)
-            bulk_reduce_add_f32(gdst + (int64_t)hf * 32 * D, stg, (uint32_t)rows_h * D * 4);
+        for (int r = 0; r < 32; ++r) {
+          stg0[r * D + rl] = dq[r];
+          stg1[r * D + rl] = dq[32 + r];
         }
-        if (!ok) break;
-        // the buffer is this group's dS^T again at its next sub-tile
-        if (leader) bulk_wait_read();
+        fence_proxy_async_smem();
         if (!(ok = group_sync())) break;
+        if (leader) {
+          float* gdst = a.dq_acc + (m.zh * a.N + q0) * D;
+          bulk_reduce_add_f32(gdst, stg0, (uint32_t)min(32, rows) * D * 4);
+          if (rows > 32) bulk_reduce_add_f32(gdst + 32 * D, stg1, (uint32_t)(rows - 32) * D * 4);
+        }
       }
       if (!ok) break;
       if (n > 0) {
