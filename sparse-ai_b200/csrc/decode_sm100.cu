@@ -47,12 +47,13 @@ constexpr int kInitThreads = 1024;
 constexpr int kMaxHeads = 128;
 constexpr int kMaxSelLevels = 16;   // routing levels compared (req_depth)
 constexpr int kCw = 4;              // consumer warps (16 token rows each)
-constexpr int kStreamThreads = 32 * (3 + kCw);  // + producer, epilogue and scheduler warps
-constexpr int kSchedWarp = 2 + kCw;
+constexpr int kSched = 4;           // scheduler warps (items selected concurrently)
+constexpr int kStreamThreads = 32 * (2 + kCw + kSched);  // + producer, epilogue, schedulers
+constexpr int kSchedWarp = 2 + kCw;  // the first scheduler warp
 constexpr int kMaxG = 16;           // MMA rows = query heads of a group
 constexpr int kMaxStages = 8;
 constexpr int kQBufs = 4;   // query buffers: the producer may run 3 chunks ahead of the consumers
-constexpr int kDescs = 4;   // chunk descriptors: the scheduler reserves up to 3 chunks ahead
+constexpr int kDescs = 2 * kSched;  // item descriptors: two per scheduler warp
 constexpr int kFirst = 1, kLast = 2, kEnd = 4;
 
 struct DecHeader {
@@ -66,7 +67,7 @@ static_assert(sizeof(DecHeader) == 256, "DecHeader");
 // covers logical pages [j * PP, min(n_logical, (j + 1) * PP)).
 struct FastWs {
   DecHeader* hdr;
-  int2* rp;     // [B * NP] {request, part} of the parts that hold pages, request-major
+  int4* rp;     // [B * NP] {request, part, n_logical, context length}, request-major
   float* part;  // [BG][NP][G][D + 4]: m (log2 units; -inf = nothing attended), l, 0, 0, acc[D]
   int NP, PP;
 };
@@ -135,7 +136,7 @@ size_t carve(void* base, int64_t B, int64_t Hkv, int64_t maxL, int64_t G, int64_
   };
   FastWs t;
   t.hdr = reinterpret_cast<DecHeader*>(take(sizeof(DecHeader)));
-  t.rp = reinterpret_cast<int2*>(take((size_t)B * NP * 8));
+  t.rp = reinterpret_cast<int4*>(take((size_t)B * NP * 16));
   t.part = reinterpret_cast<float*>(take((size_t)BG * NP * G * (D + 4) * 4));
   t.NP = NP;
   t.PP = PP;
@@ -157,11 +158,11 @@ __global__ void __launch_bounds__(kInitThreads) decode_init_kernel(FastWs w, con
   int run = 0;
   for (int64_t b0 = 0; b0 < B; b0 += kInitThreads) {
     const int64_t b = b0 + tid;
-    int np = 0;
+    int np = 0, nlog = 0, c = 0;
     if (b < B) {
-      const int64_t c = ctx[b];
-      const int64_t nlog = c > 0 ? min((c + page - 1) / page, maxL) : 0;
-      np = (int)((nlog + w.PP - 1) / w.PP);
+      c = ctx[b];
+      nlog = c > 0 ? (int)min((c + page - 1) / page, maxL) : 0;
+      np = (nlog + w.PP - 1) / w.PP;
     }
     int x = np;
 #pragma unroll
@@ -178,7 +179,7 @@ __global__ void __launch_bounds__(kInitThreads) decode_init_kernel(FastWs w, con
     }
     __syncthreads();
     const int first = run + base + x - np;
-    for (int j = 0; j < np; ++j) w.rp[first + j] = make_int2((int)b, j);
+    for (int j = 0; j < np; ++j) w.rp[first + j] = make_int4((int)b, j, nlog, c);
     run += tot;
   }
   if (tid == 0) {
@@ -261,7 +262,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   ChunkDesc* desc = reinterpret_cast<ChunkDesc*>(einfo + 4);  // [kDescs] scheduler -> producer
   uint64_t* dfull = reinterpret_cast<uint64_t*>(desc + kDescs);
   uint64_t* dempty = dfull + kDescs;
-  int32_t* s_qr = reinterpret_cast<int32_t*>(dempty + kDescs);  // scheduler: [G][r] query route
+  // per scheduler warp: the item's query routing words [G][r]
+  int32_t* s_qr_all = reinterpret_cast<int32_t*>(dempty + kDescs);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -292,12 +294,19 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // ---------------- producer ----------------
     uint32_t tile = 0, qi = 0;
     bool ok = true;
-    for (uint32_t d = 0; ok; ++d) {
+    // descriptor d comes from scheduler d % kSched; each scheduler ends with one end marker,
+    // after which its slots are skipped
+    unsigned ended = 0;
+    for (uint32_t d = 0; ok && ended != (1u << kSched) - 1u; ++d) {
       const uint32_t ds = d % kDescs;
+      if (ended & (1u << (d % kSched))) continue;
       if (!(ok = mbar_wait_warp(&dfull[ds], (d / kDescs) & 1, a.status))) break;
       const ChunkDesc& cd = desc[ds];
       const int c = cd.chunk;
-      if (c < 0) break;
+      if (c < 0) {
+        ended |= 1u << (d % kSched);
+        continue;
+      }
       const int bg = cd.bg, nsel = cd.n;
       const int64_t b = bg / a.Hkv, g = bg % a.Hkv;
       if (lane == 0) {
@@ -545,71 +554,93 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfull[eb]);
     }
-  } else if (warp == kSchedWarp) {
-    // ---------------- scheduler: take items and select their pages ----------------
-    // Up to kDescs - 1 items ahead of the producer.  CTA x takes item x first; the queue
-    // counter hands out the rest from item gridDim.x on.  Per item: the query's routing
-    // words of the group's heads into shared memory, then a lane per page (PP <= 64: two
-    // rounds) reads the block-table entry and that page's routing words, and the pages that
-    // some head of the group attends are compacted in logical order into the descriptor.
+  } else if (warp >= kSchedWarp) {
+    // ---------------- schedulers: take items and select their pages ----------------
+    // kSched warps work on different items at once; scheduler w fills descriptors
+    // w, w + kSched, ... (each up to two items ahead of the producer).  The first items
+    // are static (w * gridDim.x + CTA); the queue counter hands out the rest.  Per item:
+    // its {request, part, n_logical, context} entry, then together the query's routing words
+    // of the group's heads and the block-table entries of the part's pages (a lane per page,
+    // two rounds of 32), then each page's routing words of the group's heads; the pages that
+    // some head attends are compacted in logical order into the descriptor.
+    const int sw = warp - kSchedWarp;
+    int32_t* s_qr = s_qr_all + sw * kMaxG * kMaxSelLevels;
     const int n_rp = __ldcg(&a.w.hdr->n_rp);
     const int64_t n_items = (int64_t)n_rp * a.Hkv;
-    const int PP = a.w.PP, NP = a.w.NP, r = a.r;
+    const int PP = a.w.PP, NP = a.w.NP, r = a.r, GR = G * r;
     constexpr int RSP = D + 4;
     bool first = true;
-    for (uint32_t d = 0;; ++d) {
-      const uint32_t ds = d % kDescs;
+    for (uint32_t k = 0;; ++k) {
+      const uint32_t d = sw + k * kSched, ds = d % kDescs;
       if (!mbar_wait_warp(&dempty[ds], ((d / kDescs) & 1) ^ 1, a.status)) break;
       ChunkDesc& cd = desc[ds];
       int slot = -1, bg = 0, nsel = 0;
       for (;;) {
         int64_t idx = 0;
-        if (lane == 0) idx = first ? (int64_t)blockIdx.x : (int64_t)gridDim.x + atomicAdd(&a.w.hdr->next, 1);
+        if (lane == 0)
+          idx = first ? (int64_t)sw * gridDim.x + blockIdx.x
+                      : (int64_t)kSched * gridDim.x + atomicAdd(&a.w.hdr->next, 1);
         first = false;
         idx = __shfl_sync(0xffffffffu, idx, 0);
         if (idx >= n_items) break;
-        const int2 rp = __ldcg(a.w.rp + idx / a.Hkv);
-        const int64_t b = rp.x, g = idx % a.Hkv;
+        const int4 rp = __ldcg(a.w.rp + idx / a.Hkv);
+        const int64_t b = rp.x, g = idx % a.Hkv, nlog = rp.z, cx = rp.w;
         const int part = rp.y;
         bg = (int)(b * a.Hkv + g);
-        const int64_t cx = a.ctx[b];
-        const int64_t nlog = min((cx + a.page - 1) / a.page, a.maxL);
         const int64_t lo = (int64_t)part * PP, hi = min(nlog, lo + PP);
-        for (int i = lane; i < G * r; i += 32)
-          s_qr[i] = (int32_t)load_any_i64(a.qrouter, a.qrouter_dtype,
-                                          b * a.qrs0 + (g * G + i / r) * a.qrs1 + (i % r) * a.qrs2);
+        // query routing words and block-table entries, loads in flight together
+        int32_t qv[kMaxG * kMaxSelLevels / 32];
+#pragma unroll
+        for (int j = 0; j < kMaxG * kMaxSelLevels / 32; ++j) {
+          const int i = lane + 32 * j;
+          qv[j] = i < GR ? (int32_t)load_any_i64(a.qrouter, a.qrouter_dtype,
+                                                 b * a.qrs0 + (g * G + i / r) * a.qrs1 + (i % r) * a.qrs2)
+                         : 0;
+        }
+        const int64_t pg0 = lo + lane, pg1 = lo + 32 + lane;
+        const bool in0 = pg0 < hi, in1 = pg1 < hi;
+        const int ph0 = in0 ? a.bt[b * a.bts0 + pg0 * a.bts1] : 0;
+        const int ph1 = in1 ? a.bt[b * a.bts0 + pg1 * a.bts1] : 0;
+#pragma unroll
+        for (int j = 0; j < kMaxG * kMaxSelLevels / 32; ++j)
+          if (lane + 32 * j < GR) s_qr[lane + 32 * j] = qv[j];
         __syncwarp();
-        nsel = 0;
-        for (int64_t p0 = lo; p0 < hi; p0 += 32) {
-          const int64_t pg = p0 + lane;
-          const bool in = pg < hi;
-          const int phys = in ? a.bt[b * a.bts0 + pg * a.bts1] : 0;
-          // the page's G x r routing words, 16 loads in flight at a time
-          const int GR = G * r;
-          const int64_t base = (int64_t)phys * a.rs0 + g * G * a.rs1;
-          unsigned miss = 0;
-          for (int i0 = 0; i0 < GR; i0 += 16) {
-            int64_t v[16];
+        // both pages' routing words of the group's heads, 16 + 16 loads in flight at a time
+        const int64_t base0 = (int64_t)ph0 * a.rs0 + g * G * a.rs1;
+        const int64_t base1 = (int64_t)ph1 * a.rs0 + g * G * a.rs1;
+        unsigned miss0 = 0, miss1 = 0;
+        for (int i0 = 0; i0 < GR; i0 += 16) {
+          int64_t v0[16], v1[16];
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-              const int i = i0 + u;
-              v[u] = in && i < GR ? load_any_i64(a.router, a.router_dtype,
-                                                  base + (i / r) * a.rs1 + (i % r) * a.rs2)
-                                  : 0;
-            }
+          for (int u = 0; u < 16; ++u) {
+            const int i = i0 + u;
+            const int64_t off = (i / r) * a.rs1 + (i % r) * a.rs2;
+            v0[u] = in0 && i < GR ? load_any_i64(a.router, a.router_dtype, base0 + off) : 0;
+            v1[u] = in1 && i < GR ? load_any_i64(a.router, a.router_dtype, base1 + off) : 0;
+          }
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-              const int i = i0 + u;
-              if (i < GR && v[u] != s_qr[i]) miss |= 1u << (i / r);
+          for (int u = 0; u < 16; ++u) {
+            const int i = i0 + u;
+            if (i < GR) {
+              const int64_t q = s_qr[i];
+              if (v0[u] != q) miss0 |= 1u << (i / r);
+              if (v1[u] != q) miss1 |= 1u << (i / r);
             }
           }
-          const unsigned all = (1u << G) - 1u;
+        }
+        const unsigned all = (1u << G) - 1u;
+        nsel = 0;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int64_t pg = half ? pg1 : pg0;
+          const bool in = half ? in1 : in0;
           const bool forced = (a.sink && pg == 0) || (a.local_blocks > 0 && pg >= nlog - a.local_blocks);
-          const unsigned mask = !in ? 0u : forced ? all : (~miss & all);
+          const unsigned mask = !in ? 0u : forced ? all : (~(half ? miss1 : miss0) & all);
           const unsigned bal = __ballot_sync(0xffffffffu, mask != 0u);
           if (mask) {
             const int valid = (int)min(a.page, cx - pg * a.page);
-            cd.sel[nsel + __popc(bal & ((1u << lane) - 1u))] = make_int2(phys, (int)(mask | ((unsigned)valid << 16)));
+            cd.sel[nsel + __popc(bal & ((1u << lane) - 1u))] =
+                make_int2(half ? ph1 : ph0, (int)(mask | ((unsigned)valid << 16)));
           }
           nsel += __popc(bal);
         }
@@ -733,9 +764,9 @@ int launch_stream(StreamArgs& a, int grid, cudaStream_t stream) {
   // alignment slack, query buffers, 2 merge buffers, then Q / merge barriers, hand-off
   // records, the producer's page batch and the scheduler's descriptors with barriers
   static_assert((2 * kQBufs + 4) * 8 + 16 + kDescs * (sizeof(ChunkDesc) + 16) +
-                    kMaxG * kMaxSelLevels * 4 <= 4096,
+                    kSched * kMaxG * kMaxSelLevels * 4 <= 9216,
                 "decode: barrier, descriptor and query-route area");
-  const size_t fixed = 1024 + kQBufs * (size_t)a.G * D * 2 + 2 * (size_t)kCw * a.G * (D + 4) * 4 + 4096;
+  const size_t fixed = 1024 + kQBufs * (size_t)a.G * D * 2 + 2 * (size_t)kCw * a.G * (D + 4) * 4 + 9216;
   const size_t per_stage = kStage + sizeof(TileMeta) + 16;
   const int stages = (int)std::min<size_t>(kMaxStages, (226 * 1024 - fixed) / per_stage);
   if (stages < 2) return fail(SA_EUNSUPPORTED, "decode: shared memory too small for the ring");
