@@ -309,6 +309,30 @@ SA_API int sa_ultrametric_decode_noalloc(int dtype, int64_t B, int64_t H, int64_
                           void* out, const int64_t* out_strides, void* stream);
 
 /*
+ * Append one token per request to a paged K/V cache (and refresh its page's route).
+ * No counterpart in the reference kernels: sparse-ai's paged decode
+ * (src/ultrametric/kernel_decode.py:188-247) reads such a cache but nothing there writes one
+ * (its surgery layer decodes from a dense cache, src/llama_surgery/surgery.py:883-891); this
+ * is the writer, with the tail-page route refresh of surgery.py:350-374.
+ *
+ * For request b: position pos = context_lens[b], page = block_tables[b][pos / page_size]
+ * (assigned beforehand by the caller's allocator; an unassigned or out-of-range page sets
+ * status bit 2 and skips the request), row pos % page_size of k_cache / v_cache
+ * (P, Hkv, page_size, D) <- k_new / v_new (B, Hkv, D); when routes (B, H, TD) is given,
+ * router (P, H, TD) of that page <- routes[b]; then context_lens[b] = pos + 1.
+ * dtype SA_F32 / SA_F16 / SA_BF16 for K/V, rows 16-byte aligned; routes/router int32 or int64.
+ */
+SA_API int sa_paged_kv_append(int dtype, int64_t B, int64_t Hkv, int64_t D, int64_t page_size,
+                              int64_t num_pages, const void* k_new, const int64_t* k_new_strides,
+                              const void* v_new, const int64_t* v_new_strides,
+                              const int32_t* block_tables, const int64_t* bt_strides,
+                              int64_t max_logical_pages, int32_t* context_lens, void* k_cache,
+                              const int64_t* k_strides, void* v_cache, const int64_t* v_strides,
+                              const void* routes, int routes_dtype, const int64_t* routes_strides,
+                              int64_t H, int64_t TD, void* router, int router_dtype,
+                              const int64_t* router_strides, void* stream);
+
+/*
  * Log-sum-exp merge of partial attention outputs (the combine step of the sequence-sharded
  * ring for very long prefill; the reference has no ring -- its forward LSE output,
  * src/ultrametric/block_list.py:467-470, is the hook this uses).  Per row:

@@ -235,6 +235,36 @@ __device__ __forceinline__ uint32_t swz(int row, int d) {
   return (uint32_t)((d >> 6) * (kTile * 128) + row * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4));
 }
 
+// Which of the group's heads disagree with the query on two pages: bit (i / r) of miss0 /
+// miss1 is set when routing word i (head i / r, level i % r) of the page differs from the
+// query's.  The loads are issued 16 + 16 at a time with no branch between them (the element
+// type is a template parameter, not a run-time switch), so one memory latency covers them.
+template <typename RT>
+__device__ __forceinline__ void route_misses(const RT* __restrict__ router, int64_t base0, int64_t base1,
+                                             bool in0, bool in1, int GR, int r, int64_t rs1,
+                                             int64_t rs2, const int32_t* s_qr, unsigned& miss0,
+                                             unsigned& miss1) {
+  for (int i0 = 0; i0 < GR; i0 += 16) {
+    RT v0[16], v1[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int i = min(i0 + u, GR - 1);  // in range; the word is ignored when i0 + u >= GR
+      const int64_t off = (i / r) * rs1 + (i % r) * rs2;
+      v0[u] = __ldg(router + (in0 ? base0 + off : 0));
+      v1[u] = __ldg(router + (in1 ? base1 + off : 0));
+    }
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int i = i0 + u;
+      if (i < GR) {
+        const int64_t q = s_qr[i];
+        if ((int64_t)v0[u] != q) miss0 |= 1u << (i / r);
+        if ((int64_t)v1[u] != q) miss1 |= 1u << (i / r);
+      }
+    }
+  }
+}
+
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     decode_stream_kernel(const __grid_constant__ StreamArgs a) {
@@ -590,12 +620,22 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         const int64_t lo = (int64_t)part * PP, hi = min(nlog, lo + PP);
         // query routing words and block-table entries, loads in flight together
         int32_t qv[kMaxG * kMaxSelLevels / 32];
+        if (a.qrouter_dtype == SA_I64) {
 #pragma unroll
-        for (int j = 0; j < kMaxG * kMaxSelLevels / 32; ++j) {
-          const int i = lane + 32 * j;
-          qv[j] = i < GR ? (int32_t)load_any_i64(a.qrouter, a.qrouter_dtype,
-                                                 b * a.qrs0 + (g * G + i / r) * a.qrs1 + (i % r) * a.qrs2)
-                         : 0;
+          for (int j = 0; j < kMaxG * kMaxSelLevels / 32; ++j) {
+            const int i = min(lane + 32 * j, GR - 1);
+            qv[j] = GR > 0 ? (int32_t)__ldg(static_cast<const int64_t*>(a.qrouter) + b * a.qrs0 +
+                                            (g * G + i / r) * a.qrs1 + (i % r) * a.qrs2)
+                           : 0;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kMaxG * kMaxSelLevels / 32; ++j) {
+            const int i = min(lane + 32 * j, GR - 1);
+            qv[j] = GR > 0 ? __ldg(static_cast<const int32_t*>(a.qrouter) + b * a.qrs0 +
+                                   (g * G + i / r) * a.qrs1 + (i % r) * a.qrs2)
+                           : 0;
+          }
         }
         const int64_t pg0 = lo + lane, pg1 = lo + 32 + lane;
         const bool in0 = pg0 < hi, in1 = pg1 < hi;
@@ -609,25 +649,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         const int64_t base0 = (int64_t)ph0 * a.rs0 + g * G * a.rs1;
         const int64_t base1 = (int64_t)ph1 * a.rs0 + g * G * a.rs1;
         unsigned miss0 = 0, miss1 = 0;
-        for (int i0 = 0; i0 < GR; i0 += 16) {
-          int64_t v0[16], v1[16];
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int i = i0 + u;
-            const int64_t off = (i / r) * a.rs1 + (i % r) * a.rs2;
-            v0[u] = in0 && i < GR ? load_any_i64(a.router, a.router_dtype, base0 + off) : 0;
-            v1[u] = in1 && i < GR ? load_any_i64(a.router, a.router_dtype, base1 + off) : 0;
-          }
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int i = i0 + u;
-            if (i < GR) {
-              const int64_t q = s_qr[i];
-              if (v0[u] != q) miss0 |= 1u << (i / r);
-              if (v1[u] != q) miss1 |= 1u << (i / r);
-            }
-          }
-        }
+        if (a.router_dtype == SA_I64)
+          route_misses(static_cast<const int64_t*>(a.router), base0, base1, in0, in1, GR, r, a.rs1,
+                       a.rs2, s_qr, miss0, miss1);
+        else
+          route_misses(static_cast<const int32_t*>(a.router), base0, base1, in0, in1, GR, r, a.rs1,
+                       a.rs2, s_qr, miss0, miss1);
         const unsigned all = (1u << G) - 1u;
         nsel = 0;
 #pragma unroll

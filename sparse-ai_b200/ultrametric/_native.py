@@ -33,6 +33,9 @@ _SIGNATURES = {
     "sa_abi_version": (_i32, []),
     "sa_read_device_status": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint)]),
     "sa_release_thread_resources": (_i32, []),
+    "sa_paged_kv_append": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _vp, _p64, _vp, _p64, _vp,
+                                   _p64, _i64, _vp, _vp, _p64, _vp, _p64, _vp, _i32, _p64, _i64,
+                                   _i64, _vp, _i32, _p64, _vp]),
     "sa_build_block_lists_from_assignments": (_i32, [_vp, _i32, _p64, _i64, _i64, _i64, _i64,
                                                       _i64, _i64, _i64, _vp, _i64, _i32, _i32,
                                                       _i64, _vp, _vp, _i64, _vp, _vp]),
