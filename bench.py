@@ -703,7 +703,7 @@ def run_decode(dev, seed, steps, warmup, flush, peaks, world=1, rank=0, barrier=
         # per GPU (the slowest rank), against one GPU's measured copy bandwidth
         "roofline": {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(gbs / world / peaks["hbm_gbs"], 4), "per": "GPU"},
-        "gpu_launches_per_step": 3,
+        "gpu_launches_per_step": 4,
     }
     if world > 1:
         per = B // world

@@ -333,6 +333,24 @@ SA_API int sa_paged_kv_append(int dtype, int64_t B, int64_t Hkv, int64_t D, int6
                               const int64_t* router_strides, void* stream);
 
 /*
+ * Ternary K/V rows: quantise + pack, and unpack + dequantise.
+ * Replaces: src/llama_surgery/surgery.py:15-75 (TernaryQuantize.forward, pack_ternary,
+ * unpack_ternary) and the in-kernel unpacking of kernel.py:198-205, 226-232.
+ *
+ * quantize_pack: x (rows, D) of dtype (row stride x_row_stride, D contiguous, D % 16 == 0) ->
+ *   scale[row] = mean |x[row]| (fp32), and packed (rows, D / 16) int32 contiguous: value i of
+ *   16-value group w in bits [2i, 2i + 2) of word w, code 1 where x > scale / 2, 2 where
+ *   x < -scale / 2, 0 otherwise.
+ * dequantize: packed, scale -> out (rows, D) of dtype: code 1 -> +scale, 2 -> -scale, 0 -> 0.
+ */
+SA_API int sa_ternary_quantize_pack(int dtype, int64_t rows, int64_t D, const void* x,
+                                    int64_t x_row_stride, int32_t* packed, float* scale,
+                                    void* stream);
+SA_API int sa_ternary_dequantize(int dtype, int64_t rows, int64_t D, const int32_t* packed,
+                                 const float* scale, void* out, int64_t out_row_stride,
+                                 void* stream);
+
+/*
  * Log-sum-exp merge of partial attention outputs (the combine step of the sequence-sharded
  * ring for very long prefill; the reference has no ring -- its forward LSE output,
  * src/ultrametric/block_list.py:467-470, is the hook this uses).  Per row:

@@ -1,5 +1,5 @@
-// Routed paged decode, B200 fast path: page selection inside a persistent streaming kernel,
-// TMA page streaming, and the score / value products on the tensor cores.
+// Routed paged decode, B200 fast path: balanced page chunks on a dynamic queue, TMA page
+// streaming, and the score / value products on the tensor cores.
 //
 // Semantics are those of src/ultrametric/kernel_decode.py:23-124 in sparse-ai (and of the
 // general path in decode.cu): request b, query head h attends the logical pages whose
@@ -7,30 +7,31 @@
 // q_router[b, h, :r], plus logical page 0 (sink) and the last `local_blocks` pages; tokens
 // >= context_lens[b] are masked; a request with no attended token gets zeros.
 //
-// A "unit" is one (request b, KV head g), bg = b * Hkv + g.  A work item is one unit's part
-// of PP consecutive logical pages (PP chosen on the host so that there are a few items per
-// SM).  Three kernels, each launched as the programmatic dependent of the one before:
+// A "unit" is one (request b, KV head g), bg = b * Hkv + g.  Four kernels, the last three
+// launched as programmatic dependents of the one before (their prologues overlap it):
 //
-//  1. decode_init_kernel (one CTA): zeroes the item queue and lists the (request, part)
-//     pairs that hold pages (a scan over the requests' context lengths), so the items are
-//     the pairs x KV heads with no empty ones in between.
-//  2. decode_stream_kernel, one persistent CTA per SM taking items from an atomic queue.
-//     Warp 6 (scheduler) selects each item's pages itself, up to three items ahead of the
-//     producer: the item's block-table entries (a lane per page), then the group's routing
-//     words of those pages against the query's, giving per page the mask of the group's
-//     query heads that attend it; the selected pages are compacted in order into a
-//     descriptor {physical page, head mask | valid tokens << 16}.  An item that selects
-//     nothing marks its partial empty and costs no streaming.  Warp 0 streams each item's
-//     K/V pages with TMA (4-D tensor maps over the paged caches) into a ring of 64-token
-//     tiles and the group's G query rows with a bulk copy.  Warps 1-4 each own 16 token rows
-//     of every tile: S = Q K^T and O += P V as m16n8k16 MMAs whose 16 rows are the group's
-//     query heads (so K and V bytes are read once per KV head), online softmax in registers in
-//     the log2 domain.  At an item's end they hand their states to warp 5 through a
-//     double-buffered shared area; warp 5 merges them into one partial (m, l, acc[D]) per
-//     query head.  The products are < 1 % of the tensor pipe at HBM speed, so the warp-level
-//     MMA is enough; what matters is that the ring keeps ~200 KB of loads in flight per SM.
-//  3. decode_unit_combine_kernel, one CTA per unit: merges the unit's part partials by
-//     log-sum-exp weights and writes its G output rows (zeros when nothing was attended).
+//  1. decode_init_kernel: zeroes the work header (selection ticket, queue counter).
+//  2. decode_select_kernel, one CTA per (request, part of its logical pages): one pass over
+//     the part's pages (a warp per 8 pages; each page's [H][TD] routing block read as
+//     coalesced 128-byte runs) writes, per KV head, the ascending list of the part's pages
+//     selected by ANY query head of the group as {physical page, head mask | valid tokens
+//     << 16}.  The last CTA to finish (atomic ticket) cuts every list into chunks of `chp`
+//     pages, chp chosen so that the batch has about kChunkTarget chunks whatever the spread
+//     of context lengths, writes the chunk table, and zeroes the output rows of units that
+//     attend no page.
+//  3. decode_stream_kernel, one persistent CTA per SM taking chunks from an atomic queue.
+//     Warp 6 reserves the next chunk and fetches its table entry and first page entries
+//     one chunk ahead of warp 0, which streams each chunk's K/V pages with TMA (4-D tensor
+//     maps over the paged caches) into a ring of 64-token tiles and the chunk's G query rows
+//     with a bulk copy.  Warps 1-4 each own 16 token rows of every tile: S = Q K^T and
+//     O += P V as m16n8k16 MMAs whose 16 rows are the group's query heads (so K and V bytes
+//     are read once per KV head), online softmax in registers in the log2 domain.  At a
+//     chunk's end they hand their states to warp 5 through a double-buffered shared area
+//     and go on; warp 5 merges them into one partial (m, l, acc[D]) per query head.  The
+//     products are < 1 % of the tensor pipe at HBM speed, so the warp-level MMA is enough;
+//     what matters is that the ring keeps ~200 KB of loads in flight per SM.
+//  4. decode_unit_combine_kernel, one CTA per unit: merges the unit's chunk partials by
+//     log-sum-exp weights and writes its G output rows.
 #include <algorithm>
 #include <string>
 #include <type_traits>
@@ -42,34 +43,45 @@ namespace sa {
 namespace {
 
 constexpr int kTile = 64;           // token rows per ring stage
-constexpr int kMaxPP = 64;          // logical pages per work item (at most)
-constexpr int kInitThreads = 1024;
-constexpr int kMaxHeads = 128;
-constexpr int kMaxSelLevels = 16;   // routing levels compared (req_depth)
+constexpr int kChunkTarget = 2048;  // chunks per batch; bounds the partials workspace
+constexpr int kMaxUnitChunks = 32;  // chunks per unit; bounds the final merge
+constexpr int kSelThreads = 256;
+constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kSelTile = kSelThreads;  // pages per pass of the selection kernel
+constexpr int kSelSplitCtas = 296;     // selection CTAs at most: 2 resident per SM, one wave
+constexpr int kMaxParts = 16;          // parts per request
+constexpr int kMaxHeadWords = 4;       // query heads <= 128
+constexpr int kMaxHeads = kMaxHeadWords * 32;
+constexpr int kMaxSelLevels = 16;      // routing levels compared (req_depth)
 constexpr int kCw = 4;              // consumer warps (16 token rows each)
-constexpr int kSched = 4;           // scheduler warps (items selected concurrently)
-constexpr int kStreamThreads = 32 * (2 + kCw + kSched);  // + producer, epilogue, schedulers
-constexpr int kSchedWarp = 2 + kCw;  // the first scheduler warp
+constexpr int kStreamThreads = 32 * (3 + kCw);  // + producer, epilogue and scheduler warps
+constexpr int kSchedWarp = 2 + kCw;
 constexpr int kMaxG = 16;           // MMA rows = query heads of a group
 constexpr int kMaxStages = 8;
 constexpr int kQBufs = 4;   // query buffers: the producer may run 3 chunks ahead of the consumers
-constexpr int kDescs = 2 * kSched;  // item descriptors: two per scheduler warp
+constexpr int kDescs = 4;   // chunk descriptors: the scheduler reserves up to 3 chunks ahead
 constexpr int kFirst = 1, kLast = 2, kEnd = 4;
 
 struct DecHeader {
-  int next;   // queue counter of the stream kernel
-  int n_rp;   // (request, part) pairs that hold pages
-  int pad[62];
+  unsigned ticket;  // CTAs of the select kernel that finished
+  int n_chunks;
+  int chp;          // pages per chunk
+  int next;         // queue counter of the stream kernel
+  unsigned long long total;  // selected (unit, page) pairs, summed by the select CTAs
+  int pad[58];
 };
 static_assert(sizeof(DecHeader) == 256, "DecHeader");
 
-// Items: index i -> (request, part) pair rp[i / Hkv], KV head i % Hkv.  Part j of request b
-// covers logical pages [j * PP, min(n_logical, (j + 1) * PP)).
+// A request's logical pages are selected in P parts of `seg` pages (one CTA each); part q of
+// unit bg writes its list at sel[bg][q * seg ...] and its length at count[bg][q].
 struct FastWs {
   DecHeader* hdr;
-  int4* rp;     // [B * NP] {request, part, n_logical, context length}, request-major
-  float* part;  // [BG][NP][G][D + 4]: m (log2 units; -inf = nothing attended), l, 0, 0, acc[D]
-  int NP, PP;
+  int* count;   // [BG][P] selected pages of each unit's parts
+  int2* uinfo;  // [BG] {first chunk, chunks} of each unit
+  int4* table;  // [max chunks] {unit, first | end list index << 16, unit's first chunk, chunks}
+  int2* sel;    // [BG][P * seg] {physical page, head mask | valid tokens << 16}
+  float* part;  // [max chunks][G][D + 4]: m (log2 units), l, 0, 0, acc[D]
+  int P, seg;
 };
 
 struct TileMeta {
@@ -81,11 +93,10 @@ struct TileMeta {
 };
 static_assert(sizeof(TileMeta) == 32, "TileMeta");
 
-// A reserved item with its selected pages, prepared by the scheduler warp.
+// A reserved chunk with its first 32 list entries, prepared by the scheduler warp.
 struct ChunkDesc {
-  int chunk;  // partial slot bg * NP + part, or -1 (no more work)
-  int bg, n, pad;
-  int2 sel[kMaxPP];  // {physical page, head mask | valid tokens << 16}
+  int chunk, bg, p0, p1;
+  int2 sel[32];
 };
 
 struct StreamArgs {
@@ -94,39 +105,33 @@ struct StreamArgs {
   int64_t qs0, qs1;
   void* out;
   int64_t os0, os1;
-  int64_t Hkv, page;
+  int64_t Hkv, sel_row, page;
   int G, ppt, stages;
   float scale2;
   FastWs w;
-  // selection inputs (DecodeParams subset)
-  const int32_t* bt;
-  int64_t bts0, bts1;
-  const int32_t* ctx;
-  const void* router;
-  int router_dtype;
-  int64_t rs0, rs1, rs2;
-  const void* qrouter;
-  int qrouter_dtype;
-  int64_t qrs0, qrs1, qrs2;
-  int64_t maxL, local_blocks;
-  int r, sink;
   unsigned* status;
 };
 
 inline size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// Logical pages per work item: 64, halved (down to 8) while the batch would give fewer than
-// about four items per SM.
-int pages_per_item(int64_t B, int64_t Hkv, int64_t maxL, int sms) {
-  int pp = kMaxPP;
-  while (pp > 8 && B * Hkv * ((std::max<int64_t>(maxL, 1) + pp - 1) / pp) < 4 * (int64_t)sms) pp /= 2;
-  return pp;
+// Parts per request: enough selection CTAs to cover the GPU, parts of >= 64 pages.
+int sel_parts(int64_t B, int64_t maxL) {
+  const int64_t want = kSelSplitCtas / std::max<int64_t>(B, 1);
+  const int64_t cap = std::max<int64_t>(1, (maxL + 63) / 64);
+  return (int)std::max<int64_t>(1, std::min<int64_t>({kMaxParts, want, cap}));
+}
+
+// Chunks never span two parts: a unit has <= (its pages / chunk pages) + P chunks.
+int64_t max_chunks(int64_t BG, int64_t maxL, int P) {
+  return BG * P + std::min<int64_t>(kChunkTarget, BG * std::max<int64_t>(maxL, 1));
 }
 
 // Workspace layout; returns its size.  Fills *w when base is given.
-size_t carve(void* base, int64_t B, int64_t Hkv, int64_t maxL, int64_t G, int64_t D, int PP, FastWs* w) {
+size_t carve(void* base, int64_t B, int64_t Hkv, int64_t maxL, int64_t G, int64_t D, FastWs* w) {
   const int64_t BG = B * Hkv;
-  const int NP = (int)((std::max<int64_t>(maxL, 1) + PP - 1) / PP);
+  const int P = sel_parts(B, maxL);
+  const int seg = (int)((std::max<int64_t>(maxL, 1) + P - 1) / P);
+  const int64_t mc = max_chunks(BG, maxL, P);
   char* c = static_cast<char*>(base);
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -136,55 +141,267 @@ size_t carve(void* base, int64_t B, int64_t Hkv, int64_t maxL, int64_t G, int64_
   };
   FastWs t;
   t.hdr = reinterpret_cast<DecHeader*>(take(sizeof(DecHeader)));
-  t.rp = reinterpret_cast<int4*>(take((size_t)B * NP * 16));
-  t.part = reinterpret_cast<float*>(take((size_t)BG * NP * G * (D + 4) * 4));
-  t.NP = NP;
-  t.PP = PP;
+  t.count = reinterpret_cast<int*>(take((size_t)BG * P * 4));
+  t.uinfo = reinterpret_cast<int2*>(take((size_t)BG * 8));
+  t.table = reinterpret_cast<int4*>(take((size_t)mc * 16));
+  t.sel = reinterpret_cast<int2*>(take((size_t)BG * P * seg * 8));
+  t.part = reinterpret_cast<float*>(take((size_t)mc * G * (D + 4) * 4));
+  t.P = P;
+  t.seg = seg;
   if (w) *w = t;
   return o;
 }
 
 // ---------------------------------------------------------------------------------------
-// 1. the item list
+// 1-2. page selection and chunking
 // ---------------------------------------------------------------------------------------
-// One CTA: the (request, part) pairs holding pages, request-major, by an exclusive scan of
-// the parts per request over the batch.
-__global__ void __launch_bounds__(kInitThreads) decode_init_kernel(FastWs w, const int32_t* ctx,
-                                                                   int64_t B, int64_t page,
-                                                                   int64_t maxL) {
+__global__ void decode_init_kernel(DecHeader* hdr) {
   pdl_trigger();
-  __shared__ int s_warp[kInitThreads / 32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int run = 0;
-  for (int64_t b0 = 0; b0 < B; b0 += kInitThreads) {
-    const int64_t b = b0 + tid;
-    int np = 0, nlog = 0, c = 0;
-    if (b < B) {
-      c = ctx[b];
-      nlog = c > 0 ? (int)min((c + page - 1) / page, maxL) : 0;
-      np = (nlog + w.PP - 1) / w.PP;
-    }
-    int x = np;
+  hdr->ticket = 0;
+  hdr->next = 0;
+  hdr->total = 0;
+}
+
+// Exclusive prefix of v over the CTA (kSelThreads threads); *total gets the sum.
+__device__ __forceinline__ int cta_excl_scan(int v, int* s_warp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  int base = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < kSelThreads / 32; ++w) {
+    const int t = s_warp[w];
+    base += w < warp ? t : 0;
+    tot += t;
+  }
+  __syncthreads();  // s_warp may be rewritten by the next call
+  *total = tot;
+  return base + x - v;
+}
+
+// One CTA per request.  Pass 1 (per 512-page tile): each warp takes 4 pages at a time, its
+// lanes the query heads, so a page's routing vectors for all heads are read as one
+// contiguous run; a ballot per page gives the H-bit mask of heads that select it.  Pass 2:
+// one thread per page, per KV group a warp ballot + per-warp counts give the ascending
+// compaction of the group's selected pages into the unit's list.
+template <typename RT, int PP, int KK>
+__global__ void __launch_bounds__(kSelThreads, 2) decode_select_kernel(const DecodeParams p,
+                                                                    const FastWs w, int ppt) {
+  const RT* router = static_cast<const RT*>(p.router);
+  pdl_trigger();
+  const int part = blockIdx.x;
+  const int64_t b = blockIdx.y;
+  const int H = (int)p.H, G = (int)p.G, r = (int)p.r, Hkv = (int)p.Hkv;
+  const int HW = (H + 31) / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ uint32_t s_hmask[kSelTile][kMaxHeadWords];
+  __shared__ int s_phys[kSelTile];
+  __shared__ int s_valid[kSelTile];
+  __shared__ int32_t s_qr[kMaxHeads][kMaxSelLevels + 1];  // padded: lanes over heads, distinct banks
+  __shared__ uint8_t s_miss[kSelWarps][PP * kMaxHeads];  // per warp: [page of the step][head]
+  __shared__ int s_cnt[kSelWarps][kMaxHeadWords * 32];
+  __shared__ int s_run[kMaxHeadWords * 32];
+  __shared__ int s_warp[kSelWarps];
+  __shared__ long long s_sum[kSelWarps];
+  __shared__ int s_last;
+  const int64_t ctx = p.ctx[b];
+  // Lanes run over the (head, level < r) pairs that are compared, KK words per lane and PP
+  // pages per step: the loads of one step (PP * KK per lane) are all in flight together.
+  constexpr int NST = 32 / PP;  // steps covered by one block-table load per lane
+  const int64_t lo = (int64_t)part * w.seg;
+  // Warp w takes a tile's pages s * 8PP + w * PP + [0, PP) in steps s < NST; one block-table
+  // load per lane covers all NST steps.  The first tile's load is issued with the context
+  // length's: it reads within the part and the table's width, and entries past the context
+  // are never used.
+  const int my_lt = (lane / PP) * (kSelWarps * PP) + warp * PP + (lane % PP);
+  int my_phys_next =
+      my_lt < min((int64_t)min(kSelTile, w.seg), p.maxL - lo) ? p.bt[b * p.bts[0] + (lo + my_lt) * p.bts[1]] : 0;
+  for (int i = tid; i < H * r; i += kSelThreads) {
+    const int h = i / r, lvl = i % r;
+    s_qr[h][lvl] = (int32_t)load_any_i64(p.qrouter, p.qrouter_dtype,
+                                         b * p.qrs[0] + h * p.qrs[1] + lvl * p.qrs[2]);
+  }
+  for (int g = tid; g < Hkv; g += kSelThreads) s_run[g] = 0;
+  __syncthreads();
+  // logical pages past the block table's width are not read (a consistent request has none)
+  const int64_t nlog = ctx > 0 ? min((ctx + p.page - 1) / p.page, p.maxL) : 0;
+  const int HR = H * r;
+  uint8_t* mflag = s_miss[warp];
+  const int64_t hi = min(nlog, lo + w.seg);
+  const int64_t row = (int64_t)w.P * w.seg;  // one unit's list row
+  for (int64_t t0 = lo; t0 < hi; t0 += kSelTile) {
+    const int tn = (int)min((int64_t)kSelTile, hi - t0);
+    // ---- pass 1: head masks
+    const int my_phys = my_phys_next;  // entries past tn are never used
+    if (t0 + kSelTile < hi) {
+      const int64_t nt = min((int64_t)kSelTile, hi - t0 - kSelTile);
+      my_phys_next = my_lt < nt ? p.bt[b * p.bts[0] + (t0 + kSelTile + my_lt) * p.bts[1]] : 0;
     }
-    if (lane == 31) s_warp[warp] = x;
-    __syncthreads();
-    int base = 0, tot = 0;
-    for (int i = 0; i < kInitThreads / 32; ++i) {
-      base += i < warp ? s_warp[i] : 0;
-      tot += s_warp[i];
+    for (int st = 0; st < NST; ++st) {
+      const int lt = st * (kSelWarps * PP) + warp * PP;  // first page of this step
+      if (lt >= tn) break;
+      int ph[PP];  // pages past the tile's end repeat the step's first page (ignored)
+#pragma unroll
+      for (int u = 0; u < PP; ++u) ph[u] = __shfl_sync(0xffffffffu, my_phys, st * PP + (lt + u < tn ? u : 0));
+      for (int x = lane; x < PP * kMaxHeads / 4; x += 32) reinterpret_cast<uint32_t*>(mflag)[x] = 0u;
+      __syncwarp();
+      for (int k0 = 0; k0 < HR; k0 += 32 * KK) {
+        int64_t off[KK];
+#pragma unroll
+        for (int kk = 0; kk < KK; ++kk) {
+          const int jp = min(k0 + kk * 32 + lane, HR - 1);
+          const int h = jp / r, lvl = jp - h * r;
+          off[kk] = h * p.rs[1] + lvl * p.rs[2];
+        }
+        RT v[PP][KK];
+#pragma unroll
+        for (int u = 0; u < PP; ++u)
+#pragma unroll
+          for (int kk = 0; kk < KK; ++kk) v[u][kk] = __ldg(router + (int64_t)ph[u] * p.rs[0] + off[kk]);
+#pragma unroll
+        for (int kk = 0; kk < KK; ++kk) {
+          const int jp = k0 + kk * 32 + lane;
+          if (jp < HR) {
+            const int h = jp / r, lvl = jp - h * r;
+            const int64_t q = s_qr[h][lvl];
+#pragma unroll
+            for (int u = 0; u < PP; ++u)
+              if ((int64_t)v[u][kk] != q) mflag[u * kMaxHeads + h] = 1;
+          }
+        }
+      }
+      __syncwarp();
+      for (int hc = 0; hc < HW; ++hc) {
+        const int h = hc * 32 + lane;
+        const bool active = h < H;
+#pragma unroll
+        for (int u = 0; u < PP; ++u) {
+          const int64_t l = t0 + lt + u;
+          const bool forced = (p.sink && l == 0) || (p.local_blocks > 0 && l >= nlog - p.local_blocks);
+          const bool match = active && (forced || !mflag[u * kMaxHeads + (active ? h : 0)]);
+          const unsigned m = __ballot_sync(0xffffffffu, match);
+          if (lane == 0 && lt + u < tn) s_hmask[lt + u][hc] = m;
+        }
+      }
+      const int phys_l = __shfl_sync(0xffffffffu, my_phys, st * PP + (lane % PP));  // all lanes
+      if (lane < PP && lt + lane < tn) {
+        s_phys[lt + lane] = phys_l;
+        s_valid[lt + lane] = (int)min(p.page, ctx - (t0 + lt + lane) * p.page);
+      }
     }
     __syncthreads();
-    const int first = run + base + x - np;
-    for (int j = 0; j < np; ++j) w.rp[first + j] = make_int4((int)b, j, nlog, c);
-    run += tot;
+    // ---- pass 2: per-group ascending compaction of this tile (one thread per page)
+    const int i = tid;
+    auto group_bits = [&](int g) -> unsigned {
+      if (i >= tn) return 0u;
+      const int bit = g * G, wd = bit >> 5, off = bit & 31;
+      uint64_t x = s_hmask[i][wd];
+      if (wd + 1 < HW) x |= (uint64_t)s_hmask[i][wd + 1] << 32;
+      return (unsigned)((x >> off) & ((1ull << G) - 1ull));
+    };
+    for (int g = 0; g < Hkv; ++g) {
+      const unsigned bl = __ballot_sync(0xffffffffu, group_bits(g) != 0u);
+      if (lane == 0) s_cnt[warp][g] = __popc(bl);
+    }
+    __syncthreads();
+    for (int g = tid; g < Hkv; g += kSelThreads) {  // exclusive prefix over the warp slices
+      int run = s_run[g];
+      for (int q = 0; q < kSelWarps; ++q) {
+        const int c = s_cnt[q][g];
+        s_cnt[q][g] = run;
+        run += c;
+      }
+      s_run[g] = run;
+    }
+    __syncthreads();
+    for (int g = 0; g < Hkv; ++g) {
+      const unsigned gb = group_bits(g);
+      const unsigned bl = __ballot_sync(0xffffffffu, gb != 0u);
+      if (gb) {
+        const int pos = s_cnt[warp][g] + __popc(bl & ((1u << lane) - 1u));
+        w.sel[(b * Hkv + g) * row + (int64_t)part * w.seg + pos] =
+            make_int2(s_phys[i], (int)(gb | ((unsigned)s_valid[i] << 16)));
+      }
+    }
+    __syncthreads();  // the tile's shared arrays are rewritten by the next tile
+  }
+  long long mine = 0;
+  for (int g = tid; g < Hkv; g += kSelThreads) {
+    w.count[(b * Hkv + g) * w.P + part] = s_run[g];
+    mine += s_run[g];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+  if (lane == 0) s_sum[warp] = mine;
+
+  // The CTA adds its selected pairs to the header's total, then takes a ticket; the last CTA
+  // to finish cuts the lists into chunks (the header was zeroed by the init kernel, which
+  // must have completed).
+  pdl_wait();
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    long long cta = 0;
+    for (int i = 0; i < kSelWarps; ++i) cta += s_sum[i];
+    if (cta) atomicAdd(&w.hdr->total, (unsigned long long)cta);
+    __threadfence();
+    s_last = atomicAdd(&w.hdr->ticket, 1u) == gridDim.x * gridDim.y - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int64_t BG = p.B * p.Hkv;
+  const int P = w.P;
+  const long long total = (long long)__ldcg(&w.hdr->total);
+  int chp = (int)std::max<long long>(ppt, (total + kChunkTarget - 1) / kChunkTarget);
+  chp = (chp + ppt - 1) / ppt * ppt;
+  int run = 0;
+  uint16_t* out = static_cast<uint16_t*>(p.out);
+  for (int64_t i0 = 0; i0 < BG; i0 += kSelThreads) {
+    const int64_t i = i0 + tid;
+    int cnt[kMaxParts];  // this unit's part lengths, loaded once
+#pragma unroll
+    for (int q = 0; q < kMaxParts; ++q) cnt[q] = i < BG && q < P ? __ldcg(w.count + i * P + q) : 0;
+    int cu_tot = 0;
+#pragma unroll
+    for (int q = 0; q < kMaxParts; ++q) cu_tot += cnt[q];
+    // a long list gets longer chunks so that its final merge reads about kMaxUnitChunks
+    // partials; chunks never span two parts
+    int cu = max(chp, (cu_tot + kMaxUnitChunks - 1) / kMaxUnitChunks);
+    cu = (cu + ppt - 1) / ppt * ppt;
+    int n = 0;
+#pragma unroll
+    for (int q = 0; q < kMaxParts; ++q) n += (cnt[q] + cu - 1) / cu;
+    int t;
+    const int base = run + cta_excl_scan(n, s_warp, &t);
+    if (i < BG) {
+      w.uinfo[i] = make_int2(base, n);
+      int k = 0;
+#pragma unroll
+      for (int q = 0; q < kMaxParts; ++q) {
+        const int c = cnt[q], off = q * w.seg;
+        for (int pb = 0; pb < c; pb += cu, ++k) {
+          const int pe = off + min(c, pb + cu);
+          w.table[base + k] = make_int4((int)i, (off + pb) | (pe << 16), base, n);
+        }
+      }
+      if (cu_tot == 0) {  // a unit with no page: its rows are zero (no chunk writes them)
+        const int64_t b = i / p.Hkv, g = i % p.Hkv;
+        for (int j = 0; j < G * p.D; ++j)
+          out[b * p.os[0] + (g * G + j / p.D) * p.os[1] + j % p.D] = 0;  // +0.0 in bf16 and fp16
+      }
+    }
+    run += t;
   }
   if (tid == 0) {
-    w.hdr->next = 0;
-    w.hdr->n_rp = run;
+    w.hdr->n_chunks = run;
+    w.hdr->chp = chp;
   }
 }
 
@@ -235,36 +452,6 @@ __device__ __forceinline__ uint32_t swz(int row, int d) {
   return (uint32_t)((d >> 6) * (kTile * 128) + row * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4));
 }
 
-// Which of the group's heads disagree with the query on two pages: bit (i / r) of miss0 /
-// miss1 is set when routing word i (head i / r, level i % r) of the page differs from the
-// query's.  The loads are issued 16 + 16 at a time with no branch between them (the element
-// type is a template parameter, not a run-time switch), so one memory latency covers them.
-template <typename RT>
-__device__ __forceinline__ void route_misses(const RT* __restrict__ router, int64_t base0, int64_t base1,
-                                             bool in0, bool in1, int GR, int r, int64_t rs1,
-                                             int64_t rs2, const int32_t* s_qr, unsigned& miss0,
-                                             unsigned& miss1) {
-  for (int i0 = 0; i0 < GR; i0 += 16) {
-    RT v0[16], v1[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int i = min(i0 + u, GR - 1);  // in range; the word is ignored when i0 + u >= GR
-      const int64_t off = (i / r) * rs1 + (i % r) * rs2;
-      v0[u] = __ldg(router + (in0 ? base0 + off : 0));
-      v1[u] = __ldg(router + (in1 ? base1 + off : 0));
-    }
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int i = i0 + u;
-      if (i < GR) {
-        const int64_t q = s_qr[i];
-        if ((int64_t)v0[u] != q) miss0 |= 1u << (i / r);
-        if ((int64_t)v1[u] != q) miss1 |= 1u << (i / r);
-      }
-    }
-  }
-}
-
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     decode_stream_kernel(const __grid_constant__ StreamArgs a) {
@@ -289,11 +476,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   uint64_t* mfull = qempty + kQBufs;
   uint64_t* mempty = mfull + 2;
   int* einfo = reinterpret_cast<int*>(mempty + 2);   // [2] chunk handed to the epilogue warp
-  ChunkDesc* desc = reinterpret_cast<ChunkDesc*>(einfo + 4);  // [kDescs] scheduler -> producer
+  int2* s_sel = reinterpret_cast<int2*>(einfo + 4);  // [32] producer's page batch
+  ChunkDesc* desc = reinterpret_cast<ChunkDesc*>(s_sel + 32);  // [kDescs] scheduler -> producer
   uint64_t* dfull = reinterpret_cast<uint64_t*>(desc + kDescs);
   uint64_t* dempty = dfull + kDescs;
-  // per scheduler warp: the item's query routing words [G][r]
-  int32_t* s_qr_all = reinterpret_cast<int32_t*>(dempty + kDescs);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -318,26 +504,19 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     prefetch_tmap(&a.tm_v);
   }
   __syncthreads();
-  pdl_wait();  // the init kernel's item list and queue header are complete from here on
+  pdl_wait();  // the selection kernel's lists, table and header are complete from here on
 
   if (warp == 0) {
     // ---------------- producer ----------------
     uint32_t tile = 0, qi = 0;
     bool ok = true;
-    // descriptor d comes from scheduler d % kSched; each scheduler ends with one end marker,
-    // after which its slots are skipped
-    unsigned ended = 0;
-    for (uint32_t d = 0; ok && ended != (1u << kSched) - 1u; ++d) {
+    for (uint32_t d = 0; ok; ++d) {
       const uint32_t ds = d % kDescs;
-      if (ended & (1u << (d % kSched))) continue;
       if (!(ok = mbar_wait_warp(&dfull[ds], (d / kDescs) & 1, a.status))) break;
       const ChunkDesc& cd = desc[ds];
       const int c = cd.chunk;
-      if (c < 0) {
-        ended |= 1u << (d % kSched);
-        continue;
-      }
-      const int bg = cd.bg, nsel = cd.n;
+      if (c < 0) break;
+      const int bg = cd.bg, p0 = cd.p0, p1 = cd.p1;
       const int64_t b = bg / a.Hkv, g = bg % a.Hkv;
       if (lane == 0) {
         const uint32_t qb = qi % kQBufs;
@@ -348,66 +527,81 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           for (int hh = 0; hh < G; ++hh)
             bulk_load(qbuf + qb * kQBuf + hh * D * 2, src + hh * a.qs1 * 2, D * 2, &qfull[qb]);
         }
+      }
+      ++qi;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      const int2* sel = a.w.sel + (int64_t)bg * a.sel_row;
+      for (int i0 = p0; i0 < p1 && ok; i0 += 32) {
+        const int nb = min(32, p1 - i0);
+        // the first 32 entries came with the descriptor; longer chunks load the rest here
         const int2* bsel = cd.sel;
-        if (a.page >= kTile) {
-          // a page is page/64 tiles; tiles past the context end are skipped
-          for (int k = 0; k < nsel && ok; ++k) {
-            const int2 e = bsel[k];
-            const int valid = (int)((unsigned)e.y >> 16);
-            const uint16_t mk = (uint16_t)(e.y & 0xffff);
-            for (int t0 = 0; t0 < valid; t0 += kTile, ++tile) {
+        if (i0 != p0) {
+          __syncwarp();
+          if (lane < nb) s_sel[lane] = __ldcg(sel + i0 + lane);
+          __syncwarp();
+          bsel = s_sel;
+        }
+        if (lane == 0) {
+          if (a.page >= kTile) {
+            // a page is page/64 tiles; tiles past the context end are skipped
+            for (int k = 0; k < nb && ok; ++k) {
+              const int2 e = bsel[k];
+              const int valid = (int)((unsigned)e.y >> 16);
+              const uint16_t mk = (uint16_t)(e.y & 0xffff);
+              for (int t0 = 0; t0 < valid; t0 += kTile, ++tile) {
+                const uint32_t st = tile % stages;
+                if (!(ok = mbar_wait(&empty[st], ((tile / stages) & 1) ^ 1, a.status))) break;
+                TileMeta& m = meta[st];
+                const bool last = i0 + k == p1 - 1 && t0 + kTile >= valid;
+                m.chunk = c;
+                m.flags = (i0 + k == p0 && t0 == 0 ? kFirst : 0) | (last ? kLast : 0);
+                m.vr = min(kTile, valid - t0);
+#pragma unroll
+                for (int q = 0; q < kCw; ++q) m.wmask[q] = mk;
+                mbar_arrive_expect_tx(&full[st], kStage);
+                unsigned char* sk = ring + st * kStage;
+#pragma unroll
+                for (int ch = 0; ch < KC; ++ch) {
+                  tma_load_4d(sk + ch * (kTile * 128), &a.tm_k, &full[st], ch * 64, t0, (int)g, e.x);
+                  tma_load_4d(sk + kHalf + ch * (kTile * 128), &a.tm_v, &full[st], ch * 64, t0,
+                              (int)g, e.x);
+                }
+              }
+            }
+          } else {
+            // ppt = 64/page pages per tile; chunk boundaries are multiples of ppt
+            const int ppt = a.ppt, page = (int)a.page;
+            for (int k = 0; k < nb && ok; k += ppt, ++tile) {
+              const int n = min(ppt, nb - k);
               const uint32_t st = tile % stages;
               if (!(ok = mbar_wait(&empty[st], ((tile / stages) & 1) ^ 1, a.status))) break;
               TileMeta& m = meta[st];
-              const bool last = k == nsel - 1 && t0 + kTile >= valid;
+              const bool last = i0 + k + n == p1;
               m.chunk = c;
-              m.flags = (k == 0 && t0 == 0 ? kFirst : 0) | (last ? kLast : 0);
-              m.vr = min(kTile, valid - t0);
+              m.flags = (i0 + k == p0 ? kFirst : 0) | (last ? kLast : 0);
+              m.vr = (n - 1) * page + (int)((unsigned)bsel[k + n - 1].y >> 16);
 #pragma unroll
-              for (int q = 0; q < kCw; ++q) m.wmask[q] = mk;
-              mbar_arrive_expect_tx(&full[st], kStage);
-              unsigned char* sk = ring + st * kStage;
-#pragma unroll
-              for (int ch = 0; ch < KC; ++ch) {
-                tma_load_4d(sk + ch * (kTile * 128), &a.tm_k, &full[st], ch * 64, t0, (int)g, e.x);
-                tma_load_4d(sk + kHalf + ch * (kTile * 128), &a.tm_v, &full[st], ch * 64, t0,
-                            (int)g, e.x);
+              for (int q = 0; q < kCw; ++q) {
+                const int j = q * 16 / page;
+                m.wmask[q] = j < n ? (uint16_t)(bsel[k + j].y & 0xffff) : (uint16_t)0;
               }
-            }
-          }
-        } else {
-          // ppt = 64/page selected pages per tile
-          const int ppt = a.ppt, page = (int)a.page;
-          for (int k = 0; k < nsel && ok; k += ppt, ++tile) {
-            const int n = min(ppt, nsel - k);
-            const uint32_t st = tile % stages;
-            if (!(ok = mbar_wait(&empty[st], ((tile / stages) & 1) ^ 1, a.status))) break;
-            TileMeta& m = meta[st];
-            m.chunk = c;
-            m.flags = (k == 0 ? kFirst : 0) | (k + n == nsel ? kLast : 0);
-            m.vr = (n - 1) * page + (int)((unsigned)bsel[k + n - 1].y >> 16);
+              mbar_arrive_expect_tx(&full[st], (uint32_t)(n * page * D * 2 * 2));
+              unsigned char* sk = ring + st * kStage;
+              for (int j = 0; j < n; ++j) {
+                const int phys = bsel[k + j].x;
 #pragma unroll
-            for (int q = 0; q < kCw; ++q) {
-              const int j = q * 16 / page;
-              m.wmask[q] = j < n ? (uint16_t)(bsel[k + j].y & 0xffff) : (uint16_t)0;
-            }
-            mbar_arrive_expect_tx(&full[st], (uint32_t)(n * page * D * 2 * 2));
-            unsigned char* sk = ring + st * kStage;
-            for (int j = 0; j < n; ++j) {
-              const int phys = bsel[k + j].x;
-#pragma unroll
-              for (int ch = 0; ch < KC; ++ch) {
-                tma_load_4d(sk + ch * (kTile * 128) + j * page * 128, &a.tm_k, &full[st], ch * 64, 0,
-                            (int)g, phys);
-                tma_load_4d(sk + kHalf + ch * (kTile * 128) + j * page * 128, &a.tm_v, &full[st],
-                            ch * 64, 0, (int)g, phys);
+                for (int ch = 0; ch < KC; ++ch) {
+                  tma_load_4d(sk + ch * (kTile * 128) + j * page * 128, &a.tm_k, &full[st], ch * 64, 0,
+                              (int)g, phys);
+                  tma_load_4d(sk + kHalf + ch * (kTile * 128) + j * page * 128, &a.tm_v, &full[st],
+                              ch * 64, 0, (int)g, phys);
+                }
               }
             }
           }
         }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
       }
-      ++qi;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
       __syncwarp();
       if (lane == 0) mbar_arrive(&dempty[ds]);  // the descriptor's entries are no longer read
     }
@@ -584,108 +778,37 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfull[eb]);
     }
-  } else if (warp >= kSchedWarp) {
-    // ---------------- schedulers: take items and select their pages ----------------
-    // kSched warps work on different items at once; scheduler w fills descriptors
-    // w, w + kSched, ... (each up to two items ahead of the producer).  The first items
-    // are static (w * gridDim.x + CTA); the queue counter hands out the rest.  Per item:
-    // its {request, part, n_logical, context} entry, then together the query's routing words
-    // of the group's heads and the block-table entries of the part's pages (a lane per page,
-    // two rounds of 32), then each page's routing words of the group's heads; the pages that
-    // some head attends are compacted in logical order into the descriptor.
-    const int sw = warp - kSchedWarp;
-    int32_t* s_qr = s_qr_all + sw * kMaxG * kMaxSelLevels;
-    const int n_rp = __ldcg(&a.w.hdr->n_rp);
-    const int64_t n_items = (int64_t)n_rp * a.Hkv;
-    const int PP = a.w.PP, NP = a.w.NP, r = a.r, GR = G * r;
-    constexpr int RSP = D + 4;
-    bool first = true;
-    for (uint32_t k = 0;; ++k) {
-      const uint32_t d = sw + k * kSched, ds = d % kDescs;
+  } else if (warp == kSchedWarp) {
+    // ---------------- scheduler: reserve the next chunk and fetch its entries ----------------
+    // Up to kDescs - 1 descriptors ahead of the producer, so that runs of one-page chunks do
+    // not wait on the queue's atomic -> table -> list chain.  CTA x takes chunk x first; the
+    // queue counter hands out the rest from chunk gridDim.x on.
+    const int n_chunks = __ldcg(&a.w.hdr->n_chunks);
+    for (uint32_t d = 0;; ++d) {
+      const uint32_t ds = d % kDescs;
       if (!mbar_wait_warp(&dempty[ds], ((d / kDescs) & 1) ^ 1, a.status)) break;
+      int c = 0;
+      if (lane == 0) c = d == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(&a.w.hdr->next, 1);
+      c = __shfl_sync(0xffffffffu, c, 0);
       ChunkDesc& cd = desc[ds];
-      int slot = -1, bg = 0, nsel = 0;
-      for (;;) {
-        int64_t idx = 0;
-        if (lane == 0)
-          idx = first ? (int64_t)sw * gridDim.x + blockIdx.x
-                      : (int64_t)kSched * gridDim.x + atomicAdd(&a.w.hdr->next, 1);
-        first = false;
-        idx = __shfl_sync(0xffffffffu, idx, 0);
-        if (idx >= n_items) break;
-        const int4 rp = __ldcg(a.w.rp + idx / a.Hkv);
-        const int64_t b = rp.x, g = idx % a.Hkv, nlog = rp.z, cx = rp.w;
-        const int part = rp.y;
-        bg = (int)(b * a.Hkv + g);
-        const int64_t lo = (int64_t)part * PP, hi = min(nlog, lo + PP);
-        // query routing words and block-table entries, loads in flight together
-        int32_t qv[kMaxG * kMaxSelLevels / 32];
-        if (a.qrouter_dtype == SA_I64) {
-#pragma unroll
-          for (int j = 0; j < kMaxG * kMaxSelLevels / 32; ++j) {
-            const int i = min(lane + 32 * j, GR - 1);
-            qv[j] = GR > 0 ? (int32_t)__ldg(static_cast<const int64_t*>(a.qrouter) + b * a.qrs0 +
-                                            (g * G + i / r) * a.qrs1 + (i % r) * a.qrs2)
-                           : 0;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < kMaxG * kMaxSelLevels / 32; ++j) {
-            const int i = min(lane + 32 * j, GR - 1);
-            qv[j] = GR > 0 ? __ldg(static_cast<const int32_t*>(a.qrouter) + b * a.qrs0 +
-                                   (g * G + i / r) * a.qrs1 + (i % r) * a.qrs2)
-                           : 0;
-          }
+      if (c >= n_chunks) {
+        if (lane == 0) {
+          cd.chunk = -1;
+          mbar_arrive(&dfull[ds]);
         }
-        const int64_t pg0 = lo + lane, pg1 = lo + 32 + lane;
-        const bool in0 = pg0 < hi, in1 = pg1 < hi;
-        const int ph0 = in0 ? a.bt[b * a.bts0 + pg0 * a.bts1] : 0;
-        const int ph1 = in1 ? a.bt[b * a.bts0 + pg1 * a.bts1] : 0;
-#pragma unroll
-        for (int j = 0; j < kMaxG * kMaxSelLevels / 32; ++j)
-          if (lane + 32 * j < GR) s_qr[lane + 32 * j] = qv[j];
-        __syncwarp();
-        // both pages' routing words of the group's heads, 16 + 16 loads in flight at a time
-        const int64_t base0 = (int64_t)ph0 * a.rs0 + g * G * a.rs1;
-        const int64_t base1 = (int64_t)ph1 * a.rs0 + g * G * a.rs1;
-        unsigned miss0 = 0, miss1 = 0;
-        if (a.router_dtype == SA_I64)
-          route_misses(static_cast<const int64_t*>(a.router), base0, base1, in0, in1, GR, r, a.rs1,
-                       a.rs2, s_qr, miss0, miss1);
-        else
-          route_misses(static_cast<const int32_t*>(a.router), base0, base1, in0, in1, GR, r, a.rs1,
-                       a.rs2, s_qr, miss0, miss1);
-        const unsigned all = (1u << G) - 1u;
-        nsel = 0;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int64_t pg = half ? pg1 : pg0;
-          const bool in = half ? in1 : in0;
-          const bool forced = (a.sink && pg == 0) || (a.local_blocks > 0 && pg >= nlog - a.local_blocks);
-          const unsigned mask = !in ? 0u : forced ? all : (~(half ? miss1 : miss0) & all);
-          const unsigned bal = __ballot_sync(0xffffffffu, mask != 0u);
-          if (mask) {
-            const int valid = (int)min(a.page, cx - pg * a.page);
-            cd.sel[nsel + __popc(bal & ((1u << lane) - 1u))] =
-                make_int2(half ? ph1 : ph0, (int)(mask | ((unsigned)valid << 16)));
-          }
-          nsel += __popc(bal);
-        }
-        __syncwarp();  // s_qr is rewritten for the next item
-        slot = bg * NP + part;
-        if (nsel > 0) break;
-        // nothing attended in this part: its partial is marked empty, no streaming
-        if (lane < G) a.w.part[((int64_t)slot * G + lane) * RSP] = -INFINITY;
-        slot = -1;
+        break;
       }
+      const int4 ent = __ldcg(a.w.table + c);
+      const int bg = ent.x, p0 = ent.y & 0xffff, p1 = (int)((unsigned)ent.y >> 16);
+      if (lane < min(32, p1 - p0)) cd.sel[lane] = __ldcg(a.w.sel + (int64_t)bg * a.sel_row + p0 + lane);
       if (lane == 0) {
-        cd.chunk = slot;
+        cd.chunk = c;
         cd.bg = bg;
-        cd.n = nsel;
+        cd.p0 = p0;
+        cd.p1 = p1;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&dfull[ds]);
-      if (slot < 0) break;
     }
   } else {
     // ---------------- epilogue warp: chunk partials ----------------
@@ -726,48 +849,41 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------
-// 3. per-unit merge of the part partials (a programmatic dependent of the stream kernel)
+// 4. per-unit merge of the chunk partials (a programmatic dependent of the stream kernel)
 // ---------------------------------------------------------------------------------------
-// One CTA per unit, one thread per float4 output column of the unit's G heads; the unit's
-// parts (those holding pages: ceil(n_logical / PP)) are merged online with eight parts'
-// loads in flight.  Parts (or heads) that attended nothing have m = -inf and are skipped
-// (their other fields are not written); a unit with nothing attended gets zeros.
+// One CTA per unit, one thread per float4 output column of the unit's G heads; the chunks
+// are merged online with eight chunks' loads in flight.
 template <typename T, int D>
-__global__ void __launch_bounds__(kMaxG * D / 4) decode_unit_combine_kernel(const FastWs w,
-                                                                          const int32_t* ctx,
-                                                                          int64_t page, int64_t maxL,
-                                                                          void* out_, int64_t os0,
-                                                                          int64_t os1, int64_t Hkv,
-                                                                          int G) {
+__global__ void __launch_bounds__(kMaxG * D / 4) decode_unit_combine_kernel(const FastWs w, void* out_,
+                                                                          int64_t os0, int64_t os1,
+                                                                          int64_t Hkv, int G) {
   constexpr int RS = D + 4;
   pdl_wait();
   const int64_t bg = blockIdx.x;
+  const int2 ui = w.uinfo[bg];
   const int i = threadIdx.x;
-  if (i >= G * (D / 4)) return;
-  const int64_t cx = ctx[bg / Hkv];
-  const int64_t nlog = cx > 0 ? min((cx + page - 1) / page, maxL) : 0;
-  const int nparts = (int)((nlog + w.PP - 1) / w.PP);
+  if (ui.y == 0 || i >= G * (D / 4)) return;  // a unit without pages was zeroed at selection
   const int hh = i / (D / 4), d4 = i % (D / 4);
-  const float* ph = w.part + (int64_t)bg * w.NP * G * RS + hh * RS;
+  const float* ph = w.part + (int64_t)ui.x * G * RS + hh * RS;
   const int64_t CS = (int64_t)G * RS;
   float M = -INFINITY, L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   constexpr int NU = 8;
-  for (int k0 = 0; k0 < nparts; k0 += NU) {
+  for (int k0 = 0; k0 < ui.y; k0 += NU) {
     float2 ml[NU];
     float4 x[NU];
 #pragma unroll
     for (int u = 0; u < NU; ++u) {
-      const int k = min(k0 + u, nparts - 1);
+      const int k = min(k0 + u, ui.y - 1);
       ml[u] = __ldcg(reinterpret_cast<const float2*>(ph + k * CS));
       x[u] = __ldcg(reinterpret_cast<const float4*>(ph + k * CS + 4 + 4 * d4));
     }
 #pragma unroll
     for (int u = 0; u < NU; ++u) {
-      if (k0 + u >= nparts) break;
-      if (ml[u].x == -INFINITY) continue;  // nothing attended by this head in this part
+      if (k0 + u >= ui.y) break;
       const float mn = fmaxf(M, ml[u].x);
-      const float so = fast_exp2(M - mn), sn = fast_exp2(ml[u].x - mn);
+      const float ref = mn == -INFINITY ? 0.f : mn;
+      const float so = fast_exp2(M - ref), sn = fast_exp2(ml[u].x - ref);
       acc.x = acc.x * so + x[u].x * sn;
       acc.y = acc.y * so + x[u].y * sn;
       acc.z = acc.z * so + x[u].z * sn;
@@ -790,10 +906,9 @@ int launch_stream(StreamArgs& a, int grid, cudaStream_t stream) {
   constexpr size_t kStage = 2 * (size_t)kTile * D * 2;
   // alignment slack, query buffers, 2 merge buffers, then Q / merge barriers, hand-off
   // records, the producer's page batch and the scheduler's descriptors with barriers
-  static_assert((2 * kQBufs + 4) * 8 + 16 + kDescs * (sizeof(ChunkDesc) + 16) +
-                    kSched * kMaxG * kMaxSelLevels * 4 <= 9216,
-                "decode: barrier, descriptor and query-route area");
-  const size_t fixed = 1024 + kQBufs * (size_t)a.G * D * 2 + 2 * (size_t)kCw * a.G * (D + 4) * 4 + 9216;
+  static_assert((2 * kQBufs + 4) * 8 + 16 + 32 * 8 + kDescs * (sizeof(ChunkDesc) + 16) <= 2048,
+                "decode: barrier and descriptor area");
+  const size_t fixed = 1024 + kQBufs * (size_t)a.G * D * 2 + 2 * (size_t)kCw * a.G * (D + 4) * 4 + 2048;
   const size_t per_stage = kStage + sizeof(TileMeta) + 16;
   const int stages = (int)std::min<size_t>(kMaxStages, (226 * 1024 - fixed) / per_stage);
   if (stages < 2) return fail(SA_EUNSUPPORTED, "decode: shared memory too small for the ring");
@@ -820,22 +935,18 @@ bool decode_fast_eligible(const DecodeParams& p, int dtype) {
 
 int64_t decode_fast_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t maxL) {
   if (B <= 0 || H <= 0 || Hkv <= 0 || D <= 0) return 0;
-  return (int64_t)carve(nullptr, B, Hkv, maxL, H / Hkv, D,
-                        pages_per_item(B, Hkv, maxL, device_sm_count()), nullptr);
+  return (int64_t)carve(nullptr, B, Hkv, maxL, H / Hkv, D, nullptr);
 }
 
 int launch_decode_fast(const DecodeParams& p, int dtype, void* workspace, int64_t workspace_bytes,
                        cudaStream_t stream) {
   const int64_t BG = p.B * p.Hkv;
-  const int sms = device_sm_count();
   FastWs w;
-  const size_t need = carve(workspace, p.B, p.Hkv, p.maxL, p.G, p.D,
-                            pages_per_item(p.B, p.Hkv, p.maxL, sms), &w);
+  const size_t need = carve(workspace, p.B, p.Hkv, p.maxL, p.G, p.D, &w);
   if ((int64_t)need > workspace_bytes || !workspace)
     return fail(SA_EWORKSPACE, "decode: workspace too small (" + std::to_string(workspace_bytes) +
                                    " < " + std::to_string(need) + ")");
   if (p.B > 65535) return fail(SA_EUNSUPPORTED, "decode: more than 65535 requests");
-  if (BG * w.NP > INT32_MAX) return fail(SA_EUNSUPPORTED, "decode: too many work items");
   StreamArgs a{};
   a.status = device_status_ptr();
   if (!a.status) return fail(SA_ELAUNCH, std::string("decode: ") + sa_last_error());
@@ -844,8 +955,23 @@ int launch_decode_fast(const DecodeParams& p, int dtype, void* workspace, int64_
   if (!rc) rc = make_tmap_4d(&a.tm_v, p.vc, dtype, p.num_pages, p.Hkv, p.page, p.D, p.vs, 64, box_n);
   if (rc) return fail(SA_ELAUNCH, std::string("decode: tensor map: ") + sa_last_error());
 
-  decode_init_kernel<<<1, kInitThreads, 0, stream>>>(w, p.ctx, p.B, p.page, p.maxL);
+  decode_init_kernel<<<1, 1, 0, stream>>>(w.hdr);
   rc = check_launch("decode_init_kernel");
+  if (rc) return rc;
+  const int ppt = p.page >= kTile ? 1 : (int)(kTile / p.page);
+  {
+    // pages x compared words per lane and step: as many loads in flight as fit in registers
+    const int64_t HR = p.H * p.r;
+    const dim3 sg((unsigned)w.P, (unsigned)p.B), sb(kSelThreads);
+    const char* sn = "decode_select_kernel";
+    const bool i64 = p.router_dtype == SA_I64;
+    if (HR <= 128)
+      rc = i64 ? launch_dependent(decode_select_kernel<int64_t, 4, 4>, sg, sb, 0, stream, sn, p, w, ppt)
+               : launch_dependent(decode_select_kernel<int32_t, 8, 4>, sg, sb, 0, stream, sn, p, w, ppt);
+    else
+      rc = i64 ? launch_dependent(decode_select_kernel<int64_t, 4, 4>, sg, sb, 0, stream, sn, p, w, ppt)
+               : launch_dependent(decode_select_kernel<int32_t, 4, 8>, sg, sb, 0, stream, sn, p, w, ppt);
+  }
   if (rc) return rc;
 
   a.q = p.q;
@@ -855,30 +981,13 @@ int launch_decode_fast(const DecodeParams& p, int dtype, void* workspace, int64_
   a.os0 = p.os[0];
   a.os1 = p.os[1];
   a.Hkv = p.Hkv;
+  a.sel_row = (int64_t)w.P * w.seg;
   a.page = p.page;
   a.G = (int)p.G;
-  a.ppt = p.page >= kTile ? 1 : (int)(kTile / p.page);
+  a.ppt = ppt;
   a.scale2 = (1.0f / sqrtf((float)p.D)) * kLog2e;
   a.w = w;
-  a.bt = p.bt;
-  a.bts0 = p.bts[0];
-  a.bts1 = p.bts[1];
-  a.ctx = p.ctx;
-  a.router = p.router;
-  a.router_dtype = p.router_dtype;
-  a.rs0 = p.rs[0];
-  a.rs1 = p.rs[1];
-  a.rs2 = p.rs[2];
-  a.qrouter = p.qrouter;
-  a.qrouter_dtype = p.qrouter_dtype;
-  a.qrs0 = p.qrs[0];
-  a.qrs1 = p.qrs[1];
-  a.qrs2 = p.qrs[2];
-  a.maxL = p.maxL;
-  a.local_blocks = p.local_blocks;
-  a.r = (int)p.r;
-  a.sink = p.sink;
-  const int grid = (int)std::min<int64_t>(sms, BG * w.NP);
+  const int grid = (int)std::min<int64_t>(device_sm_count(), max_chunks(BG, p.maxL, w.P));
   const bool bf = dtype == SA_BF16;
   if (p.D == 64)
     rc = bf ? launch_stream<64, true>(a, grid, stream) : launch_stream<64, false>(a, grid, stream);
@@ -889,13 +998,13 @@ int launch_decode_fast(const DecodeParams& p, int dtype, void* workspace, int64_
   const char* cn = "decode_unit_combine_kernel";
   if (p.D == 64)
     return bf ? launch_dependent(decode_unit_combine_kernel<__nv_bfloat16, 64>, cg, cb, 0, stream, cn, w,
-                                 p.ctx, p.page, p.maxL, p.out, p.os[0], p.os[1], p.Hkv, (int)p.G)
-              : launch_dependent(decode_unit_combine_kernel<__half, 64>, cg, cb, 0, stream, cn, w, p.ctx,
-                                 p.page, p.maxL, p.out, p.os[0], p.os[1], p.Hkv, (int)p.G);
+                                 p.out, p.os[0], p.os[1], p.Hkv, (int)p.G)
+              : launch_dependent(decode_unit_combine_kernel<__half, 64>, cg, cb, 0, stream, cn, w, p.out,
+                                 p.os[0], p.os[1], p.Hkv, (int)p.G);
   return bf ? launch_dependent(decode_unit_combine_kernel<__nv_bfloat16, 128>, cg, cb, 0, stream, cn, w,
-                               p.ctx, p.page, p.maxL, p.out, p.os[0], p.os[1], p.Hkv, (int)p.G)
-            : launch_dependent(decode_unit_combine_kernel<__half, 128>, cg, cb, 0, stream, cn, w, p.ctx,
-                               p.page, p.maxL, p.out, p.os[0], p.os[1], p.Hkv, (int)p.G);
+                               p.out, p.os[0], p.os[1], p.Hkv, (int)p.G)
+            : launch_dependent(decode_unit_combine_kernel<__half, 128>, cg, cb, 0, stream, cn, w, p.out,
+                               p.os[0], p.os[1], p.Hkv, (int)p.G);
 }
 
 }  // namespace sa

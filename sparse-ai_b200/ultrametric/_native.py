@@ -36,6 +36,8 @@ _SIGNATURES = {
     "sa_paged_kv_append": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _vp, _p64, _vp, _p64, _vp,
                                    _p64, _i64, _vp, _vp, _p64, _vp, _p64, _vp, _i32, _p64, _i64,
                                    _i64, _vp, _i32, _p64, _vp]),
+    "sa_ternary_quantize_pack": (_i32, [_i32, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "sa_ternary_dequantize": (_i32, [_i32, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
     "sa_build_block_lists_from_assignments": (_i32, [_vp, _i32, _p64, _i64, _i64, _i64, _i64,
                                                       _i64, _i64, _i64, _vp, _i64, _i32, _i32,
                                                       _i64, _vp, _vp, _i64, _vp, _vp]),

@@ -73,7 +73,8 @@ def test_builder_and_decode_kernels_run():
     ri = torch.zeros(8, H, 3, dtype=torch.int32, device=DEV)
     qri = torch.zeros(B, H, 3, dtype=torch.int32, device=DEV)
     names = kernel_names(lambda: ultrametric_decode(q, kc, kc, bt, ctx, ri, qri, 2))
-    for k in ("decode_init_kernel", "decode_stream_kernel", "decode_unit_combine_kernel"):
+    for k in ("decode_init_kernel", "decode_select_kernel", "decode_stream_kernel",
+              "decode_unit_combine_kernel"):
         assert any(k in n for n in names), names
     assert not any("decode_split_kernel" in n for n in names), names
     assert _native.read_device_status() == 0
