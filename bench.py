@@ -966,8 +966,8 @@ def run_c4(dev, rank, world, warmup, flush, barrier=None, cpu=False):
                "fused_vote_and_lists": round(ms_lists / L, 4),
                "torch_vote_glue_plus_builder": round(ms_glue / L, 4),
                "fused_vote_and_lists_graph": graph_ms(lambda: [lists_of(a) for *_, a in layers]),
-               "torch_vote_glue_plus_builder_graph": graph_ms(glue),
-               "note": "eager calls are host-bound at this size; the graph replays give GPU time"},
+               "note": "eager calls are host-bound at this size; the graph replay gives the fused "
+                       "path's GPU time (the torch glue copies host data and cannot be captured)"},
            "timed": "per layer: router outputs -> vote + lists (one C-ABI call) -> forward; "
                     "router projection not included"}
     if cpu and rank == 0 and world == 1:

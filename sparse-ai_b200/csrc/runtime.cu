@@ -61,6 +61,13 @@ unsigned* device_status_ptr() {
 
 int check_stream_device(void* stream, const char* what) {
   if (!stream) return SA_OK;  // the legacy default stream belongs to the current device
+  // a stream being captured into a graph is not queried (the capture holds the device)
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SA_EINVAL, std::string(what) + ": not a valid CUDA stream");
+  }
+  if (cs != cudaStreamCaptureStatusNone) return SA_OK;
   int dev = 0, sdev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
