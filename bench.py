@@ -742,7 +742,7 @@ def make_c5(dev, rank=0, world=1):
     Z, H, Hkv, N, D, RB = (C5[k] for k in ("Z", "H", "Hkv", "N", "D", "RB"))
     router = tree_router(Z, H, N // RB, C5["TD"])
     bl = build_block_lists(router.to(dev), C5["t"], is_causal=True, sink_block=True, arity=2)
-    Nl = N // world
+    Nl = N // world  # this rank's rows: with several ranks, the zigzag pair of chunks
     g = torch.Generator(device=dev).manual_seed(40 + rank)
     q = torch.randn(Z, H, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
     k = torch.randn(Z, Hkv, Nl, D, generator=g, device=dev, dtype=torch.bfloat16)
@@ -784,14 +784,16 @@ def run_c5(dev, rank, world, steps, warmup, flush, barrier=None, cpu=False):
     q, k, v, bl, Nl = c5["q"], c5["k"], c5["v"], c5["bl"], c5["rows_per_rank"]
     kept = int(bl.counts.sum())
     scale = 1.0 / math.sqrt(D)
-    # the ring's schedule depends only on the lists: planned once, like the lists themselves
-    plan = RingPlan(bl, world, rank, Nl, RB, True) if world > 1 else None
+    # the ring's schedule depends only on the lists: planned once, like the lists themselves.
+    # Zigzag layout: rank r holds chunks r and 2P - 1 - r, so the causal work is balanced.
+    plan = RingPlan(bl, world, rank, Nl, RB, True, layout="zigzag") if world > 1 else None
 
     def one():
         if world == 1:
             _fwd(q, k, v, bl.lists, bl.counts, RB, True, scale, True, None)
         else:
-            ring_block_list_attention(q, k, v, bl, route_block=RB, is_causal=True, plan=plan)
+            ring_block_list_attention(q, k, v, bl, route_block=RB, is_causal=True, plan=plan,
+                                      layout="zigzag")
 
     for _ in range(warmup):
         one()
@@ -814,7 +816,8 @@ def run_c5(dev, rank, world, steps, warmup, flush, barrier=None, cpu=False):
            "kept_tflops": round(flops / (ms * 1e-3) / 1e12, 2)}
     if world > 1:
         sent = sum(int(g.numel()) for _, g, _, _ in plan.exchange if g is not None)
-        res["ring"] = {"ranks": world, "rows_per_rank": Nl, "hops_computed": len(plan.hops),
+        res["ring"] = {"ranks": world, "rows_per_rank": Nl, "layout": "zigzag (chunks r, 2P-1-r)",
+                       "hops_computed": len(plan.hops),
                        "kv_rows_sent_by_rank0": sent,
                        "kv_bytes_sent_by_rank0": 2 * Z * Hkv * sent * D * 2,
                        "dense_ring_bytes_per_hop": 2 * Z * Hkv * Nl * D * 2,

@@ -14,6 +14,13 @@ Causality needs no kernel change: the diagonal chunk (c == r) runs causally, ear
 chunks lie entirely before this rank's queries, and later chunks hold no kept pair of a
 causal list, so those hops are skipped.
 
+With contiguous chunks a causal ring is unbalanced: rank r computes r + 1 hops and the last
+rank carries the most work.  ``layout="zigzag"`` splits the sequence into 2P chunks and gives
+rank r chunks r and 2P - 1 - r (one early, one late), stored one after the other in its local
+q / k / v.  Every rank then holds the same causal work.  In local order the two chunks keep
+their global order, so the diagonal hop still runs causally on local indices, and every other
+hop is fully visible where its lists have entries.
+
 ``attn`` and ``merge`` can be replaced (same signatures) so that the schedule is testable
 on CPU ranks; by default they are this package's CUDA entry points.
 """
@@ -45,6 +52,41 @@ def chunk_lists(lists: torch.Tensor, counts: torch.Tensor, q_lo: int, q_hi: int,
     sub = torch.gather(L, -1, idx) - k_lo
     sub = torch.where(slot < n[..., None], sub, torch.zeros_like(sub))
     return sub.to(torch.int32).contiguous(), n.to(torch.int32).contiguous()
+
+
+def chunk_lists_multi(lists: torch.Tensor, counts: torch.Tensor, q_ranges, k_ranges
+                      ) -> tuple[torch.Tensor, torch.Tensor]:
+    """The lists of the query blocks in ``q_ranges`` (a list of [lo, hi) block ranges, taken
+    in order as the local query blocks) restricted to the key blocks in ``k_ranges`` and
+    re-based to the local key order (the ranges one after the other).  The ranges are
+    ascending and disjoint, so the mapping keeps each row ascending."""
+    L = torch.cat([lists[:, :, lo:hi] for lo, hi in q_ranges], dim=2).long()
+    cnt = torch.cat([counts[:, :, lo:hi] for lo, hi in q_ranges], dim=2).long()
+    mc = max(L.shape[-1], 1)
+    slot = torch.arange(L.shape[-1], device=L.device)
+    valid = slot < cnt[..., None]
+    local = torch.full_like(L, -1)
+    base = 0
+    for lo, hi in k_ranges:
+        inr = valid & (L >= lo) & (L < hi)
+        local = torch.where(inr, L - lo + base, local)
+        base += hi - lo
+    keep = local >= 0
+    n = keep.sum(-1)
+    pos = torch.cumsum(keep.long(), -1) - 1
+    sub = torch.zeros_like(L)
+    sub.scatter_(-1, torch.where(keep, pos, torch.full_like(pos, mc - 1)).clamp_min(0),
+                 torch.where(keep, local, torch.zeros_like(local)))
+    # slots past n: zero (a masked scatter may have written the last slot)
+    sub = torch.where(slot < n[..., None], sub, torch.zeros_like(sub))
+    return sub.to(torch.int32).contiguous(), n.to(torch.int32).contiguous()
+
+
+def rank_chunks(rank: int, world: int, layout: str) -> list[int]:
+    """Chunk ids (in units of the layout's chunk size) that ``rank`` holds, in local order."""
+    if layout == "zigzag":
+        return [rank, 2 * world - 1 - rank]
+    return [rank]
 
 
 def _attn_cuda(q, k, v, lists, counts, route_block, is_causal, scale):
@@ -82,12 +124,15 @@ def ring_hops(rank: int, world: int, is_causal: bool) -> list[tuple[int, int, bo
     return hops
 
 
-def reference_masks(lists: torch.Tensor, counts: torch.Tensor, nbl: int, world: int) -> torch.Tensor:
-    """(world, NB) bool: ref[r, kb] = some query block of rank r lists key block kb."""
+def reference_masks(lists: torch.Tensor, counts: torch.Tensor, owner, world: int) -> torch.Tensor:
+    """(world, NB) bool: ref[r, kb] = some query block held by rank r lists key block kb.
+    ``owner``: (NB,) rank of each query block, or an int (blocks per rank, contiguous)."""
     Z, H, NB, mc = lists.shape
     slot = torch.arange(mc, device=lists.device)
     valid = slot < counts.long()[..., None]
-    owner = (torch.arange(NB, device=lists.device) // nbl).view(1, 1, NB, 1)
+    if isinstance(owner, int):
+        owner = torch.arange(NB, device=lists.device) // owner
+    owner = owner.to(lists.device).view(1, 1, NB, 1)
     flat = torch.where(valid, owner * (NB + 1) + lists.long(), torch.full_like(lists, NB, dtype=torch.long))
     ref = torch.zeros(world * (NB + 1), dtype=torch.bool, device=lists.device)
     ref[flat.reshape(-1)] = True
@@ -98,37 +143,67 @@ class RingPlan:
     """One rank's ring schedule for one set of block lists, built once (two small host
     reads) and reused by every call with those lists:
 
-    * ``hops``: (chunk, causal?, chunk-local lists, counts) for the chunks this rank attends;
-    * ``exchange``: per hop j > 0, the rows of this rank's chunk that rank r + j references
-      (sent) and the rows of chunk r - j that this rank references (received)."""
+    * ``hops``: (rank whose K/V it reads, causal?, local lists, counts) for the hops this rank
+      computes (lists in this rank's local query order against that rank's local key order);
+    * ``exchange``: per hop j > 0, the local rows of this rank's K/V that rank r + j
+      references (sent) and the local rows of rank r - j's K/V that this rank references
+      (received).
+
+    ``layout``: "contiguous" (rank r holds rows [r N/P, (r+1) N/P)) or "zigzag" (rank r holds
+    chunks r and 2P - 1 - r of N / 2P rows, one after the other)."""
 
     def __init__(self, block_lists: BlockLists, world: int, rank: int, rows_per_rank: int,
-                 route_block: int, is_causal: bool):
-        if rows_per_rank % route_block:
-            raise ValueError(f"the per-rank chunk ({rows_per_rank} rows) must be a multiple of route_block")
-        nbl = rows_per_rank // route_block
+                 route_block: int, is_causal: bool, layout: str = "contiguous"):
+        if layout not in ("contiguous", "zigzag"):
+            raise ValueError(f"unknown ring layout {layout!r}")
+        nparts = len(rank_chunks(rank, world, layout))
+        if rows_per_rank % (route_block * nparts):
+            raise ValueError(f"the per-rank rows ({rows_per_rank}) must split into {nparts} chunk(s) "
+                             f"that are multiples of route_block")
+        nbc = rows_per_rank // route_block // nparts  # blocks per chunk
         lists, counts = block_lists.lists, block_lists.counts
-        if lists.shape[2] != nbl * world:
+        if lists.shape[2] != nbc * nparts * world:
             raise ValueError(f"block_lists cover {lists.shape[2]} query blocks, "
-                             f"expected {nbl * world} (= N / route_block)")
+                             f"expected {nbc * nparts * world} (= N / route_block)")
         mc = int(counts.max()) if counts.numel() else 0  # sync-free lists are NB slots wide
         lists = lists[..., :max(mc, 1)]
         self.world, self.rank, self.rows, self.route_block = world, rank, rows_per_rank, route_block
-        self.is_causal = is_causal
+        self.is_causal, self.layout = is_causal, layout
+        ranges = lambda r: [(c * nbc, (c + 1) * nbc) for c in rank_chunks(r, world, layout)]
         self.hops = []
-        for _, c, causal in ring_hops(rank, world, is_causal):
-            sub, cnt = chunk_lists(lists, counts, rank * nbl, (rank + 1) * nbl, c * nbl, (c + 1) * nbl)
-            self.hops.append((c, causal, sub, cnt))
+        for j in range(world):
+            c = (rank - j) % world
+            if layout == "contiguous":
+                if is_causal and c > rank:
+                    continue  # a causal list holds no pair with a later chunk
+                sub, cnt = chunk_lists(lists, counts, rank * nbc, (rank + 1) * nbc, c * nbc, (c + 1) * nbc)
+            else:
+                sub, cnt = chunk_lists_multi(lists, counts, ranges(rank), ranges(c))
+                if c != rank and int(cnt.sum()) == 0:
+                    continue
+            # only the diagonal hop needs the token-level causal mask: in local order the two
+            # zigzag chunks keep their global order, and other hops' listed pairs are visible
+            self.hops.append((c, is_causal and c == rank, sub, cnt))
         self.exchange = []
         if world > 1:
-            ref = reference_masks(lists, counts, nbl, world).cpu()
+            # owner of each global query block, its local key position on the owning rank
+            NB = lists.shape[2]
+            owner = torch.empty(NB, dtype=torch.long)
+            lpos = torch.empty(NB, dtype=torch.long)
+            for r in range(world):
+                for i, (lo, hi) in enumerate(ranges(r)):
+                    owner[lo:hi] = r
+                    lpos[lo:hi] = torch.arange(hi - lo) + i * nbc
+            ref = reference_masks(lists, counts, owner.to(lists.device), world).cpu()
             dev = lists.device
             rows = torch.arange(route_block)
             to_rows = lambda b: (b.view(-1, 1) * route_block + rows).reshape(-1).to(dev)
             for j in range(1, world):
                 dst, src = (rank + j) % world, (rank - j) % world
-                give = ref[dst, rank * nbl:(rank + 1) * nbl].nonzero().view(-1)
-                need = ref[rank, src * nbl:(src + 1) * nbl].nonzero().view(-1)
+                mine = (owner == rank).nonzero().view(-1)    # global blocks this rank holds
+                theirs = (owner == src).nonzero().view(-1)
+                give = lpos[mine[ref[dst, mine]]]
+                need = lpos[theirs[ref[rank, theirs]]]
                 self.exchange.append((dst, to_rows(give) if give.numel() else None,
                                       src, to_rows(need) if need.numel() else None))
 
@@ -162,13 +237,16 @@ def ring_block_list_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                               group=None, plan: Optional[RingPlan] = None,
                               attn: Optional[Callable] = None,
                               merge_factory: Optional[Callable] = None,
+                              layout: str = "contiguous",
                               ) -> tuple[torch.Tensor, torch.Tensor]:
     """Block-list attention forward over a sequence split across the ranks of ``group``.
 
-    q: (Z, H, N/P, D) this rank's query rows (chunk ``rank``); k, v: (Z, Hkv, N/P, D) the
-    matching K/V rows; ``block_lists``: the global lists for all N/route_block query
-    blocks.  N/P must be a multiple of ``route_block``.  ``plan``: a ``RingPlan`` built
-    once for these lists (else one is built here).  Returns this rank's (out, lse).
+    q: (Z, H, N/P, D) this rank's query rows (``layout`` "contiguous": chunk ``rank``;
+    "zigzag": chunks ``rank`` and ``2P - 1 - rank`` of N/2P rows, in that order); k, v:
+    (Z, Hkv, N/P, D) the matching K/V rows; ``block_lists``: the global lists for all
+    N/route_block query blocks.  Chunks must be multiples of ``route_block``.  ``plan``: a
+    ``RingPlan`` built once for these lists (else one is built here).  Returns this rank's
+    (out, lse) in its local row order.
 
     Hop j pairs rank r with ranks r - j (whose chunk it attends) and r + j (which attends
     r's chunk).  Only the key blocks that the receiver's lists reference cross the link --
@@ -189,7 +267,7 @@ def ring_block_list_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if k.shape != v.shape or k.shape[0] != Z or k.shape[2] != Nl or k.shape[3] != D:
         raise ValueError("k and v must be (Z, Hkv, N/P, D) chunks matching q")
     if plan is None:
-        plan = RingPlan(block_lists, world, rank, Nl, route_block, is_causal)
+        plan = RingPlan(block_lists, world, rank, Nl, route_block, is_causal, layout)
     elif (plan.world, plan.rank, plan.rows, plan.route_block, plan.is_causal) != (
             world, rank, Nl, route_block, is_causal):
         raise ValueError("plan was built for another ring layout")
@@ -256,29 +334,33 @@ def ring_block_list_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 def ring_emulate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_lists: BlockLists,
                  world: int, *, route_block: int = 128, is_causal: bool = False,
-                 sm_scale: Optional[float] = None) -> tuple[torch.Tensor, torch.Tensor]:
+                 sm_scale: Optional[float] = None, layout: str = "contiguous"
+                 ) -> tuple[torch.Tensor, torch.Tensor]:
     """The ring's per-rank hop computations and merges run one rank after another on one
-    device (no transfer): same chunk lists, attention and merge calls as
-    ``ring_block_list_attention``.  q, k, v are the full (Z, *, N, D) tensors."""
+    device (no transfer): same plans, lists, attention and merge calls as
+    ``ring_block_list_attention``.  q, k, v are the full (Z, *, N, D) tensors; the result is
+    in global row order."""
     Z, H, N, D = q.shape
-    if N % world or (N // world) % route_block:
-        raise ValueError("N must split into world chunks that are multiples of route_block")
+    nparts = 2 if layout == "zigzag" else 1
+    if N % (world * nparts) or (N // (world * nparts)) % route_block:
+        raise ValueError("N must split into chunks that are multiples of route_block")
     Nl = N // world
-    nbl = Nl // route_block
+    cs = Nl // nparts
     scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(D)
-    outs, lses = [], []
+    out_all = torch.empty_like(q)
+    lse_all = torch.empty((Z, H, N), dtype=torch.float32, device=q.device)
+    local_rows = lambda r: torch.cat([torch.arange(c * cs, (c + 1) * cs)
+                                      for c in rank_chunks(r, world, layout)]).to(q.device)
     for rank in range(world):
-        rows = slice(rank * Nl, (rank + 1) * Nl)
-        qr = q[:, :, rows]
+        rows = local_rows(rank)
+        qr = q.index_select(2, rows)
+        plan = RingPlan(block_lists, world, rank, Nl, route_block, is_causal, layout)
         acc = _accumulate_ok(qr, route_block)
         merge = None if acc else _CudaMerge(qr)
         out = torch.empty_like(qr)
         lse = torch.empty(qr.shape[:3], dtype=torch.float32, device=q.device)
-        hops = ring_hops(rank, world, is_causal)
-        for i, (_, c, causal) in enumerate(hops):
-            kr, vr = k[:, :, c * Nl:(c + 1) * Nl], v[:, :, c * Nl:(c + 1) * Nl]
-            sub, cnt = chunk_lists(block_lists.lists, block_lists.counts, rank * nbl,
-                                   (rank + 1) * nbl, c * nbl, (c + 1) * nbl)
+        for i, (c, causal, sub, cnt) in enumerate(plan.hops):
+            kr, vr = k.index_select(2, local_rows(c)), v.index_select(2, local_rows(c))
             if acc:
                 # odd ranks without a planner workspace: both schedules stay exercised
                 ws = None
@@ -288,7 +370,7 @@ def ring_emulate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_lists:
                 _fwd_direct(qr, kr, vr, sub, cnt, route_block, causal, scale, out, lse, i > 0, ws)
             else:
                 o_j, lse_j = _attn_cuda(qr, kr, vr, sub, cnt, route_block, causal, scale)
-                merge(o_j, lse_j, i == 0, out if i == len(hops) - 1 else None)
-        outs.append(out)
-        lses.append(lse if acc else merge.lse)
-    return torch.cat(outs, dim=2), torch.cat(lses, dim=2)
+                merge(o_j, lse_j, i == 0, out if i == len(plan.hops) - 1 else None)
+        out_all.index_copy_(2, rows, out)
+        lse_all.index_copy_(2, rows, lse if acc else merge.lse)
+    return out_all, lse_all

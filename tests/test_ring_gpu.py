@@ -52,9 +52,11 @@ def test_lse_merge_kernel_matches_cpu_merge():
     assert_half_close(out_g.cpu(), out_c.float(), "merge out")
 
 
-@pytest.mark.parametrize("world,causal", [(4, True), (2, False)])
-def test_ring_emulation_matches_whole_forward(world, causal):
-    """C5-shaped (H=16/8 heads of 128, causal + sink, tree routes) at N=4096."""
+@pytest.mark.parametrize("world,causal,layout", [(4, True, "contiguous"), (2, False, "contiguous"),
+                                                 (4, True, "zigzag"), (2, True, "zigzag")])
+def test_ring_emulation_matches_whole_forward(world, causal, layout):
+    """C5-shaped (H=16/8 heads of 128, causal + sink, tree routes) at N=4096; both ring
+    layouts (contiguous chunks, and the balanced zigzag pair of chunks per rank)."""
     Z, H, Hkv, N, D, RB, TD = 1, 16, 8, 4096, 128, 128, 6
     gen = torch.Generator().manual_seed(5)
     q = torch.randn(Z, H, N, D, generator=gen).bfloat16().to(DEV)
@@ -62,7 +64,7 @@ def test_ring_emulation_matches_whole_forward(world, causal):
     v = torch.randn(Z, Hkv, N, D, generator=gen).bfloat16().to(DEV)
     router = tree_router(Z, H, N // RB, TD).to(DEV)
     bl = build_block_lists(router, 3, is_causal=causal, sink_block=True, arity=2)
-    out_r, lse_r = ring_emulate(q, k, v, bl, world, route_block=RB, is_causal=causal)
+    out_r, lse_r = ring_emulate(q, k, v, bl, world, route_block=RB, is_causal=causal, layout=layout)
     out_f, lse_f = block_list_attention(q, k, v, bl, route_block=RB, is_causal=causal, return_lse=True)
     assert_half_close(out_r.float().cpu(), out_f.float().cpu(), "ring vs whole forward")
     torch.testing.assert_close(lse_r.cpu(), lse_f.cpu(), rtol=1e-4, atol=1e-3)
