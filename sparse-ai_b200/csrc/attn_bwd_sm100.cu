@@ -805,50 +805,53 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
 // =======================================================================================
 //
 // The dK/dV kernel's pipeline plus, per streamed 64-row query sub-tile,
-//    dQ^T[b] = K^T dS^T   (M=128 head-dim rows, N=64 query rows, K=128 keys)
-// with K^T read MN-major from the resident K tile, dS^T (bf16) written by the elementwise
-// warps into shared memory as well as TMEM, and the accumulator in the dP^T[b] columns, which
-// are free once the elementwise warps have read dP^T.  P^T and dS^T (bf16 pairs) both go into
-// the S^T[b] columns: half hc of the 64 query columns puts P^T at [32 hc, 32 hc + 16) and dS^T
-// at [32 hc + 16, 32 hc + 32).  The owning elementwise group then reads the dQ^T tile out of
-// TMEM, releases the columns and adds it into an fp32 dQ accumulator in global memory
-// (red.global.add.f32: per warp and query row one coalesced 128-byte reduction at L2).  The
-// group that brings a query sub-tile's last contribution (an arrival counter per 64-row
-// sub-tile) converts its 64 accumulated rows to dQ.  Tensor work per kept pair is 10 RB^2 D
+//    dQ^T = K^T dS^T   (M=128 head-dim rows, N=64 query rows, K=128 keys)
+// with K^T read MN-major from the resident K tile and dS^T (bf16) written by the elementwise
+// warps into shared memory as well as into TMEM.  Tensor work per kept pair is 10 RB^2 D
 // (S^T, dP^T, dV, dK, dQ) against 14 for the separate dQ and dK/dV kernels, and there is one
-// elementwise pass instead of two.  dQ's summation order depends on timing (atomics), so it is
-// not bitwise reproducible from run to run; the two-kernel path is.
+// elementwise pass instead of two.
 //
-// The MMA thread polls its barriers instead of following a fixed order: it issues S^T/dP^T of
-// the next sub-tile as soon as its stage is loaded and its TMEM buffer drained, and the
-// accumulating MMAs of the oldest pending sub-tile as soon as its P^T/dS^T are written, so the
-// tensor pipe is fed whichever way the elementwise and drain latencies fall.  The
-// accumulating MMAs stay in sub-tile order (dV and dK sums are reproducible).
+// TMEM (512 columns): S^T[2] at 0 / 64 (double-buffered: P^T and dS^T bf16 pairs overwrite
+// them, half hc of the 64 query columns holding P^T at [32 hc, 32 hc + 16) and dS^T at
+// [32 hc + 16, 32 hc + 32)), one dP^T buffer at 128, one dQ^T buffer at 192, dV at 256 and dK
+// at 384.  The tensor pipe runs A(j+1) B(j) A(j+2) B(j+1) ..., where A(j) = S^T, dP^T of
+// sub-tile j and B(j) = dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T.  A(j) needs the dP^T
+// buffer read out by sub-tile j-1's group (DPFREE, signalled right after its first TMEM
+// loads) and B(j) needs dQ^T(j-1) read out (DQEMPTY): both happen while the other block
+// runs, so neither waits for a drain.
+//
+// The owning group reads dQ^T out of TMEM and stages it as fp32 rows [q][d] in the
+// sub-tile's own Q/dO stage, whose tiles B(j) no longer needs once DQFULL(j) fired; one
+// bulk reduction (cp.reduce.async.bulk .add.f32, performed at L2) adds the rows into an
+// fp32 dQ accumulator, and the group's leader hands the stage back to the loader once the
+// reduction has read it.  dQ's summation order depends on timing, so it is not bitwise
+// reproducible from run to run; the two-kernel path is.
+//
+// The MMA thread polls its barriers (mbarrier.test_wait, never a blocking try_wait) and
+// issues whichever block is ready; the accumulating MMAs stay in sub-tile order, so dV and
+// dK sums are reproducible.
 
-constexpr int kFuStages = 3;
+constexpr int kFuStages = 4;
 
 struct FuLayout {
   static constexpr int D = 128;
   static constexpr uint32_t kK = 0;                      // [128][128] (2 boxes of 64 columns)
   static constexpr uint32_t kV = kRows * D * 2;
   static constexpr uint32_t kQD = 2 * kRows * D * 2;     // stages x (Q [64][D], dO [64][D])
-  static constexpr uint32_t kStage = 2 * kSub * D * 2;
+  static constexpr uint32_t kStage = 2 * kSub * D * 2;   // later: dQ rows [64][D] fp32
   static constexpr uint32_t kDsT = kQD + kFuStages * kStage;  // 2 x dS^T [128 keys][64 q] bf16
   static constexpr uint32_t kDsTBytes = kRows * kSub * 2;
-  static constexpr uint32_t kStg = kDsT + 2 * kDsTBytes;  // per group: dQ rows [32][D] fp32
-  static constexpr uint32_t kStgBytes = 32 * D * 4;
-  static constexpr uint32_t kStats = kStg + 2 * kStgBytes;  // stages x {lse*log2e[64], delta[64]}
+  static constexpr uint32_t kStats = kDsT + 2 * kDsTBytes;  // stages x {lse*log2e[64], delta[64]}
   static constexpr uint32_t kBars = kStats + kFuStages * 512;
   static constexpr uint32_t kMeta = kBars + 256;  // FuMeta[kFuStages]
-  static constexpr uint32_t kRingOff = kMeta + 128;
-  static constexpr uint32_t kTmemSlot = kRingOff + 64;
+  static constexpr uint32_t kRingOff = kMeta + 32 * kFuStages;
+  static constexpr uint32_t kTmemSlot = kRingOff + 16 * kRing;
   static constexpr uint32_t kBytes = kTmemSlot + 16;
   // alignment slack for the 1024-byte aligned tiles, as far as the opt-in limit allows; the
   // kernel checks the padding it needs against %dynamic_smem_size
   static constexpr uint32_t kAlloc = kBytes + 1024 <= 232448 ? kBytes + 1024 : 232448;
-  static_assert(kDsT % 1024 == 0 && kStage % 1024 == 0 && kStg % 1024 == 0,
-                "swizzled tiles need 1024-byte alignment");
-  static_assert(kDsTBytes == kStgBytes, "a dS^T buffer doubles as a dQ staging buffer");
+  static_assert(kDsT % 1024 == 0 && kStage % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+  static_assert(kStage == kSub * D * 4, "a Q/dO stage holds the sub-tile's fp32 dQ rows");
   static_assert(kBytes <= 232448, "fused backward shared-memory layout too large");
 };
 
@@ -861,9 +864,11 @@ struct FuMeta {
 };
 static_assert(sizeof(FuMeta) == 32, "FuMeta layout");
 
+constexpr uint32_t kFuColDp = 128, kFuColDq = 192;  // TMEM: single dP^T and dQ^T buffers
+
 enum { FU_KVFULL = 0, FU_KVEMPTY, FU_QFULL0, FU_QEMPTY0 = FU_QFULL0 + kFuStages,
-       FU_SFULL0 = FU_QEMPTY0 + kFuStages, FU_PFULL0 = FU_SFULL0 + 2, FU_DQFULL0 = FU_PFULL0 + 2,
-       FU_DQEMPTY0 = FU_DQFULL0 + 2, FU_DONE = FU_DQEMPTY0 + 2, FU_EPI, FU_GSYNC0,
+       FU_SFULL0 = FU_QEMPTY0 + kFuStages, FU_PFULL0 = FU_SFULL0 + 2, FU_DPFREE = FU_PFULL0 + 2,
+       FU_DQFULL0, FU_DQEMPTY = FU_DQFULL0 + 2, FU_DONE, FU_EPI, FU_GSYNC0,
        FU_WFULL0 = FU_GSYNC0 + 2, FU_WEMPTY0 = FU_WFULL0 + kRing, FU_NUM = FU_WEMPTY0 + kRing };
 static_assert(FU_NUM * 8 <= 256, "fused backward barriers");
 
@@ -894,10 +899,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
     for (int i = 0; i < FU_NUM; ++i) cnt[i] = 1;
     for (int b = 0; b < 2; ++b) {
       cnt[FU_PFULL0 + b] = kEwThreads / 2;   // the owning group
-      cnt[FU_DQEMPTY0 + b] = kEwThreads / 2;
       cnt[FU_GSYNC0 + b] = kEwThreads / 2;   // group-wide sync of group b
     }
-    cnt[FU_EPI] = kEwThreads;  // both groups have read the dV / dK accumulators
+    cnt[FU_DPFREE] = kEwThreads / 2;   // the sub-tile's group has read dP^T
+    cnt[FU_DQEMPTY] = kEwThreads / 2;  // the sub-tile's group has read dQ^T
+    cnt[FU_EPI] = kEwThreads;          // both groups have read the dV / dK accumulators
+    // QEMPTY: one arrival, the owning group's leader once its dQ reduction read the stage
     for (int i = 0; i < kRing; ++i) cnt[FU_WEMPTY0 + i] = 1 + kEwThreads;
     init_bars(bars, cnt, FU_NUM);
   }
@@ -951,6 +958,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
           meta[st].bias_idx = a.dbias ? (zh * a.NB + qb) * a.list_stride + slot : -1;
           meta[st].b2 = bias_log2(a, it.z, h, qb, slot);
           meta[st].qb = (int)qb;
+          // the previous user of the stage wrote dQ rows into it with generic stores, and
+          // its reduction read them, before the leader's QEMPTY arrival
           mbar_arrive_expect_tx(&bars[FU_QFULL0 + st], L::kStage + 2 * kSub * 4);
           for (int c = 0; c < D / 64; ++c) {
             tma_load_4d(stage + c * kSub * 128, &a.tm_q, &bars[FU_QFULL0 + st], c * 64, (int)q0,
@@ -973,8 +982,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
       constexpr uint32_t id_acc = idesc_f16(kRows, D, BF16, false, true);
       // dQ^T = K^T dS^T: A (head dim x keys) and B (keys x query rows) both MN-major
       constexpr uint32_t id_dq = idesc_f16(kRows, kSub, BF16, true, true);
-      const uint32_t k_addr = smem_u32(sm + L::kK), v_addr = smem_u32(sm + L::kV);
-      const uint32_t ds_addr = smem_u32(sm + L::kDsT);
+      // base descriptors (K-major for S^T / dP^T, MN-major for dQ^T); per-MMA tiles by desc_add
+      const uint64_t kd_k = smem_desc(smem_u32(sm + L::kK), 16, 1024);
+      const uint64_t vd_k = smem_desc(smem_u32(sm + L::kV), 16, 1024);
+      const uint64_t kd_mn = smem_desc(smem_u32(sm + L::kK), kRows * 128, 1024);
+      const uint64_t dsd0_mn = smem_desc(smem_u32(sm + L::kDsT), kSub * 128, 1024);
       uint32_t ga = 0, gb = 0, jk = 0, n_items = 0;  // sub-tiles with A / B issued (all items)
       bool ok = true;
       for (uint32_t w = 0; ok; ++w) {
@@ -989,25 +1001,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
         long long idle_since = clock64();
         while (ib < n) {
           bool progressed = false;
-          // A: S^T / dP^T of sub-tile ga into TMEM buffer ga & 1.  The buffer's S^T columns
-          // are free once the accumulating MMAs of sub-tile ga - 2 are issued (ia - ib < 2;
-          // MMAs execute in issue order), its dP^T columns once that sub-tile's dQ^T tile
-          // was read out (DQEMPTY).
+          // A: S^T / dP^T of sub-tile ga, S^T into buffer ga & 1.  That buffer is free once
+          // B(ga - 2) is issued (ia - ib < 2; MMAs execute in issue order), the dP^T buffer
+          // once sub-tile ga - 1's group has read it (DPFREE).
           if (ia < n && ia - ib < 2) {
             const uint32_t st = ga % kFuStages, ph = (ga / kFuStages) & 1, sb = ga & 1;
-            const bool drained = ga < 2 || mbar_try_wait(&bars[FU_DQEMPTY0 + sb], ((ga >> 1) - 1) & 1);
-            if (drained && mbar_try_wait(&bars[FU_QFULL0 + st], ph)) {
+            if ((ga == 0 || mbar_test(&bars[FU_DPFREE], (ga - 1) & 1)) &&
+                mbar_test(&bars[FU_QFULL0 + st], ph)) {
               tc_fence_after();
-              const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
-              const uint32_t do_addr = q_addr + kSub * D * 2;
+              const uint64_t qd_k = smem_desc(smem_u32(sm + L::kQD + st * L::kStage), 16, 1024);
+              const uint64_t dod_k = desc_add(qd_k, kSub * D * 2);
 #pragma unroll
               for (int kk = 0; kk < D / 16; ++kk) {
                 const uint32_t oa = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
                 const uint32_t ob = (kk >> 2) * (kSub * 128) + (kk & 3) * 32;
-                tc_mma_f16(tmem + kColS + sb * kSub, smem_desc(k_addr + oa, 16, 1024),
-                           smem_desc(q_addr + ob, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-                tc_mma_f16(tmem + kColP + sb * kSub, smem_desc(v_addr + oa, 16, 1024),
-                           smem_desc(do_addr + ob, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+                tc_mma_f16(tmem + kColS + sb * kSub, desc_add(kd_k, oa), desc_add(qd_k, ob), id_s,
+                           kk > 0 ? 1u : 0u);
+                tc_mma_f16(tmem + kFuColDp, desc_add(vd_k, oa), desc_add(dod_k, ob), id_s,
+                           kk > 0 ? 1u : 0u);
               }
               tc_commit(&bars[FU_SFULL0 + sb]);
               ++ga;
@@ -1015,34 +1026,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
               progressed = true;
             }
           }
-          // B: dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T of the oldest pending sub-tile.  The
-          // item's first one overwrites the dV / dK accumulators: the previous item's epilogue
-          // must have read them (EPI).
+          // B: dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T of the oldest pending sub-tile,
+          // once its P^T / dS^T are written (PFULL) and dQ^T(gb - 1) was read out (DQEMPTY).
+          // The item's first one overwrites the dV / dK accumulators: the previous item's
+          // epilogue must have read them (EPI).
           if (ib < ia) {
             const uint32_t pb = gb & 1;
-            const bool epi_ok = ib > 0 || n_items == 0 || mbar_try_wait(&bars[FU_EPI], (n_items - 1) & 1);
-            if (epi_ok && mbar_try_wait(&bars[FU_PFULL0 + pb], (gb >> 1) & 1)) {
+            if ((ib > 0 || n_items == 0 || mbar_test(&bars[FU_EPI], (n_items - 1) & 1)) &&
+                (gb == 0 || mbar_test(&bars[FU_DQEMPTY], (gb - 1) & 1)) &&
+                mbar_test(&bars[FU_PFULL0 + pb], (gb >> 1) & 1)) {
               tc_fence_after();
               const uint32_t st = gb % kFuStages;
-              const uint32_t q_addr = smem_u32(sm + L::kQD + st * L::kStage);
-              const uint32_t do_addr = q_addr + kSub * D * 2;
+              const uint64_t qd_mn = smem_desc(smem_u32(sm + L::kQD + st * L::kStage), kSub * 128, 1024);
+              const uint64_t dod_mn = desc_add(qd_mn, kSub * D * 2);
               const uint32_t colS = kColS + pb * kSub;
 #pragma unroll
               for (int kk = 0; kk < kSub / 16; ++kk) {
                 const uint32_t acc = (ib > 0 || kk > 0) ? 1u : 0u;
                 const uint32_t pcol = colS + (kk >> 1) * 32 + (kk & 1) * 8;  // P^T, then dS^T + 16
-                tc_mma_f16_ts(tmem + kColAcc, tmem + pcol,
-                              smem_desc(do_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
-                tc_mma_f16_ts(tmem + kColAcc + D, tmem + pcol + 16,
-                              smem_desc(q_addr + kk * 16 * 128, kSub * 128, 1024), id_acc, acc);
+                tc_mma_f16_ts(tmem + kColAcc, tmem + pcol, desc_add(dod_mn, kk * 16 * 128), id_acc, acc);
+                tc_mma_f16_ts(tmem + kColAcc + D, tmem + pcol + 16, desc_add(qd_mn, kk * 16 * 128), id_acc,
+                              acc);
               }
-              const uint32_t dsb = ds_addr + pb * L::kDsTBytes;
+              const uint64_t dsd_mn = desc_add(dsd0_mn, pb * L::kDsTBytes);
 #pragma unroll
               for (int kk = 0; kk < kRows / 16; ++kk)
-                tc_mma_f16(tmem + kColP + pb * kSub,
-                           smem_desc(k_addr + kk * 16 * 128, kRows * 128, 1024),
-                           smem_desc(dsb + kk * 16 * 128, kSub * 128, 1024), id_dq, kk > 0 ? 1u : 0u);
-              tc_commit(&bars[FU_QEMPTY0 + st]);
+                tc_mma_f16(tmem + kFuColDq, desc_add(kd_mn, kk * 16 * 128),
+                           desc_add(dsd_mn, kk * 16 * 128), id_dq, kk > 0 ? 1u : 0u);
               tc_commit(&bars[FU_DQFULL0 + pb]);
               ++gb;
               ++ib;
@@ -1072,6 +1082,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
     const float scale2 = a.scale * kLog2e;
     const bool leader = (warp & 3) == 2 && lane == 0;  // one thread per group (warps 2 and 6)
     uint32_t s_it = 0, done_it = 0, qd = 0, gsync = 0;
+    int pend_st = -1;  // the leader's stage awaiting its reduction's read before release
     bool ok = true;
     // Sync of this group's 4 warps on an mbarrier with a bounded wait (a named barrier would
     // wait forever on a warp that gave up); warp-uniform result.
@@ -1091,49 +1102,63 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
         if ((int)sb != grp) continue;
         const uint32_t st = qd % kFuStages, ph = (qd / kFuStages) & 1;
         if (!(ok = mbar_wait_warp(&bars[FU_QFULL0 + st], ph, a.status))) break;
-        const float* stats = reinterpret_cast<const float*>(sm + L::kStats + st * 512);
+        float* stats = reinterpret_cast<float*>(sm + L::kStats + st * 512);
         const FuMeta m = meta[st];
         const int64_t q0 = m.start;
+        // per-column constants of the sub-tile, once for the group, over its stage's row
+        // stats (only this group reads them): soft bias - lse (both in log2 units) and
+        // -delta * scale, so that an element costs one f32x2 FMA per pair for the exponent
+        // and one for dP - delta
+        if (rl < kSub) {
+          stats[rl] = m.b2 - stats[rl];
+          stats[kSub + rl] = -stats[kSub + rl] * a.scale;
+        }
         if (!(ok = mbar_wait_warp(&bars[FU_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
-        // this group's bulk reductions of its previous sub-tile have read their sources (its
-        // staging buffer and this dS^T buffer) before either is written again
-        if (leader) bulk_wait_read();
-        if (!(ok = group_sync())) break;
+        // dP^T out first, so that A(s_it + 1) can overwrite the buffer as early as possible
+        float dp[64], s[32];
+        tmem_ld32(lane_addr + kFuColDp, *reinterpret_cast<float(*)[32]>(dp));
+        tmem_ld32(lane_addr + kFuColDp + 32, *reinterpret_cast<float(*)[32]>(dp + 32));
+        tmem_ld32(lane_addr + kColS + sb * kSub, s);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[FU_DPFREE]);
+        if (!(ok = group_sync())) break;  // the column constants are visible
         const int64_t cmin = a.causal ? key - q0 : 0;
         const int lo = (int)max((int64_t)0, min((int64_t)kSub, cmin));
         const int hi = key < a.N ? (int)max((int64_t)0, min((int64_t)kSub, a.N - q0)) : 0;
         const bool full = lo == 0 && hi == kSub;
         unsigned char* dsrow = sm + L::kDsT + sb * L::kDsTBytes + rl * 128;
-        float rs = 0.f;
+        uint64_t rs2 = 0;  // dS * scale summed in pairs (the soft bias gradient, rescaled below)
+        const uint64_t scale2x2 = f32x2(scale2, scale2), scalex2 = f32x2(a.scale, a.scale);
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc) {
-          float s[32], dp[32];
-          tmem_ld32(lane_addr + kColS + sb * kSub + hc * 32, s);
-          tmem_ld32(lane_addr + kColP + sb * kSub + hc * 32, dp);
-          tmem_wait_ld();
-          const float4* l2v = reinterpret_cast<const float4*>(stats + hc * 32);
-          const float4* dlv = reinterpret_cast<const float4*>(stats + kSub + hc * 32);
+          if (hc == 1) {
+            tmem_ld32(lane_addr + kColS + sb * kSub + 32, s);
+            tmem_wait_ld();
+          }
+          const float4* cv = reinterpret_cast<const float4*>(stats + hc * 32);
+          const float4* nv = reinterpret_cast<const float4*>(stats + kSub + hc * 32);
           uint32_t pk[16], dk[16];
 #pragma unroll
           for (int c4 = 0; c4 < 8; ++c4) {
-            const float4 l4 = l2v[c4], d4 = dlv[c4];
-            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+            const float4 c = cv[c4], nd = nv[c4];
+            const int c0 = c4 * 4, cd = hc * 32 + c0;
             float p[4], d[4];
+            f32x2_split(fma_f32x2(f32x2(s[c0], s[c0 + 1]), scale2x2, f32x2(c.x, c.y)), p[0], p[1]);
+            f32x2_split(fma_f32x2(f32x2(s[c0 + 2], s[c0 + 3]), scale2x2, f32x2(c.z, c.w)), p[2], p[3]);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-              const int c = c4 * 4 + u;
-              p[u] = fast_exp2(fmaf(s[c], scale2, m.b2) - lv[u]);
-              d[u] = p[u] * (dp[c] - dv[u]);
-              if (!full) {
-                const int cc = hc * 32 + c;
-                const bool vis = cc >= lo && cc < hi;
-                p[u] = vis ? p[u] : 0.f;
-                d[u] = vis ? d[u] : 0.f;
-              }
-              rs += d[u];
-              d[u] *= a.scale;
+              p[u] = fast_exp2(p[u]);
+              if (!full) p[u] = (cd + u >= lo && cd + u < hi) ? p[u] : 0.f;
             }
+            const uint64_t d01 = mul_f32x2(f32x2(p[0], p[1]),
+                                           fma_f32x2(f32x2(dp[cd], dp[cd + 1]), scalex2, f32x2(nd.x, nd.y)));
+            const uint64_t d23 = mul_f32x2(f32x2(p[2], p[3]),
+                                           fma_f32x2(f32x2(dp[cd + 2], dp[cd + 3]), scalex2, f32x2(nd.z, nd.w)));
+            rs2 = add_f32x2(rs2, add_f32x2(d01, d23));
+            f32x2_split(d01, d[0], d[1]);
+            f32x2_split(d23, d[2], d[3]);
             pk[c4 * 2] = pack2(p[0], p[1], BF16);
             pk[c4 * 2 + 1] = pack2(p[2], p[3], BF16);
             dk[c4 * 2] = pack2(d[0], d[1], BF16);
@@ -1143,7 +1168,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
           tmem_st16(lane_addr + kColS + sb * kSub + hc * 32, pk);
           tmem_st16(lane_addr + kColS + sb * kSub + hc * 32 + 16, dk);
           // dS^T row `rl`, query columns [32 hc, 32 hc + 32), into the dQ MMA's B tile
-          // (128-byte rows, 16-byte units swizzled by the row's low 3 bits)
+          // (128-byte rows, 16-byte units swizzled by the row's low 3 bits).  The buffer's
+          // previous dQ^T MMA (sub-tile s_it - 2, this group's) completed before this group
+          // read its dQ^T out.
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             const int unit = hc * 4 + v;
@@ -1158,38 +1185,42 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
         tc_fence_before();
         mbar_arrive(&bars[FU_PFULL0 + sb]);
         if (m.bias_idx >= 0) {
+          float r0, r1;
+          f32x2_split(rs2, r0, r1);
+          float rs = (r0 + r1) / a.scale;
 #pragma unroll
           for (int o = 16; o; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
           if (lane == 0) atomicAdd(&a.dbias[m.bias_idx], rs);
         }
-        // dQ^T of this sub-tile: out of TMEM, release the columns, add into the accumulator
+        // this group's previous stage goes back to the loader once its reduction has read it
+        // (long done by now: off the elementwise path)
+        if (leader && pend_st >= 0) {
+          bulk_wait_read();
+          mbar_arrive(&bars[FU_QEMPTY0 + pend_st]);
+          pend_st = -1;
+        }
+        // dQ^T of this sub-tile: out of TMEM, release the buffer, stage the rows, reduce
+        // one barrier per sub-tile parity: this group saw the phase before last of its own
         if (!(ok = mbar_wait_warp(&bars[FU_DQFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
         float dq[64];
-        tmem_ld32(lane_addr + kColP + sb * kSub, *reinterpret_cast<float(*)[32]>(dq));
-        tmem_ld32(lane_addr + kColP + sb * kSub + 32, *reinterpret_cast<float(*)[32]>(dq + 32));
+        tmem_ld32(lane_addr + kFuColDq, *reinterpret_cast<float(*)[32]>(dq));
+        tmem_ld32(lane_addr + kFuColDq + 32, *reinterpret_cast<float(*)[32]>(dq + 32));
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&bars[FU_DQEMPTY0 + sb]);
-        // dQ^T -> fp32 rows [q][d]: query rows 0-31 into this group's staging buffer, 32-63
-        // into this dS^T buffer (free: the dQ^T MMA that read it has completed); each half is
-        // added into the accumulator by one bulk reduction (cp.reduce.async.bulk .add.f32,
-        // performed at L2).  Nobody waits for them here: the next sub-tile of this group
-        // waits for their reads before it writes either buffer.
+        mbar_arrive(&bars[FU_DQEMPTY]);
+        // dQ^T -> fp32 rows [q][d] over the stage's Q/dO tiles (B of this sub-tile, their
+        // last reader, has completed: DQFULL), added into the accumulator by one bulk
+        // reduction performed at L2
         const int rows = (int)min((int64_t)kSub, a.N - q0);
-        float* stg0 = reinterpret_cast<float*>(sm + L::kStg + grp * L::kStgBytes);
-        float* stg1 = reinterpret_cast<float*>(sm + L::kDsT + sb * L::kDsTBytes);
+        float* stg = reinterpret_cast<float*>(sm + L::kQD + st * L::kStage);
 #pragma unroll
-        for (int r = 0; r < 32; ++r) {
-          stg0[r * D + rl] = dq[r];
-          stg1[r * D + rl] = dq[32 + r];
-        }
+        for (int r = 0; r < kSub; ++r) stg[r * D + rl] = dq[r];
         fence_proxy_async_smem();
         if (!(ok = group_sync())) break;
         if (leader) {
-          float* gdst = a.dq_acc + (m.zh * a.N + q0) * D;
-          bulk_reduce_add_f32(gdst, stg0, (uint32_t)min(32, rows) * D * 4);
-          if (rows > 32) bulk_reduce_add_f32(gdst + 32 * D, stg1, (uint32_t)(rows - 32) * D * 4);
+          bulk_reduce_add_f32(a.dq_acc + (m.zh * a.N + q0) * D, stg, (uint32_t)rows * D * 4);
+          pend_st = (int)st;
         }
       }
       if (!ok) break;
@@ -1227,6 +1258,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
       }
       tc_fence_before();
       if (n > 0) mbar_arrive(&bars[FU_EPI]);
+    }
+    // a stage still held for its reduction: the loader has nothing left to load into it, but
+    // release it all the same so that every QEMPTY phase completes
+    if (leader && pend_st >= 0) {
+      bulk_wait_read();
+      mbar_arrive(&bars[FU_QEMPTY0 + pend_st]);
     }
   }
   // bulk reductions still in flight complete before the CTA (and its shared memory) ends
