@@ -833,6 +833,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
 
 constexpr int kFuStages = 4;
 
+
 struct FuLayout {
   static constexpr int D = 128;
   static constexpr uint32_t kK = 0;                      // [128][128] (2 boxes of 64 columns)
@@ -872,7 +873,9 @@ enum { FU_KVFULL = 0, FU_KVEMPTY, FU_QFULL0, FU_QEMPTY0 = FU_QFULL0 + kFuStages,
        FU_WFULL0 = FU_GSYNC0 + 2, FU_WEMPTY0 = FU_WFULL0 + kRing, FU_NUM = FU_WEMPTY0 + kRing };
 static_assert(FU_NUM * 8 <= 256, "fused backward barriers");
 
-template <bool BF16>
+// BIAS_GRAD: the launch wants the soft-bias gradient (a.dbias).  A separate instantiation, so
+// that the kernel without it gets a register allocation free of the running dS sum.
+template <bool BF16, bool BIAS_GRAD>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const __grid_constant__ BwdArgs a) {
   using L = FuLayout;
   constexpr int D = L::D;
@@ -1103,94 +1106,103 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
         const uint32_t st = qd % kFuStages, ph = (qd / kFuStages) & 1;
         if (!(ok = mbar_wait_warp(&bars[FU_QFULL0 + st], ph, a.status))) break;
         float* stats = reinterpret_cast<float*>(sm + L::kStats + st * 512);
-        const FuMeta m = meta[st];
-        const int64_t q0 = m.start;
+        // the sub-tile's meta stays put until this group's leader hands the stage back, so it
+        // is read where it is needed instead of held in registers across the loop
+        const FuMeta* m = &meta[st];
+        const int64_t q0 = m->start;
         // per-column constants of the sub-tile, once for the group, over its stage's row
         // stats (only this group reads them): soft bias - lse (both in log2 units) and
         // -delta * scale, so that an element costs one f32x2 FMA per pair for the exponent
         // and one for dP - delta
         if (rl < kSub) {
-          stats[rl] = m.b2 - stats[rl];
+          stats[rl] = m->b2 - stats[rl];
           stats[kSub + rl] = -stats[kSub + rl] * a.scale;
         }
         if (!(ok = mbar_wait_warp(&bars[FU_SFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
-        // dP^T out first, so that A(s_it + 1) can overwrite the buffer as early as possible
-        float dp[64], s[32];
-        tmem_ld32(lane_addr + kFuColDp, *reinterpret_cast<float(*)[32]>(dp));
-        tmem_ld32(lane_addr + kFuColDp + 32, *reinterpret_cast<float(*)[32]>(dp + 32));
-        tmem_ld32(lane_addr + kColS + sb * kSub, s);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&bars[FU_DPFREE]);
         if (!(ok = group_sync())) break;  // the column constants are visible
         const int64_t cmin = a.causal ? key - q0 : 0;
         const int lo = (int)max((int64_t)0, min((int64_t)kSub, cmin));
         const int hi = key < a.N ? (int)max((int64_t)0, min((int64_t)kSub, a.N - q0)) : 0;
         const bool full = lo == 0 && hi == kSub;
         unsigned char* dsrow = sm + L::kDsT + sb * L::kDsTBytes + rl * 128;
-        uint64_t rs2 = 0;  // dS * scale summed in pairs (the soft bias gradient, rescaled below)
         const uint64_t scale2x2 = f32x2(scale2, scale2), scalex2 = f32x2(a.scale, a.scale);
+        uint64_t rs2 = 0;  // dS * scale summed in pairs (the soft bias gradient, rescaled below)
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc) {
+          // S^T and dP^T by 32-column halves (registers: holding all of dP^T spills).  The
+          // dP^T buffer is released once its second half is read, well before A(s_it + 1)
+          // is due (it follows B(s_it - 1) on the tensor pipe)
+          float s[32], dp[32];
+          tmem_ld32(lane_addr + kColS + sb * kSub + hc * 32, s);
+          tmem_ld32(lane_addr + kFuColDp + hc * 32, dp);
+          tmem_wait_ld();
           if (hc == 1) {
-            tmem_ld32(lane_addr + kColS + sb * kSub + 32, s);
-            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&bars[FU_DPFREE]);
           }
           const float4* cv = reinterpret_cast<const float4*>(stats + hc * 32);
           const float4* nv = reinterpret_cast<const float4*>(stats + kSub + hc * 32);
-          uint32_t pk[16], dk[16];
+          // two quarters of 16 query columns: packed P^T / dS^T (8 columns each) go out as soon
+          // as a quarter is done, which keeps the live registers below the spill line
 #pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            const float4 c = cv[c4], nd = nv[c4];
-            const int c0 = c4 * 4, cd = hc * 32 + c0;
-            float p[4], d[4];
-            f32x2_split(fma_f32x2(f32x2(s[c0], s[c0 + 1]), scale2x2, f32x2(c.x, c.y)), p[0], p[1]);
-            f32x2_split(fma_f32x2(f32x2(s[c0 + 2], s[c0 + 3]), scale2x2, f32x2(c.z, c.w)), p[2], p[3]);
+          for (int qq = 0; qq < 2; ++qq) {
+            uint32_t pk[8], dk[8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              p[u] = fast_exp2(p[u]);
-              if (!full) p[u] = (cd + u >= lo && cd + u < hi) ? p[u] : 0.f;
+            for (int c4i = 0; c4i < 4; ++c4i) {
+              const int c4 = qq * 4 + c4i;
+              const float4 c = cv[c4], nd = nv[c4];
+              const int c0 = c4 * 4, cd = hc * 32 + c0;
+              float p[4], d[4];
+              f32x2_split(fma_f32x2(f32x2(s[c0], s[c0 + 1]), scale2x2, f32x2(c.x, c.y)), p[0], p[1]);
+              f32x2_split(fma_f32x2(f32x2(s[c0 + 2], s[c0 + 3]), scale2x2, f32x2(c.z, c.w)), p[2], p[3]);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                p[u] = fast_exp2(p[u]);
+                if (!full) p[u] = (cd + u >= lo && cd + u < hi) ? p[u] : 0.f;
+              }
+              const uint64_t d01 = mul_f32x2(f32x2(p[0], p[1]),
+                                             fma_f32x2(f32x2(dp[c0], dp[c0 + 1]), scalex2, f32x2(nd.x, nd.y)));
+              const uint64_t d23 = mul_f32x2(f32x2(p[2], p[3]),
+                                             fma_f32x2(f32x2(dp[c0 + 2], dp[c0 + 3]), scalex2, f32x2(nd.z, nd.w)));
+              if constexpr (BIAS_GRAD) rs2 = add_f32x2(rs2, add_f32x2(d01, d23));
+              f32x2_split(d01, d[0], d[1]);
+              f32x2_split(d23, d[2], d[3]);
+              pk[c4i * 2] = pack2(p[0], p[1], BF16);
+              pk[c4i * 2 + 1] = pack2(p[2], p[3], BF16);
+              dk[c4i * 2] = pack2(d[0], d[1], BF16);
+              dk[c4i * 2 + 1] = pack2(d[2], d[3], BF16);
             }
-            const uint64_t d01 = mul_f32x2(f32x2(p[0], p[1]),
-                                           fma_f32x2(f32x2(dp[cd], dp[cd + 1]), scalex2, f32x2(nd.x, nd.y)));
-            const uint64_t d23 = mul_f32x2(f32x2(p[2], p[3]),
-                                           fma_f32x2(f32x2(dp[cd + 2], dp[cd + 3]), scalex2, f32x2(nd.z, nd.w)));
-            rs2 = add_f32x2(rs2, add_f32x2(d01, d23));
-            f32x2_split(d01, d[0], d[1]);
-            f32x2_split(d23, d[2], d[3]);
-            pk[c4 * 2] = pack2(p[0], p[1], BF16);
-            pk[c4 * 2 + 1] = pack2(p[2], p[3], BF16);
-            dk[c4 * 2] = pack2(d[0], d[1], BF16);
-            dk[c4 * 2 + 1] = pack2(d[2], d[3], BF16);
-          }
-          // P^T and dS^T (bf16 pairs) into this half's 32 S^T columns, which this thread has read
-          tmem_st16(lane_addr + kColS + sb * kSub + hc * 32, pk);
-          tmem_st16(lane_addr + kColS + sb * kSub + hc * 32 + 16, dk);
-          // dS^T row `rl`, query columns [32 hc, 32 hc + 32), into the dQ MMA's B tile
-          // (128-byte rows, 16-byte units swizzled by the row's low 3 bits).  The buffer's
-          // previous dQ^T MMA (sub-tile s_it - 2, this group's) completed before this group
-          // read its dQ^T out.
+            // P^T and dS^T (bf16 pairs) into this half's S^T columns, which this thread has
+            // read: quarter qq's P^T at [32 hc + 8 qq, +8), its dS^T 16 columns further on
+            tmem_st8(lane_addr + kColS + sb * kSub + hc * 32 + qq * 8, pk);
+            tmem_st8(lane_addr + kColS + sb * kSub + hc * 32 + 16 + qq * 8, dk);
+            // dS^T row `rl`, query columns [32 hc + 16 qq, +16), into the dQ MMA's B tile
+            // (128-byte rows, 16-byte units swizzled by the row's low 3 bits).  The buffer's
+            // previous dQ^T MMA (sub-tile s_it - 2, this group's) completed before this
+            // group read its dQ^T out.
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int unit = hc * 4 + v;
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                             smem_u32(dsrow + ((unit ^ (rl & 7)) << 4))),
-                         "r"(dk[v * 4 + 0]), "r"(dk[v * 4 + 1]), "r"(dk[v * 4 + 2]), "r"(dk[v * 4 + 3])
-                         : "memory");
+            for (int v = 0; v < 2; ++v) {
+              const int unit = hc * 4 + qq * 2 + v;
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                               smem_u32(dsrow + ((unit ^ (rl & 7)) << 4))),
+                           "r"(dk[v * 4 + 0]), "r"(dk[v * 4 + 1]), "r"(dk[v * 4 + 2]), "r"(dk[v * 4 + 3])
+                           : "memory");
+            }
           }
         }
         tmem_wait_st();
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&bars[FU_PFULL0 + sb]);
-        if (m.bias_idx >= 0) {
+        if constexpr (BIAS_GRAD) {
+          const int64_t bidx = m->bias_idx;
           float r0, r1;
           f32x2_split(rs2, r0, r1);
           float rs = (r0 + r1) / a.scale;
 #pragma unroll
           for (int o = 16; o; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
-          if (lane == 0) atomicAdd(&a.dbias[m.bias_idx], rs);
+          if (lane == 0) atomicAdd(&a.dbias[bidx], rs);
         }
         // this group's previous stage goes back to the loader once its reduction has read it
         // (long done by now: off the elementwise path)
@@ -1203,23 +1215,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
         // one barrier per sub-tile parity: this group saw the phase before last of its own
         if (!(ok = mbar_wait_warp(&bars[FU_DQFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
-        float dq[64];
-        tmem_ld32(lane_addr + kFuColDq, *reinterpret_cast<float(*)[32]>(dq));
-        tmem_ld32(lane_addr + kFuColDq + 32, *reinterpret_cast<float(*)[32]>(dq + 32));
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&bars[FU_DQEMPTY]);
-        // dQ^T -> fp32 rows [q][d] over the stage's Q/dO tiles (B of this sub-tile, their
-        // last reader, has completed: DQFULL), added into the accumulator by one bulk
-        // reduction performed at L2
+        // by 32-column halves (registers); the buffer is released after the second read
         const int rows = (int)min((int64_t)kSub, a.N - q0);
         float* stg = reinterpret_cast<float*>(sm + L::kQD + st * L::kStage);
 #pragma unroll
-        for (int r = 0; r < kSub; ++r) stg[r * D + rl] = dq[r];
+        for (int hq = 0; hq < 2; ++hq) {
+          float dq[32];
+          tmem_ld32(lane_addr + kFuColDq + hq * 32, dq);
+          tmem_wait_ld();
+          if (hq == 1) {
+            tc_fence_before();
+            mbar_arrive(&bars[FU_DQEMPTY]);
+          }
+          // dQ^T -> fp32 rows [q][d] over the stage's Q/dO tiles (B of this sub-tile, their
+          // last reader, has completed: DQFULL), added into the accumulator by one bulk
+          // reduction performed at L2
+#pragma unroll
+          for (int r = 0; r < 32; ++r) stg[(hq * 32 + r) * D + rl] = dq[r];
+        }
         fence_proxy_async_smem();
         if (!(ok = group_sync())) break;
         if (leader) {
-          bulk_reduce_add_f32(a.dq_acc + (m.zh * a.N + q0) * D, stg, (uint32_t)rows * D * 4);
+          bulk_reduce_add_f32(a.dq_acc + (m->zh * a.N + q0) * D, stg, (uint32_t)rows * D * 4);
           pend_st = (int)st;
         }
       }
@@ -1436,7 +1453,7 @@ int launch_fused_t(const AttnParams& p, cudaStream_t stream) {
   const PlanPtrs pp = plan_carve(p.plan_dkdv, kPlanDkdv, items, ctas, D);
   a.sched = SchedArgs{pp.header, pp.queue, items, 0};
   a.partials = pp.partials;
-  auto kern = bwd_fused_sm100_kernel<BF16>;
+  auto kern = a.dbias ? bwd_fused_sm100_kernel<BF16, true> : bwd_fused_sm100_kernel<BF16, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FuLayout::kAlloc);
   kern<<<(unsigned)ctas, kBwdThreads, FuLayout::kAlloc, stream>>>(a);
   rc = check_launch("bwd_fused_sm100_kernel");
