@@ -68,12 +68,15 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
   __shared__ int s_cnt[kBins][kPlanWarps];  // counts, then cursors
   __shared__ int s_wsum[kPlanWarps];
   __shared__ unsigned long long s_total;
+  __shared__ int s_wmin, s_wmax;
   __shared__ int s_slots, s_nsplit, s_entries;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nthr = blockDim.x;
   for (int b = tid; b < kBins * kPlanWarps; b += nthr) (&s_cnt[0][0])[b] = 0;
   if (tid == 0) {
     s_total = 0;
+    s_wmin = 0x7fffffff;
+    s_wmax = 0;
     s_slots = 0;
     s_nsplit = 0;
     s_entries = 0;
@@ -95,11 +98,46 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
   if (lane == 0) atomicAdd(&s_total, tot);
+  {  // weight range: with every weight equal the sort is the identity
+    int wmin = 0x7fffffff, wmax = 0;
+#pragma unroll
+    for (int k = 0; k < kRegItems; ++k)
+      if (a.skip + tid + k * nthr < a.items) {
+        wmin = min(wmin, wreg[k]);
+        wmax = max(wmax, wreg[k]);
+      }
+    for (int i = a.skip + tid + kRegItems * nthr; i < a.items; i += nthr) {
+      wmin = min(wmin, a.weights[i]);
+      wmax = max(wmax, a.weights[i]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      wmin = min(wmin, __shfl_xor_sync(0xffffffffu, wmin, o));
+      wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+    }
+    if (lane == 0) {
+      atomicMin(&s_wmin, wmin);
+      atomicMax(&s_wmax, wmax);
+    }
+  }
   __syncthreads();
   int T = 0x7fffffff;
   if (a.kind == kPlanDkdv) {
     const unsigned long long t = (s_total + a.ctas - 1) / (unsigned long long)a.ctas;
     T = (int)max((unsigned long long)kMinSplit, t);
+  }
+  // All weights equal and none to split (very sparse lists: every item one key tile): the
+  // heaviest-first order is the index order, so the queue is left unwritten and the kernels
+  // hand out items skip + k directly; the sort's latency would otherwise sit in front of the
+  // consumers' second fetch.
+  if (s_wmin == s_wmax && s_wmax <= T) {
+    if (tid == 0) {
+      a.plan.header->counter = 0;
+      a.plan.header->n_entries = a.items > a.skip ? a.items - a.skip : 0;
+      a.plan.header->n_split = 0;
+      a.plan.header->natural = 1;
+    }
+    return;
   }
   auto chunks_of = [&](int w) { return w > T ? (w + T - 1) / T : 1; };
   auto bin_of = [&](int w, int chunks) { return weight_bin((w + chunks - 1) / chunks); };
@@ -172,6 +210,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     a.plan.header->counter = 0;
     a.plan.header->n_entries = s_entries;
     a.plan.header->n_split = s_nsplit;
+    a.plan.header->natural = 0;
   }
 }
 

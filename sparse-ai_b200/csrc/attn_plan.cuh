@@ -34,7 +34,7 @@ struct PlanHeader {
   int counter;    // next entry to hand out (atomic)
   int n_entries;
   int n_split;
-  int pad;
+  int natural;    // 1: no queue was written, entry k is item skip + k (all weights equal)
 };
 
 // Bytes of planner workspace for `items` items and `ctas` persistent CTAs.  Split chunks need

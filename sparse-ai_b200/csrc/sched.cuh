@@ -50,7 +50,14 @@ struct WorkFetcher {
         waited = true;
       }
       const int idx = atomicAdd(&s->header->counter, 1);
-      e_next = idx < s->header->n_entries ? s->queue[idx] : no_work();
+      if (idx >= s->header->n_entries) {
+        e_next = no_work();
+      } else if (s->header->natural) {  // the planner found the index order heaviest-first
+        const int64_t item = (s->first_static ? (int64_t)gridDim.x : 0) + idx;
+        e_next = WorkEntry{(int)item, 0, weight(item), -1};
+      } else {
+        e_next = s->queue[idx];
+      }
     } else {
       const int64_t idx = (int64_t)blockIdx.x + (int64_t)w * gridDim.x;
       e_next = idx < s->items ? WorkEntry{(int)idx, 0, weight(idx), -1} : no_work();
