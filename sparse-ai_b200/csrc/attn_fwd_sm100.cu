@@ -310,7 +310,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         uint32_t u;
         int ks, hk, z;
       };
-      PendV pq[3];
+      // pending V loads, oldest first, as three named slots (an array indexed by a runtime
+      // count would live on the stack)
+      PendV pq0{}, pq1{}, pq2{};
       int pq_n = 0;
       auto load_v = [&](const PendV& pv) -> bool {
         const uint32_t st = pv.u & 1, ph = (pv.u >> 1) & 1;
@@ -321,6 +323,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
                       &bars[B_VFULL0 + st], c * 64, pv.ks, pv.hk, pv.z);
         mbar_arrive(&bars[B_KEYEMPTY0 + pv.u % kKeyRing]);  // the tile's key slot is done
         return true;
+      };
+      auto flush_v = [&]() -> bool {
+        bool good = true;
+        if (pq_n > 0 && good) good = load_v(pq0);
+        if (pq_n > 1 && good) good = load_v(pq1);
+        if (pq_n > 2 && good) good = load_v(pq2);
+        pq_n = 0;
+        return good;
       };
       for (uint32_t w = 0; ok; ++w) {
         WorkEntry e;
@@ -335,8 +345,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         if (e.item < 0) break;
         const int n = e.end - e.begin;
         if (n == 0) continue;
-        for (int i = 0; i < pq_n && ok; ++i) ok = load_v(pq[i]);
-        pq_n = 0;
+        ok = flush_v();
         if (!ok) break;
         ok = mbar_wait(&bars[B_QEMPTY], (jq & 1) ^ 1, a.status);
         if (!ok) break;
@@ -357,17 +366,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           for (int c = 0; c < D / 64; ++c)
             tma_load_4d(sm + L::kK0 + st * L::kTileBytes + c * kT * 128, &a.tm_k,
                         &bars[B_KFULL0 + st], c * 64, ks, ip.hk, ip.z);
-          pq[pq_n++] = PendV{u, ks, ip.hk, ip.z};
-          if (pq_n == 3) {
-            ok = load_v(pq[0]);
-            pq[0] = pq[1];
-            pq[1] = pq[2];
+          const PendV nv{u, ks, ip.hk, ip.z};
+          if (pq_n == 0) pq0 = nv;
+          else if (pq_n == 1) pq1 = nv;
+          else pq2 = nv;
+          if (++pq_n == 3) {
+            ok = load_v(pq0);
+            pq0 = pq1;
+            pq1 = pq2;
             pq_n = 2;
           }
         }
         kv += n;
       }
-      for (int i = 0; i < pq_n && ok; ++i) ok = load_v(pq[i]);
+      if (ok) ok = flush_v();
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
@@ -375,21 +387,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       constexpr uint32_t idesc_qk = idesc_f16(kT, kT, BF16, false, false);
       constexpr uint32_t idesc_pv = idesc_f16(kT, D, BF16, false, true);
       const uint32_t q_addr = smem_u32(sm + L::kQ);
-      uint32_t kv = 0, jq = 0, n_multi = 0, n_solo[2] = {0, 0};
-      uint32_t sq[2] = {0, 0}, pv[2] = {0, 0};
+      // Per-group counters as scalar pairs selected by g (a two-element array indexed by a
+      // runtime g would live on the stack: local loads on the issue path).
+      uint32_t kv = 0, jq = 0, n_multi = 0, n_solo0 = 0, n_solo1 = 0;
+      uint32_t sq0 = 0, sq1 = 0, pv0 = 0, pv1 = 0;
       // O[g] is free for a new item once the readers of its last item are done: that item's
       // epilogue barrier and phase (EPI for items of >= 2 tiles, EPI1[g] for one-tile items)
-      int guard_bar[2] = {-1, -1};
-      uint32_t guard_ph[2] = {0, 0};
+      int guard_bar0 = -1, guard_bar1 = -1;
+      uint32_t guard_ph0 = 0, guard_ph1 = 0;
       bool ok = true;
       // PV of tile u into O[g]; the group's first PV of an item (first_of_g) waits for O[g]'s
       // guard and, unless O[g] was seeded, starts it afresh
       auto issue_pv = [&](uint32_t u, int g, bool first_of_g, bool seeded) -> bool {
         const uint32_t st = u & 1, ph = (u >> 1) & 1;
-        if (first_of_g && guard_bar[g] >= 0 &&
-            !mbar_wait(&bars[guard_bar[g]], guard_ph[g] & 1, a.status))
-          return false;
-        if (!mbar_wait(&bars[B_PFULL0 + g], pv[g] & 1, a.status)) return false;
+        const int gbar = g ? guard_bar1 : guard_bar0;
+        const uint32_t gph = g ? guard_ph1 : guard_ph0;
+        if (first_of_g && gbar >= 0 && !mbar_wait(&bars[gbar], gph & 1, a.status)) return false;
+        if (!mbar_wait(&bars[B_PFULL0 + g], (g ? pv1 : pv0) & 1, a.status)) return false;
         if (!mbar_wait(&bars[B_VFULL0 + st], ph, a.status)) return false;
         tc_fence_after();
         const uint32_t p_addr = smem_u32(sm + L::kP0 + g * L::kPBytes);
@@ -403,7 +417,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         }
         tc_commit(&bars[B_ODONE0 + g]);
         tc_commit(&bars[B_VEMPTY0 + st]);
-        ++pv[g];
+        if (g) ++pv1; else ++pv0;
         return true;
       };
       // A one-tile item's PV waits until the next item's first QK is issued, so that runs of
@@ -416,8 +430,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         if (!pend) return true;
         pend = false;
         if (!issue_pv(pend_u, pend_g, true, a.accumulate != 0)) return false;
-        guard_bar[pend_g] = B_EPI1_0 + pend_g;
-        guard_ph[pend_g] = n_solo[pend_g]++;
+        if (pend_g) {
+          guard_bar1 = B_EPI1_0 + 1;
+          guard_ph1 = n_solo1++;
+        } else {
+          guard_bar0 = B_EPI1_0;
+          guard_ph0 = n_solo0++;
+        }
         return true;
       };
       for (uint32_t w = 0; ok; ++w) {
@@ -435,7 +454,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           const uint32_t u = kv + t, g = (gb + t) & 1;
           const uint32_t st = u & 1, ph = (u >> 1) & 1;
           ok = mbar_wait(&bars[B_KFULL0 + st], ph, a.status) &&
-               mbar_wait(&bars[B_SEMPTY0 + g], (sq[g] & 1) ^ 1, a.status);
+               mbar_wait(&bars[B_SEMPTY0 + g], ((g ? sq1 : sq0) & 1) ^ 1, a.status);
           if (!ok) break;
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sm + L::kK0 + st * L::kTileBytes);
@@ -448,7 +467,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           tc_commit(&bars[B_SFULL0 + g]);
           tc_commit(&bars[B_KEMPTY0 + st]);
           if (t == n_sub - 1) tc_commit(&bars[B_QEMPTY]);
-          ++sq[g];
+          if (g) ++sq1; else ++sq0;
           if (t == 0) ok = issue_pending();
           // after the QKs of pair (t-1, t): the PVs of the previous pair, so that both groups
           // run the same code in step (one instruction-cache footprint) and find the next S ready
@@ -464,8 +483,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         } else {
           for (; pv_next < n_sub && ok; ++pv_next)
             ok = issue_pv(kv + pv_next, (gb + pv_next) & 1, pv_next < 2, a.accumulate && pv_next == 0);
-          guard_bar[0] = guard_bar[1] = B_EPI;
-          guard_ph[0] = guard_ph[1] = n_multi++;
+          guard_bar0 = guard_bar1 = B_EPI;
+          guard_ph0 = guard_ph1 = n_multi++;
         }
         kv += n_sub;
       }
