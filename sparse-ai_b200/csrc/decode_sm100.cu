@@ -31,7 +31,8 @@
 //     products are < 1 % of the tensor pipe at HBM speed, so the warp-level MMA is enough;
 //     what matters is that the ring keeps ~200 KB of loads in flight per SM.
 //  4. decode_unit_combine_kernel, one CTA per unit: merges the unit's chunk partials by
-//     log-sum-exp weights and writes its G output rows.
+//     log-sum-exp weights (spread over kMaxG / G thread groups, then folded through shared
+//     memory) and writes its G output rows.
 #include <algorithm>
 #include <string>
 #include <type_traits>
@@ -783,13 +784,22 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // Up to kDescs - 1 descriptors ahead of the producer, so that runs of one-page chunks do
     // not wait on the queue's atomic -> table -> list chain.  CTA x takes chunk x first; the
     // queue counter hands out the rest from chunk gridDim.x on.
+    // Near the queue's end (fewer than two chunks per CTA left) the lookahead shrinks to one:
+    // the next chunk is reserved only once the producer has issued the previous one's loads,
+    // so that the last chunks spread over the CTAs instead of waiting in one CTA's ring while
+    // the others go idle.
     const int n_chunks = __ldcg(&a.w.hdr->n_chunks);
+    int last_c = 0;
     for (uint32_t d = 0;; ++d) {
       const uint32_t ds = d % kDescs;
       if (!mbar_wait_warp(&dempty[ds], ((d / kDescs) & 1) ^ 1, a.status)) break;
+      if (d > 0 && n_chunks - last_c < 2 * (int)gridDim.x &&
+          !mbar_wait_warp(&dempty[(d - 1) % kDescs], ((d - 1) / kDescs) & 1, a.status))
+        break;
       int c = 0;
       if (lane == 0) c = d == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(&a.w.hdr->next, 1);
       c = __shfl_sync(0xffffffffu, c, 0);
+      last_c = c;
       ChunkDesc& cd = desc[ds];
       if (c >= n_chunks) {
         if (lane == 0) {
@@ -851,36 +861,45 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 // ---------------------------------------------------------------------------------------
 // 4. per-unit merge of the chunk partials (a programmatic dependent of the stream kernel)
 // ---------------------------------------------------------------------------------------
-// One CTA per unit, one thread per float4 output column of the unit's G heads; the chunks
-// are merged online with eight chunks' loads in flight.
+// One CTA per unit.  Its kMaxG * D / 4 threads are CG = kMaxG / G groups of one thread per
+// float4 output column of the unit's G heads; group c merges the unit's chunks c, c + CG, ...
+// online (eight chunks' loads in flight, one round for most units), then the CG partial
+// states are merged through shared memory.  A unit's long chunk list thus costs one round
+// of loads instead of a chain of them.
 template <typename T, int D>
 __global__ void __launch_bounds__(kMaxG * D / 4) decode_unit_combine_kernel(const FastWs w, void* out_,
                                                                           int64_t os0, int64_t os1,
                                                                           int64_t Hkv, int G) {
   constexpr int RS = D + 4;
+  constexpr int kThreads = kMaxG * D / 4;
+  __shared__ float4 s_acc[kThreads];
+  __shared__ float2 s_ml[kThreads];
   pdl_wait();
   const int64_t bg = blockIdx.x;
+  const int per_unit = G * (D / 4);
+  const int CG = (int)blockDim.x / per_unit;
+  const int cg = (int)threadIdx.x / per_unit, i = (int)threadIdx.x % per_unit;
   const int2 ui = w.uinfo[bg];
-  const int i = threadIdx.x;
-  if (ui.y == 0 || i >= G * (D / 4)) return;  // a unit without pages was zeroed at selection
+  if (ui.y == 0) return;  // (CTA-uniform) a unit without pages was zeroed at selection
   const int hh = i / (D / 4), d4 = i % (D / 4);
   const float* ph = w.part + (int64_t)ui.x * G * RS + hh * RS;
   const int64_t CS = (int64_t)G * RS;
   float M = -INFINITY, L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   constexpr int NU = 8;
-  for (int k0 = 0; k0 < ui.y; k0 += NU) {
+  const int mine = cg < ui.y ? (ui.y - cg + CG - 1) / CG : 0;  // chunks cg, cg + CG, ...
+  for (int k0 = 0; k0 < mine; k0 += NU) {
     float2 ml[NU];
     float4 x[NU];
 #pragma unroll
     for (int u = 0; u < NU; ++u) {
-      const int k = min(k0 + u, ui.y - 1);
+      const int k = cg + CG * min(k0 + u, mine - 1);
       ml[u] = __ldcg(reinterpret_cast<const float2*>(ph + k * CS));
       x[u] = __ldcg(reinterpret_cast<const float4*>(ph + k * CS + 4 + 4 * d4));
     }
 #pragma unroll
     for (int u = 0; u < NU; ++u) {
-      if (k0 + u >= ui.y) break;
+      if (k0 + u >= mine) break;
       const float mn = fmaxf(M, ml[u].x);
       const float ref = mn == -INFINITY ? 0.f : mn;
       const float so = fast_exp2(M - ref), sn = fast_exp2(ml[u].x - ref);
@@ -891,6 +910,25 @@ __global__ void __launch_bounds__(kMaxG * D / 4) decode_unit_combine_kernel(cons
       L = L * so + ml[u].y * sn;
       M = mn;
     }
+  }
+  if (threadIdx.x < (unsigned)(CG * per_unit)) {
+    s_acc[threadIdx.x] = acc;
+    s_ml[threadIdx.x] = make_float2(M, L);
+  }
+  __syncthreads();
+  if (cg != 0) return;
+  for (int c = 1; c < CG; ++c) {  // group 0 folds in the other groups' states
+    const float2 ml = s_ml[c * per_unit + i];
+    const float4 x = s_acc[c * per_unit + i];
+    const float mn = fmaxf(M, ml.x);
+    const float ref = mn == -INFINITY ? 0.f : mn;
+    const float so = fast_exp2(M - ref), sn = fast_exp2(ml.x - ref);
+    acc.x = acc.x * so + x.x * sn;
+    acc.y = acc.y * so + x.y * sn;
+    acc.z = acc.z * so + x.z * sn;
+    acc.w = acc.w * so + x.w * sn;
+    L = L * so + ml.y * sn;
+    M = mn;
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
   const int64_t b = bg / Hkv, g = bg % Hkv;
@@ -994,7 +1032,8 @@ int launch_decode_fast(const DecodeParams& p, int dtype, void* workspace, int64_
   else
     rc = bf ? launch_stream<128, true>(a, grid, stream) : launch_stream<128, false>(a, grid, stream);
   if (rc) return rc;
-  const dim3 cg((unsigned)BG), cb((unsigned)(p.G * p.D / 4));
+  // one CTA per unit: kMaxG / G chunk groups of G * D / 4 threads (<= kMaxG * D / 4)
+  const dim3 cg((unsigned)BG), cb((unsigned)((kMaxG / p.G) * p.G * p.D / 4));
   const char* cn = "decode_unit_combine_kernel";
   if (p.D == 64)
     return bf ? launch_dependent(decode_unit_combine_kernel<__nv_bfloat16, 64>, cg, cb, 0, stream, cn, w,
