@@ -352,10 +352,10 @@ class C2Problem:
             f"bwd phase {phase}")
 
     # our kernels per part.  fwd: planner + kernel.  Fused path -- prep: Delta (+ zeroing of
-    # the dQ accumulator), transposed lists, dK/dV planner; bwd: fused kernel + split reduce.
-    # Two-kernel path -- prep: Delta, transposed lists, planner; dq: planner + kernel; dkdv:
-    # kernel + split reduce.
-    LAUNCHES = {"build": 1, "fwd": 2, "prep": 3, "bwd": 2, "dq": 2, "dkdv": 2}
+    # the dQ accumulator), transposed lists, dK/dV planner; bwd: fused kernel + split reduce +
+    # dQ conversion.  Two-kernel path -- prep: Delta, transposed lists, planner; dq: planner +
+    # kernel; dkdv: kernel + split reduce.
+    LAUNCHES = {"build": 1, "fwd": 2, "prep": 3, "bwd": 3, "dq": 2, "dkdv": 2}
 
     def launches(self):
         return sum(self.LAUNCHES[p] for p in self.parts)
