@@ -10,12 +10,12 @@
 // A "unit" is one (request b, KV head g), bg = b * Hkv + g.  Four kernels, the last three
 // launched as programmatic dependents of the one before (their prologues overlap it):
 //
-//  1. decode_init_kernel: zeroes the work header (selection ticket, queue counter).
+//  1. decode_init_kernel: zeroes the work header (selection count, queue counter).
 //  2. decode_select_kernel, one CTA per (request, part of its logical pages): one pass over
 //     the part's pages (a warp per 8 pages; each page's [H][TD] routing block read as
 //     coalesced 128-byte runs) writes, per KV head, the ascending list of the part's pages
 //     selected by ANY query head of the group as {physical page, head mask | valid tokens
-//     << 16}.  The last CTA to finish (atomic ticket) cuts every list into chunks of `chp`
+//     << 16}.  The last CTA to finish (one 64-bit atomic) cuts every list into chunks of `chp`
 //     pages, chp chosen so that the batch has about kChunkTarget chunks whatever the spread
 //     of context lengths, writes the chunk table, and zeroes the output rows of units that
 //     attend no page.
@@ -62,13 +62,14 @@ constexpr int kMaxStages = 8;
 constexpr int kQBufs = 4;   // query buffers: the producer may run 3 chunks ahead of the consumers
 constexpr int kDescs = 4;   // chunk descriptors: the scheduler reserves up to 3 chunks ahead
 constexpr int kFirst = 1, kLast = 2, kEnd = 4;
+constexpr int kTickShift = 40;  // DecHeader::total: CTA count above, pair count below
 
 struct DecHeader {
-  unsigned ticket;  // CTAs of the select kernel that finished
+  unsigned spare;
   int n_chunks;
   int chp;          // pages per chunk
   int next;         // queue counter of the stream kernel
-  unsigned long long total;  // selected (unit, page) pairs, summed by the select CTAs
+  unsigned long long total;  // select CTAs finished << kTickShift | selected (unit, page) pairs
   int pad[58];
 };
 static_assert(sizeof(DecHeader) == 256, "DecHeader");
@@ -158,7 +159,6 @@ size_t carve(void* base, int64_t B, int64_t Hkv, int64_t maxL, int64_t G, int64_
 // ---------------------------------------------------------------------------------------
 __global__ void decode_init_kernel(DecHeader* hdr) {
   pdl_trigger();
-  hdr->ticket = 0;
   hdr->next = 0;
   hdr->total = 0;
 }
@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(kSelThreads, 2) decode_select_kernel(const Dec
   __shared__ int s_warp[kSelWarps];
   __shared__ long long s_sum[kSelWarps];
   __shared__ int s_last;
+  __shared__ long long s_total;
   const int64_t ctx = p.ctx[b];
   // Lanes run over the (head, level < r) pairs that are compared, KK words per lane and PP
   // pages per step: the loads of one step (PP * KK per lane) are all in flight together.
@@ -341,7 +342,7 @@ __global__ void __launch_bounds__(kSelThreads, 2) decode_select_kernel(const Dec
   for (int o = 16; o; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
   if (lane == 0) s_sum[warp] = mine;
 
-  // The CTA adds its selected pairs to the header's total, then takes a ticket; the last CTA
+  // The CTA adds its selected pairs and itself to the header's count; the last CTA
   // to finish cuts the lists into chunks (the header was zeroed by the init kernel, which
   // must have completed).
   pdl_wait();
@@ -350,25 +351,37 @@ __global__ void __launch_bounds__(kSelThreads, 2) decode_select_kernel(const Dec
   if (tid == 0) {
     long long cta = 0;
     for (int i = 0; i < kSelWarps; ++i) cta += s_sum[i];
-    if (cta) atomicAdd(&w.hdr->total, (unsigned long long)cta);
-    __threadfence();
-    s_last = atomicAdd(&w.hdr->ticket, 1u) == gridDim.x * gridDim.y - 1;
+    // one atomic: CTAs finished in the top 24 bits, selected pairs in the low 40, so the CTA
+    // that finishes last learns so, and the complete total, from the value it replaced
+    const unsigned long long old =
+        atomicAdd(&w.hdr->total, (1ull << kTickShift) | (unsigned long long)cta);
+    s_last = (old >> kTickShift) == gridDim.x * gridDim.y - 1;
+    s_total = (long long)(old & ((1ull << kTickShift) - 1ull)) + cta;
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   const int64_t BG = p.B * p.Hkv;
   const int P = w.P;
-  const long long total = (long long)__ldcg(&w.hdr->total);
+  // each round's loads of the next round's part lengths go out before its scan: one
+  // dependent round trip instead of one per round
+  const long long total = s_total;
+  int cnt_next[kMaxParts];
+#pragma unroll
+  for (int q = 0; q < kMaxParts; ++q) cnt_next[q] = tid < BG && q < P ? __ldcg(w.count + (int64_t)tid * P + q) : 0;
   int chp = (int)std::max<long long>(ppt, (total + kChunkTarget - 1) / kChunkTarget);
   chp = (chp + ppt - 1) / ppt * ppt;
   int run = 0;
   uint16_t* out = static_cast<uint16_t*>(p.out);
   for (int64_t i0 = 0; i0 < BG; i0 += kSelThreads) {
     const int64_t i = i0 + tid;
-    int cnt[kMaxParts];  // this unit's part lengths, loaded once
+    int cnt[kMaxParts];  // this unit's part lengths
 #pragma unroll
-    for (int q = 0; q < kMaxParts; ++q) cnt[q] = i < BG && q < P ? __ldcg(w.count + i * P + q) : 0;
+    for (int q = 0; q < kMaxParts; ++q) cnt[q] = cnt_next[q];
+    const int64_t inext = i + kSelThreads;
+#pragma unroll
+    for (int q = 0; q < kMaxParts; ++q)
+      cnt_next[q] = inext < BG && q < P ? __ldcg(w.count + inext * P + q) : 0;
     int cu_tot = 0;
 #pragma unroll
     for (int q = 0; q < kMaxParts; ++q) cu_tot += cnt[q];
