@@ -14,15 +14,15 @@
 //   warp 8      TMA producer: Q tile once per work item, K tiles into a 2-stage ring and V
 //               tiles into another, V running two tiles behind K within an item (the order in
 //               which the MMA frees the stages); it never touches global memory itself.
-//   warp 9      TMEM owner + single-thread tcgen05.mma issuer:
-//                 S[g] = Q K_t^T    (M=128, N=128, K=D; fp32 in TMEM)
-//                 O[g] += P_t V_t   (M=128, N=D,   K=128; fp32 in TMEM)
+//   warp 9      TMEM owner + QK issuer (one thread): S[g] = Q K_t^T (M=128, N=128, K=D; fp32
+//               in TMEM), every key tile in order as soon as its K stage and S[g] are free.
+//   warp 11     PV issuer (one thread): O[g] += P_t V_t (M=128, N=D, K=128; fp32 in TMEM), every
+//               key tile in order as soon as the group's P and the tile's V are in shared
+//               memory.  A thread issuing tcgen05.mma is held at each issue while the tensor
+//               pipe is busy; with both kinds on one thread the pipe idled through every wait,
+//               fence and commit between its MMA blocks (~45 % of each tile pair, traced).
 //               Key tiles alternate between the two softmax groups (g = running tile index
-//               mod 2, across items).  Tiles go in pairs: the QKs of pair p+1 are issued
-//               before the PVs of pair p, so each group finds its next S computed, and the
-//               two groups run the same code at the same time (one instruction-cache
-//               footprint).  A one-tile item's PV waits until the next item's first QK, so
-//               runs of one-tile items (very sparse lists) keep both groups busy.
+//               mod 2, across items).
 //   warps 0-7   two softmax groups of 4 warps, each with its own running max / sum and O[g].
 //               Thread = query row (TMEM lane); tcgen05.ld of S, masking (-inf in place),
 //               row max, exp2, P (bf16/fp16) into the group's shared-memory P buffer in the
@@ -32,7 +32,6 @@
 //               shared memory and each merges O[0] and O[1] for half of the head dim; of a
 //               one-tile item: its owner alone.  O / l is staged (128B swizzle) in the P
 //               buffer and written by TMA tile stores; LSE.
-//   warp 11     idle (it completes the control warpgroup for setmaxnreg).
 // Work item = (query tile of 128 rows, z, h).  With a planner workspace the items come
 // heaviest-first from the device-built queue (one atomic per item); without one, round-robin
 // with late (heavier, under causal masking) query tiles first.
@@ -46,7 +45,7 @@ namespace {
 
 constexpr int kT = 128;           // rows of a query tile and of a key tile
 constexpr int kFwdThreads = 384;  // 12 warps
-constexpr int kProducerWarp = 8, kMmaWarp = 9, kSchedWarp = 10;
+constexpr int kProducerWarp = 8, kMmaWarp = 9, kSchedWarp = 10, kPvWarp = 11;
 // Register split: the launch gives every thread kLaunchRegs; the control warpgroup (warps
 // 8-11) drops to kCtrlRegs and the two softmax warpgroups take what it frees.
 constexpr int kLaunchRegs = 168, kCtrlRegs = 72, kSoftmaxRegs = 216;
@@ -213,7 +212,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     }
     for (int i = 0; i < kRing; ++i) {
       mbar_init(&bars[B_WFULL0 + i], 1);
-      mbar_init(&bars[B_WEMPTY0 + i], 2 + 2 * kGroupThreads);  // producer, MMA thread, both groups
+      mbar_init(&bars[B_WEMPTY0 + i], 3 + 2 * kGroupThreads);  // producer, QK and PV issuers, both groups
     }
     fence_mbar_init();
   }
@@ -382,63 +381,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       if (ok) ok = flush_v();
     }
   } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------------ QK issuer
+    // S[g] = Q K^T for every key tile, in order.  The PVs have their own issuing thread
+    // (warp kPvWarp): a thread that issues tcgen05.mma is held at each issue while the tensor
+    // pipe is busy, so one thread issuing both would leave the pipe idle through every wait,
+    // fence and commit between its MMA blocks.  The two threads' MMAs touch disjoint TMEM
+    // (S[g] and O[g]) and meet only through the mbarriers below.
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(kT, kT, BF16, false, false);
-      constexpr uint32_t idesc_pv = idesc_f16(kT, D, BF16, false, true);
-      const uint32_t q_addr = smem_u32(sm + L::kQ);
-      // Per-group counters as scalar pairs selected by g (a two-element array indexed by a
-      // runtime g would live on the stack: local loads on the issue path).
-      uint32_t kv = 0, jq = 0, n_multi = 0, n_solo0 = 0, n_solo1 = 0;
-      uint32_t sq0 = 0, sq1 = 0, pv0 = 0, pv1 = 0;
-      // O[g] is free for a new item once the readers of its last item are done: that item's
-      // epilogue barrier and phase (EPI for items of >= 2 tiles, EPI1[g] for one-tile items)
-      int guard_bar0 = -1, guard_bar1 = -1;
-      uint32_t guard_ph0 = 0, guard_ph1 = 0;
+      const uint64_t qd = smem_desc(smem_u32(sm + L::kQ), 16, 1024);
+      uint32_t kv = 0, jq = 0, sq0 = 0, sq1 = 0;
       bool ok = true;
-      // PV of tile u into O[g]; the group's first PV of an item (first_of_g) waits for O[g]'s
-      // guard and, unless O[g] was seeded, starts it afresh
-      auto issue_pv = [&](uint32_t u, int g, bool first_of_g, bool seeded) -> bool {
-        const uint32_t st = u & 1, ph = (u >> 1) & 1;
-        const int gbar = g ? guard_bar1 : guard_bar0;
-        const uint32_t gph = g ? guard_ph1 : guard_ph0;
-        if (first_of_g && gbar >= 0 && !mbar_wait(&bars[gbar], gph & 1, a.status)) return false;
-        if (!mbar_wait(&bars[B_PFULL0 + g], (g ? pv1 : pv0) & 1, a.status)) return false;
-        if (!mbar_wait(&bars[B_VFULL0 + st], ph, a.status)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(sm + L::kP0 + g * L::kPBytes);
-        const uint32_t v_addr = smem_u32(sm + L::kV0 + st * L::kTileBytes);
-        const bool first = first_of_g && !seeded;
-#pragma unroll
-        for (int kk = 0; kk < kT / 16; ++kk) {
-          const uint64_t ad = smem_desc(p_addr + (kk >> 2) * (kT * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc(v_addr + kk * 16 * 128, kT * 128, 1024);
-          tc_mma_f16(tmem + kColO + g * D, ad, bd, idesc_pv, (!first || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(&bars[B_ODONE0 + g]);
-        tc_commit(&bars[B_VEMPTY0 + st]);
-        if (g) ++pv1; else ++pv0;
-        return true;
-      };
-      // A one-tile item's PV waits until the next item's first QK is issued, so that runs of
-      // one-tile items (owned by alternating groups) overlap their softmax.  Safe: a QK only
-      // needs its group to have started its previous tile, never a finished epilogue.
-      bool pend = false;
-      uint32_t pend_u = 0;
-      int pend_g = 0;
-      auto issue_pending = [&]() -> bool {
-        if (!pend) return true;
-        pend = false;
-        if (!issue_pv(pend_u, pend_g, true, a.accumulate != 0)) return false;
-        if (pend_g) {
-          guard_bar1 = B_EPI1_0 + 1;
-          guard_ph1 = n_solo1++;
-        } else {
-          guard_bar0 = B_EPI1_0;
-          guard_ph0 = n_solo0++;
-        }
-        return true;
-      };
       for (uint32_t w = 0; ok; ++w) {
         WorkEntry e;
         if (!(ok = ring_get(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
@@ -449,7 +402,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
         ++jq;
         if (!ok) break;
         const int gb = (int)(kv & 1);  // tile t goes to group (gb + t) & 1
-        int pv_next = 0;
         for (int t = 0; t < n_sub && ok; ++t) {
           const uint32_t u = kv + t, g = (gb + t) & 1;
           const uint32_t st = u & 1, ph = (u >> 1) & 1;
@@ -457,38 +409,81 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
                mbar_wait(&bars[B_SEMPTY0 + g], ((g ? sq1 : sq0) & 1) ^ 1, a.status);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t k_addr = smem_u32(sm + L::kK0 + st * L::kTileBytes);
+          const uint64_t kd = smem_desc(smem_u32(sm + L::kK0 + st * L::kTileBytes), 16, 1024);
+          const uint32_t d_s = tmem + kColS + g * kT;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
-            tc_mma_f16(tmem + kColS + g * kT, smem_desc(q_addr + off, 16, 1024),
-                       smem_desc(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+            tc_mma_f16(d_s, desc_add(qd, off), desc_add(kd, off), idesc_qk, kk > 0 ? 1u : 0u);
           }
           tc_commit(&bars[B_SFULL0 + g]);
           tc_commit(&bars[B_KEMPTY0 + st]);
           if (t == n_sub - 1) tc_commit(&bars[B_QEMPTY]);
           if (g) ++sq1; else ++sq0;
-          if (t == 0) ok = issue_pending();
-          // after the QKs of pair (t-1, t): the PVs of the previous pair, so that both groups
-          // run the same code in step (one instruction-cache footprint) and find the next S ready
-          if (t & 1)
-            for (; pv_next <= t - 2 && ok; ++pv_next)
-              ok = issue_pv(kv + pv_next, (gb + pv_next) & 1, pv_next < 2, a.accumulate && pv_next == 0);
+        }
+        kv += n_sub;
+      }
+    }
+  } else if (warp == kPvWarp) {
+    // ------------------------------------------------------------------ PV issuer
+    // O[g] += P[g] V for every key tile, in order, as soon as the group's P and the tile's V
+    // are in shared memory.
+    if (lane == 0) {
+      constexpr uint32_t idesc_pv = idesc_f16(kT, D, BF16, false, true);
+      uint32_t kv = 0, pv0 = 0, pv1 = 0, n_multi = 0, n_solo0 = 0, n_solo1 = 0;
+      // O[g] is free for a new item once the readers of its last item are done: that item's
+      // epilogue barrier and phase (EPI for items of >= 2 tiles, EPI1[g] for one-tile items)
+      int guard_bar0 = -1, guard_bar1 = -1;
+      uint32_t guard_ph0 = 0, guard_ph1 = 0;
+      bool ok = true;
+      for (uint32_t w = 0; ok; ++w) {
+        WorkEntry e;
+        if (!(ok = ring_get(ring, &bars[B_WFULL0], &bars[B_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const int n_sub = e.end - e.begin;
+        if (n_sub == 0) continue;
+        const int gb = (int)(kv & 1);
+        for (int t = 0; t < n_sub && ok; ++t) {
+          const uint32_t u = kv + t, g = (gb + t) & 1;
+          const uint32_t st = u & 1, ph = (u >> 1) & 1;
+          // the group's first PV of the item waits for O[g]'s guard and, unless O[g] was
+          // seeded with the previous output (accumulate mode, the first tile's group),
+          // starts it afresh
+          const bool first_of_g = t < 2, seeded = a.accumulate && t == 0;
+          const int gbar = g ? guard_bar1 : guard_bar0;
+          const uint32_t gph = g ? guard_ph1 : guard_ph0;
+          ok = (!first_of_g || gbar < 0 || mbar_wait(&bars[gbar], gph & 1, a.status)) &&
+               mbar_wait(&bars[B_PFULL0 + g], (g ? pv1 : pv0) & 1, a.status) &&
+               mbar_wait(&bars[B_VFULL0 + st], ph, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t pd = smem_desc(smem_u32(sm + L::kP0 + g * L::kPBytes), 16, 1024);
+          const uint64_t vd = smem_desc(smem_u32(sm + L::kV0 + st * L::kTileBytes), kT * 128, 1024);
+          const uint32_t d_o = tmem + kColO + g * D;
+          const bool first = first_of_g && !seeded;
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk)
+            tc_mma_f16(d_o, desc_add(pd, (kk >> 2) * (kT * 128) + (kk & 3) * 32),
+                       desc_add(vd, kk * 16 * 128), idesc_pv, (!first || kk > 0) ? 1u : 0u);
+          tc_commit(&bars[B_ODONE0 + g]);
+          tc_commit(&bars[B_VEMPTY0 + st]);
+          if (g) ++pv1; else ++pv0;
         }
         if (!ok) break;
         if (n_sub == 1) {
-          pend = true;
-          pend_u = kv;
-          pend_g = gb;
+          if (gb) {
+            guard_bar1 = B_EPI1_0 + 1;
+            guard_ph1 = n_solo1++;
+          } else {
+            guard_bar0 = B_EPI1_0;
+            guard_ph0 = n_solo0++;
+          }
         } else {
-          for (; pv_next < n_sub && ok; ++pv_next)
-            ok = issue_pv(kv + pv_next, (gb + pv_next) & 1, pv_next < 2, a.accumulate && pv_next == 0);
           guard_bar0 = guard_bar1 = B_EPI;
           guard_ph0 = guard_ph1 = n_multi++;
         }
         kv += n_sub;
       }
-      if (ok) ok = issue_pending();
     }
   }
   } else {
