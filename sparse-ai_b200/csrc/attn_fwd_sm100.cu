@@ -116,9 +116,9 @@ struct FwdLayout {
 // and to the owning softmax group (masking, bias) through a shared-memory ring, so that
 // neither reads the lists from global memory on its critical path.
 struct TileKey {
-  int64_t key_start;
-  float b2;  // soft-bias * log2(e) of the block pair
-  int pad;
+  int key_start;  // < N <= INT32_MAX (checked at launch)
+  float b2;       // soft-bias * log2(e) of the block pair
+  int hk, z;      // KV head and batch index of the tile's item
 };
 
 struct ItemInfo {
@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
             const uint32_t slot = kq % kKeyRing;
             ok = mbar_wait(&bars[B_KEYEMPTY0 + slot], ((kq / kKeyRing) & 1) ^ 1, a.status);
             if (ok) {
-              keys[slot] = TileKey{ks, b2, 0};
+              keys[slot] = TileKey{(int)ks, b2, (int)it.hk, (int)it.z};
               mbar_arrive(&bars[B_KEYFULL0 + slot]);
             }
           }
@@ -297,88 +297,86 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     }
   } else if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ TMA producer
+    // Three load channels, each in order, polled without blocking so that none holds up the
+    // others: Q once per work item (its slot frees when the item's last QK completes), K per
+    // key tile (its stage frees when QK of the tile two back completes) and V per key tile
+    // (when PV of the tile two back completes).  The PVs trail the QKs by a softmax pass, so a
+    // producer that waited for each V stage in turn delayed the next K loads and with them
+    // the QKs.  A key tile's start, KV head and batch index come from the scheduler's key
+    // ring; the slot is handed back after the tile's V load.
     if (lane == 0) {
-      uint32_t kv = 0, jq = 0;
-      bool ok = true;
-      // Within an item, V of tile u is loaded after K of tile u + 2 (the order in which the
-      // MMA frees the stages).  At the next item's start, before the wait for the Q slot, the
-      // item's pending V loads go out: the MMA needs them before (or, for a one-tile item,
-      // right after) the next item's first QK, and their stages were freed by PVs of earlier
-      // items.
-      struct PendV {
-        uint32_t u;
-        int ks, hk, z;
-      };
-      // pending V loads, oldest first, as three named slots (an array indexed by a runtime
-      // count would live on the stack)
-      PendV pq0{}, pq1{}, pq2{};
-      int pq_n = 0;
-      auto load_v = [&](const PendV& pv) -> bool {
-        const uint32_t st = pv.u & 1, ph = (pv.u >> 1) & 1;
-        if (!mbar_wait(&bars[B_VEMPTY0 + st], ph ^ 1, a.status)) return false;
-        mbar_arrive_expect_tx(&bars[B_VFULL0 + st], L::kTileBytes);
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sm + L::kV0 + st * L::kTileBytes + c * kT * 128, &a.tm_v,
-                      &bars[B_VFULL0 + st], c * 64, pv.ks, pv.hk, pv.z);
-        mbar_arrive(&bars[B_KEYEMPTY0 + pv.u % kKeyRing]);  // the tile's key slot is done
-        return true;
-      };
-      auto flush_v = [&]() -> bool {
-        bool good = true;
-        if (pq_n > 0 && good) good = load_v(pq0);
-        if (pq_n > 1 && good) good = load_v(pq1);
-        if (pq_n > 2 && good) good = load_v(pq2);
-        pq_n = 0;
-        return good;
-      };
-      for (uint32_t w = 0; ok; ++w) {
-        WorkEntry e;
-        ItemPos ip;
-        {
+      uint32_t w = 0, jq = 0, uk = 0, uv = 0, tiles = 0;
+      bool ended = false, ok = true;
+      // work items read whose Q is not loaded yet (at most two: a Q waits for the previous
+      // item's last QK, which waits for at most two K tiles beyond it)
+      ItemPos q0{}, q1{};
+      int nq = 0;
+      long long idle_since = clock64();
+      while (true) {
+        bool busy = false;
+        if (!ended && nq < 2) {
           const uint32_t slot = w % kRing;
-          if (!(ok = mbar_wait(&bars[B_WFULL0 + slot], (w / kRing) & 1, a.status))) break;
-          e = ring[slot];
-          ip = pos[slot];
-          mbar_arrive(&bars[B_WEMPTY0 + slot]);
-        }
-        if (e.item < 0) break;
-        const int n = e.end - e.begin;
-        if (n == 0) continue;
-        ok = flush_v();
-        if (!ok) break;
-        ok = mbar_wait(&bars[B_QEMPTY], (jq & 1) ^ 1, a.status);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&bars[B_QFULL], L::kTileBytes);
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sm + L::kQ + c * kT * 128, &a.tm_q, &bars[B_QFULL], c * 64, ip.q_start, ip.h,
-                      ip.z);
-        ++jq;
-        for (int i = 0; i < n && ok; ++i) {
-          const uint32_t u = kv + i, ks_slot = u % kKeyRing;
-          ok = mbar_wait(&bars[B_KEYFULL0 + ks_slot], (u / kKeyRing) & 1, a.status);
-          if (!ok) break;
-          const int ks = (int)keys[ks_slot].key_start;
-          const uint32_t st = u & 1, ph = (u >> 1) & 1;
-          ok = mbar_wait(&bars[B_KEMPTY0 + st], ph ^ 1, a.status);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&bars[B_KFULL0 + st], L::kTileBytes);
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_4d(sm + L::kK0 + st * L::kTileBytes + c * kT * 128, &a.tm_k,
-                        &bars[B_KFULL0 + st], c * 64, ks, ip.hk, ip.z);
-          const PendV nv{u, ks, ip.hk, ip.z};
-          if (pq_n == 0) pq0 = nv;
-          else if (pq_n == 1) pq1 = nv;
-          else pq2 = nv;
-          if (++pq_n == 3) {
-            ok = load_v(pq0);
-            pq0 = pq1;
-            pq1 = pq2;
-            pq_n = 2;
+          if (mbar_test(&bars[B_WFULL0 + slot], (w / kRing) & 1)) {
+            const WorkEntry e = ring[slot];
+            const ItemPos ip = pos[slot];
+            mbar_arrive(&bars[B_WEMPTY0 + slot]);
+            ++w;
+            if (e.item < 0) {
+              ended = true;
+            } else if (e.end > e.begin) {
+              tiles += (uint32_t)(e.end - e.begin);
+              if (nq == 0) q0 = ip;
+              else q1 = ip;
+              ++nq;
+            }
+            busy = true;
           }
         }
-        kv += n;
+        if (nq > 0 && mbar_test(&bars[B_QEMPTY], (jq & 1) ^ 1)) {
+          mbar_arrive_expect_tx(&bars[B_QFULL], L::kTileBytes);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(sm + L::kQ + c * kT * 128, &a.tm_q, &bars[B_QFULL], c * 64, q0.q_start, q0.h, q0.z);
+          q0 = q1;
+          --nq;
+          ++jq;
+          busy = true;
+        }
+        if (uk < tiles) {
+          const uint32_t ks_slot = uk % kKeyRing, st = uk & 1;
+          if (mbar_test(&bars[B_KEYFULL0 + ks_slot], (uk / kKeyRing) & 1) &&
+              mbar_test(&bars[B_KEMPTY0 + st], ((uk >> 1) & 1) ^ 1)) {
+            const TileKey k = keys[ks_slot];
+            mbar_arrive_expect_tx(&bars[B_KFULL0 + st], L::kTileBytes);
+            for (int c = 0; c < D / 64; ++c)
+              tma_load_4d(sm + L::kK0 + st * L::kTileBytes + c * kT * 128, &a.tm_k,
+                          &bars[B_KFULL0 + st], c * 64, k.key_start, k.hk, k.z);
+            ++uk;
+            busy = true;
+          }
+        }
+        if (uv < uk) {
+          const uint32_t ks_slot = uv % kKeyRing, st = uv & 1;
+          if (mbar_test(&bars[B_VEMPTY0 + st], ((uv >> 1) & 1) ^ 1)) {
+            const TileKey k = keys[ks_slot];
+            mbar_arrive_expect_tx(&bars[B_VFULL0 + st], L::kTileBytes);
+            for (int c = 0; c < D / 64; ++c)
+              tma_load_4d(sm + L::kV0 + st * L::kTileBytes + c * kT * 128, &a.tm_v,
+                          &bars[B_VFULL0 + st], c * 64, k.key_start, k.hk, k.z);
+            mbar_arrive(&bars[B_KEYEMPTY0 + ks_slot]);  // the tile's key slot is done
+            ++uv;
+            busy = true;
+          }
+        }
+        if (ended && nq == 0 && uv == tiles) break;
+        if (busy) {
+          idle_since = clock64();
+        } else if (clock64() - idle_since > (1ll << 31)) {
+          raise_status(a.status, kStatusWaitTimeout);
+          ok = false;
+          break;
+        }
       }
-      if (ok) ok = flush_v();
+      (void)ok;
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ QK issuer
