@@ -131,17 +131,21 @@ struct ItemPos {
   int z, h, hk, q_start;
 };
 
+// Item indices are int (WorkEntry), so the index arithmetic runs in 32 bits: the scheduler
+// decodes one item per work entry on its serial path, where 64-bit divisions cost hundreds of
+// cycles each.
 __device__ __forceinline__ ItemInfo item_info(const FwdArgs& a, int64_t item) {
   ItemInfo it;
-  const int64_t zh_total = a.Z * a.H;
-  const int64_t qt = a.QT - 1 - item / zh_total;
-  const int64_t zh = item % zh_total;
-  it.z = zh / a.H;
-  it.h = zh % a.H;
-  it.hk = it.h / (a.H / a.Hkv);
-  it.q_start = qt * kT;
-  it.qb = it.q_start / a.RB;
-  it.row_id = zh * a.NB + it.qb;
+  const uint32_t i = (uint32_t)item, zh_total = (uint32_t)(a.Z * a.H), H = (uint32_t)a.H;
+  const uint32_t qi = i / zh_total, zh = i - qi * zh_total;
+  const uint32_t qt = (uint32_t)a.QT - 1 - qi;
+  const uint32_t z = zh / H, h = zh - z * H;
+  it.z = z;
+  it.h = h;
+  it.hk = h / (H / (uint32_t)a.Hkv);
+  it.q_start = (int64_t)qt * kT;
+  it.qb = qt / (uint32_t)(a.RB / kT);
+  it.row_id = (int64_t)zh * a.NB + it.qb;
   return it;
 }
 
@@ -234,19 +238,50 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
       prefetch_tmap(&a.tm_k);
       prefetch_tmap(&a.tm_v);
     }
-    auto weight = [&](int64_t i) { return item_tiles(a, i); };
-    WorkFetcher fetch;
-    if (lane == 0) fetch.init(&a.sched, weight);
+    // Work entries: the CTA's first is item blockIdx.x (while the planner, this grid's
+    // programmatic prerequisite, orders the rest), then one queue atomic per entry -- or
+    // round-robin without a planner.  After a one-tile entry the atomic for the next one is
+    // issued before this entry's list is read and its key pushed, and resolved after them.
+    const SchedArgs& S = a.sched;
+    const bool dyn = S.header != nullptr;
+    int n_entries = 0, natural = 0;
+    bool planner_ready = !dyn || !S.first_static;
+    if (dyn && planner_ready && lane == 0) {
+      n_entries = S.header->n_entries;
+      natural = S.header->natural;
+    }
+    auto whole = [&](int64_t item) -> WorkEntry {
+      return item < S.items ? WorkEntry{(int)item, 0, item_tiles(a, item), -1} : no_work();
+    };
+    auto resolve = [&](int idx) -> WorkEntry {
+      if (idx >= n_entries) return no_work();
+      if (natural) return whole((S.first_static ? (int64_t)gridDim.x : 0) + idx);
+      return S.queue[idx];
+    };
+    WorkEntry e_next{};
+    if (lane == 0) {
+      if (!dyn || S.first_static) {
+        e_next = whole(blockIdx.x);
+      } else {
+        e_next = resolve(atomicAdd(&S.header->counter, 1));
+      }
+    }
     const int spb = (int)(a.RB / kT);  // key tiles per list entry
     uint32_t kq = 0;                   // key tiles pushed
     bool ok = true;
     for (uint32_t w = 0; ok; ++w) {
       WorkEntry e{};
-      if (lane == 0) e = fetch.next(weight);
-      e.item = __shfl_sync(0xffffffffu, e.item, 0);
-      e.begin = __shfl_sync(0xffffffffu, e.begin, 0);
-      e.end = __shfl_sync(0xffffffffu, e.end, 0);
-      e.slot = __shfl_sync(0xffffffffu, e.slot, 0);
+      e.item = __shfl_sync(0xffffffffu, e_next.item, 0);
+      e.begin = __shfl_sync(0xffffffffu, e_next.begin, 0);
+      e.end = __shfl_sync(0xffffffffu, e_next.end, 0);
+      e.slot = __shfl_sync(0xffffffffu, e_next.slot, 0);
+      // An entry of one key tile is over in about the scheduler's own serial latency per entry
+      // (atomic, index decode, list load): take the next entry's atomic now and use it after
+      // this entry's key.  Longer entries reserve after their keys as before: reserved any
+      // earlier, an entry sits unstarted while other CTAs may run dry (measured slower at C2).
+      const bool early = dyn && e.item >= 0 && planner_ready && e.end - e.begin <= 1;
+      int idx_next = 0;
+      if (lane == 0 && early) idx_next = atomicAdd(&S.header->counter, 1);
       ItemInfo it{};
       if (e.item >= 0) it = item_info(a, e.item);
       if (lane == 0) {
@@ -292,6 +327,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) break;
           ++kq;
+        }
+      }
+      if (lane == 0) {
+        if (!dyn) {
+          e_next = whole((int64_t)blockIdx.x + (int64_t)(w + 1) * gridDim.x);
+        } else if (early) {
+          e_next = resolve(idx_next);
+        } else if (planner_ready) {
+          e_next = resolve(atomicAdd(&S.header->counter, 1));
+        } else {
+          // after the first-wave item: the planner's queue and header are complete from here
+          pdl_wait();
+          planner_ready = true;
+          n_entries = S.header->n_entries;
+          natural = S.header->natural;
+          e_next = resolve(atomicAdd(&S.header->counter, 1));
         }
       }
     }
