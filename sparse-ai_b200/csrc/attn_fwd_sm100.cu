@@ -12,8 +12,8 @@
 //               and prefetches each item's Q tile into L2 (an L2 prefetch of every K/V tile as
 //               well measured slower: it shares the SM's TMA throughput with the loads).
 //   warp 8      TMA producer: Q tile once per work item, K tiles into a 2-stage ring and V
-//               tiles into another, V running two tiles behind K within an item (the order in
-//               which the MMA frees the stages); it never touches global memory itself.
+//               tiles into another, as three channels polled without blocking (each in order,
+//               none waiting behind another); it never touches global memory itself.
 //   warp 9      TMEM owner + QK issuer (one thread): S[g] = Q K_t^T (M=128, N=128, K=D; fp32
 //               in TMEM), every key tile in order as soon as its K stage and S[g] are free.
 //   warp 11     PV issuer (one thread): O[g] += P_t V_t (M=128, N=D, K=128; fp32 in TMEM), every
