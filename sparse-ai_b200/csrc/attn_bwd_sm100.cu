@@ -42,6 +42,10 @@ constexpr int kKvStages = 4;  // streamed ring depth (dK/dV kernel)
 constexpr int kEw = 8;                      // elementwise warps: 2 per TMEM lane quarter
 constexpr int kEwThreads = kEw * 32;
 constexpr int kBwdThreads = 64 + kEwThreads;
+// fused backward: producer (warp 0), A-block MMA issuer (warp 1), the two elementwise groups
+// (warps 2-9) and the B-block MMA issuer (warp 10)
+constexpr int kFuThreads = 96 + kEwThreads;
+constexpr int kFuBWarp = 2 + kEw;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 128, kColAcc = 256;  // S[2]: 0/64, dP[2]: 128/192
 
@@ -870,13 +874,14 @@ constexpr uint32_t kFuColDp = 128, kFuColDq = 192;  // TMEM: single dP^T and dQ^
 enum { FU_KVFULL = 0, FU_KVEMPTY, FU_QFULL0, FU_QEMPTY0 = FU_QFULL0 + kFuStages,
        FU_SFULL0 = FU_QEMPTY0 + kFuStages, FU_PFULL0 = FU_SFULL0 + 2, FU_DPFREE = FU_PFULL0 + 2,
        FU_DQFULL0, FU_DQEMPTY = FU_DQFULL0 + 2, FU_DONE, FU_EPI, FU_GSYNC0,
-       FU_WFULL0 = FU_GSYNC0 + 2, FU_WEMPTY0 = FU_WFULL0 + kRing, FU_NUM = FU_WEMPTY0 + kRing };
+       FU_SFREE0 = FU_GSYNC0 + 2, FU_WFULL0 = FU_SFREE0 + 2, FU_WEMPTY0 = FU_WFULL0 + kRing,
+       FU_NUM = FU_WEMPTY0 + kRing };
 static_assert(FU_NUM * 8 <= 256, "fused backward barriers");
 
 // BIAS_GRAD: the launch wants the soft-bias gradient (a.dbias).  A separate instantiation, so
 // that the kernel without it gets a register allocation free of the running dS sum.
 template <bool BF16, bool BIAS_GRAD>
-__global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const __grid_constant__ BwdArgs a) {
+__global__ void __launch_bounds__(kFuThreads, 1) bwd_fused_sm100_kernel(const __grid_constant__ BwdArgs a) {
   using L = FuLayout;
   constexpr int D = L::D;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -907,8 +912,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
     cnt[FU_DPFREE] = kEwThreads / 2;   // the sub-tile's group has read dP^T
     cnt[FU_DQEMPTY] = kEwThreads / 2;  // the sub-tile's group has read dQ^T
     cnt[FU_EPI] = kEwThreads;          // both groups have read the dV / dK accumulators
+    cnt[FU_KVEMPTY] = 2;               // both MMA issuers' last MMAs of the item completed
     // QEMPTY: one arrival, the owning group's leader once its dQ reduction read the stage
-    for (int i = 0; i < kRing; ++i) cnt[FU_WEMPTY0 + i] = 1 + kEwThreads;
+    for (int i = 0; i < kRing; ++i) cnt[FU_WEMPTY0 + i] = 2 + kEwThreads;  // both issuers, the groups
     init_bars(bars, cnt, FU_NUM);
   }
   if (warp == 1) {
@@ -980,17 +986,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
       }
     }
   } else if (warp == 1) {
+    // A blocks: S^T = K Q^T and dP^T = V dO^T of every sub-tile, in order.  The B blocks have
+    // their own issuing thread (warp kFuBWarp): a thread that issues tcgen05.mma is held at
+    // each issue while the tensor pipe is busy (~72-82 cycles per MMA here, traced), so one
+    // thread issuing both kinds left the pipe idle through every wait, fence and commit
+    // between its blocks (~54 % of each sub-tile).  The two threads meet only through
+    // mbarriers: A(j) writes S^T buffer j & 1, which B(j - 2) read (SFREE).
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16(kRows, kSub, BF16, false, false);
-      constexpr uint32_t id_acc = idesc_f16(kRows, D, BF16, false, true);
-      // dQ^T = K^T dS^T: A (head dim x keys) and B (keys x query rows) both MN-major
-      constexpr uint32_t id_dq = idesc_f16(kRows, kSub, BF16, true, true);
-      // base descriptors (K-major for S^T / dP^T, MN-major for dQ^T); per-MMA tiles by desc_add
+      // base descriptors (K-major for S^T / dP^T); per-MMA tiles by desc_add
       const uint64_t kd_k = smem_desc(smem_u32(sm + L::kK), 16, 1024);
       const uint64_t vd_k = smem_desc(smem_u32(sm + L::kV), 16, 1024);
-      const uint64_t kd_mn = smem_desc(smem_u32(sm + L::kK), kRows * 128, 1024);
-      const uint64_t dsd0_mn = smem_desc(smem_u32(sm + L::kDsT), kSub * 128, 1024);
-      uint32_t ga = 0, gb = 0, jk = 0, n_items = 0;  // sub-tiles with A / B issued (all items)
+      uint32_t ga = 0, jk = 0;  // sub-tiles with A issued (all items), K/V tiles
       bool ok = true;
       for (uint32_t w = 0; ok; ++w) {
         WorkEntry e;
@@ -1000,75 +1007,80 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_fused_sm100_kernel(const _
         if (n == 0) continue;
         if (!(ok = mbar_wait(&bars[FU_KVFULL], jk & 1, a.status))) break;
         ++jk;
-        int ia = 0, ib = 0;
-        long long idle_since = clock64();
-        while (ib < n) {
-          bool progressed = false;
-          // A: S^T / dP^T of sub-tile ga, S^T into buffer ga & 1.  That buffer is free once
-          // B(ga - 2) is issued (ia - ib < 2; MMAs execute in issue order), the dP^T buffer
-          // once sub-tile ga - 1's group has read it (DPFREE).
-          if (ia < n && ia - ib < 2) {
-            const uint32_t st = ga % kFuStages, ph = (ga / kFuStages) & 1, sb = ga & 1;
-            if ((ga == 0 || mbar_test(&bars[FU_DPFREE], (ga - 1) & 1)) &&
-                mbar_test(&bars[FU_QFULL0 + st], ph)) {
-              tc_fence_after();
-              const uint64_t qd_k = smem_desc(smem_u32(sm + L::kQD + st * L::kStage), 16, 1024);
-              const uint64_t dod_k = desc_add(qd_k, kSub * D * 2);
+        for (int i = 0; i < n && ok; ++i, ++ga) {
+          const uint32_t st = ga % kFuStages, ph = (ga / kFuStages) & 1, sb = ga & 1;
+          // the dP^T buffer once sub-tile ga - 1's group has read it, the S^T buffer once
+          // B(ga - 2) has completed, the sub-tile's Q / dO stage once loaded
+          ok = (ga == 0 || mbar_wait(&bars[FU_DPFREE], (ga - 1) & 1, a.status)) &&
+               (ga < 2 || mbar_wait(&bars[FU_SFREE0 + sb], ((ga - 2) >> 1) & 1, a.status)) &&
+               mbar_wait(&bars[FU_QFULL0 + st], ph, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t qd_k = smem_desc(smem_u32(sm + L::kQD + st * L::kStage), 16, 1024);
+          const uint64_t dod_k = desc_add(qd_k, kSub * D * 2);
 #pragma unroll
-              for (int kk = 0; kk < D / 16; ++kk) {
-                const uint32_t oa = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-                const uint32_t ob = (kk >> 2) * (kSub * 128) + (kk & 3) * 32;
-                tc_mma_f16(tmem + kColS + sb * kSub, desc_add(kd_k, oa), desc_add(qd_k, ob), id_s,
-                           kk > 0 ? 1u : 0u);
-                tc_mma_f16(tmem + kFuColDp, desc_add(vd_k, oa), desc_add(dod_k, ob), id_s,
-                           kk > 0 ? 1u : 0u);
-              }
-              tc_commit(&bars[FU_SFULL0 + sb]);
-              ++ga;
-              ++ia;
-              progressed = true;
-            }
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t oa = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+            const uint32_t ob = (kk >> 2) * (kSub * 128) + (kk & 3) * 32;
+            tc_mma_f16(tmem + kColS + sb * kSub, desc_add(kd_k, oa), desc_add(qd_k, ob), id_s,
+                       kk > 0 ? 1u : 0u);
+            tc_mma_f16(tmem + kFuColDp, desc_add(vd_k, oa), desc_add(dod_k, ob), id_s,
+                       kk > 0 ? 1u : 0u);
           }
-          // B: dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T of the oldest pending sub-tile,
-          // once its P^T / dS^T are written (PFULL) and dQ^T(gb - 1) was read out (DQEMPTY).
-          // The item's first one overwrites the dV / dK accumulators: the previous item's
-          // epilogue must have read them (EPI).
-          if (ib < ia) {
-            const uint32_t pb = gb & 1;
-            if ((ib > 0 || n_items == 0 || mbar_test(&bars[FU_EPI], (n_items - 1) & 1)) &&
-                (gb == 0 || mbar_test(&bars[FU_DQEMPTY], (gb - 1) & 1)) &&
-                mbar_test(&bars[FU_PFULL0 + pb], (gb >> 1) & 1)) {
-              tc_fence_after();
-              const uint32_t st = gb % kFuStages;
-              const uint64_t qd_mn = smem_desc(smem_u32(sm + L::kQD + st * L::kStage), kSub * 128, 1024);
-              const uint64_t dod_mn = desc_add(qd_mn, kSub * D * 2);
-              const uint32_t colS = kColS + pb * kSub;
+          tc_commit(&bars[FU_SFULL0 + sb]);
+        }
+        if (!ok) break;
+        tc_commit(&bars[FU_KVEMPTY]);  // this thread's last MMA of the item has read K / V
+      }
+    }
+  } else if (warp == kFuBWarp) {
+    // B blocks: dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T of every sub-tile, in order, once
+    // its P^T / dS^T are written (PFULL) and dQ^T(gb - 1) was read out (DQEMPTY).  The item's
+    // first one overwrites the dV / dK accumulators: the previous item's epilogue must have
+    // read them (EPI).
+    if (lane == 0) {
+      constexpr uint32_t id_acc = idesc_f16(kRows, D, BF16, false, true);
+      // dQ^T = K^T dS^T: A (head dim x keys) and B (keys x query rows) both MN-major
+      constexpr uint32_t id_dq = idesc_f16(kRows, kSub, BF16, true, true);
+      const uint64_t kd_mn = smem_desc(smem_u32(sm + L::kK), kRows * 128, 1024);
+      const uint64_t dsd0_mn = smem_desc(smem_u32(sm + L::kDsT), kSub * 128, 1024);
+      uint32_t gb = 0, jk = 0, n_items = 0;
+      bool ok = true;
+      for (uint32_t w = 0; ok; ++w) {
+        WorkEntry e;
+        if (!(ok = ring_get(ring, &bars[FU_WFULL0], &bars[FU_WEMPTY0], w, e, a.status))) break;
+        if (e.item < 0) break;
+        const int n = e.end - e.begin;
+        if (n == 0) continue;
+        // K is an operand of the dQ^T MMAs: the item's K / V tiles are in place
+        if (!(ok = mbar_wait(&bars[FU_KVFULL], jk & 1, a.status))) break;
+        ++jk;
+        for (int ib = 0; ib < n && ok; ++ib, ++gb) {
+          const uint32_t pb = gb & 1;
+          ok = (ib > 0 || n_items == 0 || mbar_wait(&bars[FU_EPI], (n_items - 1) & 1, a.status)) &&
+               (gb == 0 || mbar_wait(&bars[FU_DQEMPTY], (gb - 1) & 1, a.status)) &&
+               mbar_wait(&bars[FU_PFULL0 + pb], (gb >> 1) & 1, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t st = gb % kFuStages;
+          const uint64_t qd_mn = smem_desc(smem_u32(sm + L::kQD + st * L::kStage), kSub * 128, 1024);
+          const uint64_t dod_mn = desc_add(qd_mn, kSub * D * 2);
+          const uint32_t colS = kColS + pb * kSub;
 #pragma unroll
-              for (int kk = 0; kk < kSub / 16; ++kk) {
-                const uint32_t acc = (ib > 0 || kk > 0) ? 1u : 0u;
-                const uint32_t pcol = colS + (kk >> 1) * 32 + (kk & 1) * 8;  // P^T, then dS^T + 16
-                tc_mma_f16_ts(tmem + kColAcc, tmem + pcol, desc_add(dod_mn, kk * 16 * 128), id_acc, acc);
-                tc_mma_f16_ts(tmem + kColAcc + D, tmem + pcol + 16, desc_add(qd_mn, kk * 16 * 128), id_acc,
-                              acc);
-              }
-              const uint64_t dsd_mn = desc_add(dsd0_mn, pb * L::kDsTBytes);
+          for (int kk = 0; kk < kSub / 16; ++kk) {
+            const uint32_t acc = (ib > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t pcol = colS + (kk >> 1) * 32 + (kk & 1) * 8;  // P^T, then dS^T + 16
+            tc_mma_f16_ts(tmem + kColAcc, tmem + pcol, desc_add(dod_mn, kk * 16 * 128), id_acc, acc);
+            tc_mma_f16_ts(tmem + kColAcc + D, tmem + pcol + 16, desc_add(qd_mn, kk * 16 * 128), id_acc,
+                          acc);
+          }
+          const uint64_t dsd_mn = desc_add(dsd0_mn, pb * L::kDsTBytes);
 #pragma unroll
-              for (int kk = 0; kk < kRows / 16; ++kk)
-                tc_mma_f16(tmem + kFuColDq, desc_add(kd_mn, kk * 16 * 128),
-                           desc_add(dsd_mn, kk * 16 * 128), id_dq, kk > 0 ? 1u : 0u);
-              tc_commit(&bars[FU_DQFULL0 + pb]);
-              ++gb;
-              ++ib;
-              progressed = true;
-            }
-          }
-          if (progressed) {
-            idle_since = clock64();
-          } else if (clock64() - idle_since > (1ll << 31)) {
-            raise_status(a.status, kStatusWaitTimeout);
-            ok = false;
-            break;
-          }
+          for (int kk = 0; kk < kRows / 16; ++kk)
+            tc_mma_f16(tmem + kFuColDq, desc_add(kd_mn, kk * 16 * 128),
+                       desc_add(dsd_mn, kk * 16 * 128), id_dq, kk > 0 ? 1u : 0u);
+          tc_commit(&bars[FU_DQFULL0 + pb]);
+          tc_commit(&bars[FU_SFREE0 + pb]);  // S^T buffer pb (P^T / dS^T) is read
         }
         if (!ok) break;
         tc_commit(&bars[FU_KVEMPTY]);  // the last dQ^T MMA has read K
@@ -1455,7 +1467,7 @@ int launch_fused_t(const AttnParams& p, cudaStream_t stream) {
   a.partials = pp.partials;
   auto kern = a.dbias ? bwd_fused_sm100_kernel<BF16, true> : bwd_fused_sm100_kernel<BF16, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FuLayout::kAlloc);
-  kern<<<(unsigned)ctas, kBwdThreads, FuLayout::kAlloc, stream>>>(a);
+  kern<<<(unsigned)ctas, kFuThreads, FuLayout::kAlloc, stream>>>(a);
   rc = check_launch("bwd_fused_sm100_kernel");
   if (rc) return rc;
   rc = launch_dkdv_reduce(p, pp, ctas, stream);
