@@ -1009,10 +1009,11 @@ __global__ void __launch_bounds__(kFuThreads, 1) bwd_fused_sm100_kernel(const __
         ++jk;
         for (int i = 0; i < n && ok; ++i, ++ga) {
           const uint32_t st = ga % kFuStages, ph = (ga / kFuStages) & 1, sb = ga & 1;
-          // the dP^T buffer once sub-tile ga - 1's group has read it, the S^T buffer once
-          // B(ga - 2) has completed, the sub-tile's Q / dO stage once loaded
-          ok = (ga == 0 || mbar_wait(&bars[FU_DPFREE], (ga - 1) & 1, a.status)) &&
-               (ga < 2 || mbar_wait(&bars[FU_SFREE0 + sb], ((ga - 2) >> 1) & 1, a.status)) &&
+          // S^T once B(ga - 2) has released its buffer and the sub-tile's Q / dO stage is
+          // loaded; dP^T once sub-tile ga - 1's group has read the single dP^T buffer.  That
+          // group frees it halfway through its elementwise pass, so issuing the S^T MMAs first
+          // leaves only the dP^T half of the block on the next sub-tile's critical path.
+          ok = (ga < 2 || mbar_wait(&bars[FU_SFREE0 + sb], ((ga - 2) >> 1) & 1, a.status)) &&
                mbar_wait(&bars[FU_QFULL0 + st], ph, a.status);
           if (!ok) break;
           tc_fence_after();
@@ -1024,6 +1025,13 @@ __global__ void __launch_bounds__(kFuThreads, 1) bwd_fused_sm100_kernel(const __
             const uint32_t ob = (kk >> 2) * (kSub * 128) + (kk & 3) * 32;
             tc_mma_f16(tmem + kColS + sb * kSub, desc_add(kd_k, oa), desc_add(qd_k, ob), id_s,
                        kk > 0 ? 1u : 0u);
+          }
+          if (!(ok = ga == 0 || mbar_wait(&bars[FU_DPFREE], (ga - 1) & 1, a.status))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t oa = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+            const uint32_t ob = (kk >> 2) * (kSub * 128) + (kk & 3) * 32;
             tc_mma_f16(tmem + kFuColDp, desc_add(vd_k, oa), desc_add(dod_k, ob), id_s,
                        kk > 0 ? 1u : 0u);
           }
