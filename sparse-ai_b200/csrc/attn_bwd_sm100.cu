@@ -991,7 +991,7 @@ __global__ void __launch_bounds__(kFuThreads, 1) bwd_fused_sm100_kernel(const __
     // each issue while the tensor pipe is busy (~72-82 cycles per MMA here, traced), so one
     // thread issuing both kinds left the pipe idle through every wait, fence and commit
     // between its blocks (~54 % of each sub-tile).  The two threads meet only through
-    // mbarriers: A(j) writes S^T buffer j & 1, which B(j - 2) read (SFREE).
+    // mbarriers: A(j) writes S^T buffer j & 1, which B(j - 2)'s dV / dK MMAs read (SFREE).
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16(kRows, kSub, BF16, false, false);
       // base descriptors (K-major for S^T / dP^T); per-MMA tiles by desc_add
@@ -1082,13 +1082,15 @@ __global__ void __launch_bounds__(kFuThreads, 1) bwd_fused_sm100_kernel(const __
             tc_mma_f16_ts(tmem + kColAcc + D, tmem + pcol + 16, desc_add(qd_mn, kk * 16 * 128), id_acc,
                           acc);
           }
+          // S^T buffer pb (P^T / dS^T) is read once these complete: the dQ^T MMAs below take
+          // dS^T from shared memory, so A(gb + 2) need not wait for them
+          tc_commit(&bars[FU_SFREE0 + pb]);
           const uint64_t dsd_mn = desc_add(dsd0_mn, pb * L::kDsTBytes);
 #pragma unroll
           for (int kk = 0; kk < kRows / 16; ++kk)
             tc_mma_f16(tmem + kFuColDq, desc_add(kd_mn, kk * 16 * 128),
                        desc_add(dsd_mn, kk * 16 * 128), id_dq, kk > 0 ? 1u : 0u);
           tc_commit(&bars[FU_DQFULL0 + pb]);
-          tc_commit(&bars[FU_SFREE0 + pb]);  // S^T buffer pb (P^T / dS^T) is read
         }
         if (!ok) break;
         tc_commit(&bars[FU_KVEMPTY]);  // the last dQ^T MMA has read K
@@ -1235,24 +1237,23 @@ __global__ void __launch_bounds__(kFuThreads, 1) bwd_fused_sm100_kernel(const __
         // one barrier per sub-tile parity: this group saw the phase before last of its own
         if (!(ok = mbar_wait_warp(&bars[FU_DQFULL0 + sb], sph, a.status))) break;
         tc_fence_after();
-        // by 32-column halves (registers); the buffer is released after the second read
         const int rows = (int)min((int64_t)kSub, a.N - q0);
         float* stg = reinterpret_cast<float*>(sm + L::kQD + st * L::kStage);
 #pragma unroll
-        for (int hq = 0; hq < 2; ++hq) {
-          float dq[32];
-          tmem_ld32(lane_addr + kFuColDq + hq * 32, dq);
-          tmem_wait_ld();
-          if (hq == 1) {
-            tc_fence_before();
-            mbar_arrive(&bars[FU_DQEMPTY]);
-          }
-          // dQ^T -> fp32 rows [q][d] over the stage's Q/dO tiles (B of this sub-tile, their
-          // last reader, has completed: DQFULL), added into the accumulator by one bulk
-          // reduction performed at L2
+        // both halves first, so that the buffer (which B of the next sub-tile overwrites) goes
+        // back after two loads; then dQ^T -> fp32 rows [q][d] over the stage's Q/dO tiles (B of
+        // this sub-tile, their last reader, has completed: DQFULL), added into the accumulator
+        // by one bulk reduction performed at L2
+        float dq0[32], dq1[32];
+        tmem_ld32(lane_addr + kFuColDq, dq0);
+        tmem_ld32(lane_addr + kFuColDq + 32, dq1);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[FU_DQEMPTY]);
 #pragma unroll
-          for (int r = 0; r < 32; ++r) stg[(hq * 32 + r) * D + rl] = dq[r];
-        }
+        for (int r = 0; r < 32; ++r) stg[r * D + rl] = dq0[r];
+#pragma unroll
+        for (int r = 0; r < 32; ++r) stg[(32 + r) * D + rl] = dq1[r];
         fence_proxy_async_smem();
         if (!(ok = group_sync())) break;
         if (leader) {
