@@ -255,7 +255,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     };
     auto resolve = [&](int idx) -> WorkEntry {
       if (idx >= n_entries) return no_work();
-      if (natural) return whole((S.first_static ? (int64_t)gridDim.x : 0) + idx);
+      if (natural) {  // every queued item weighs natural - 1 tiles: no count to load
+        const int64_t item = (S.first_static ? (int64_t)gridDim.x : 0) + idx;
+        return item < S.items ? WorkEntry{(int)item, 0, natural - 1, -1} : no_work();
+      }
       return S.queue[idx];
     };
     WorkEntry e_next{};
@@ -268,8 +271,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
     }
     const int spb = (int)(a.RB / kT);  // key tiles per list entry
     uint32_t kq = 0;                   // key tiles pushed
-    bool ok = true;
-    for (uint32_t w = 0; ok; ++w) {
+    bool ok = true, batch = false;
+    uint32_t w = 0;  // ring entries pushed
+    for (; ok; ++w) {
       WorkEntry e{};
       e.item = __shfl_sync(0xffffffffu, e_next.item, 0);
       e.begin = __shfl_sync(0xffffffffu, e_next.begin, 0);
@@ -342,7 +346,80 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_sm100_kernel(const __grid_
           planner_ready = true;
           n_entries = S.header->n_entries;
           natural = S.header->natural;
-          e_next = resolve(atomicAdd(&S.header->counter, 1));
+          // every remaining item the same weight, within one list entry: batches below
+          batch = natural > 0 && natural - 1 <= spb;
+          if (!batch) e_next = resolve(atomicAdd(&S.header->counter, 1));
+        }
+      }
+      if (__shfl_sync(0xffffffffu, batch ? 1 : 0, 0)) {
+        ++w;
+        break;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, batch ? 1 : 0, 0) && ok) {
+      // Uniform small items (very sparse lists, e.g. one key tile per query tile): one queue
+      // atomic per kBatch items, taken a batch ahead, and the batch's indices, list entries
+      // and biases decoded by kBatch lanes at once, so that a CTA's scheduler is not the
+      // serial bottleneck (atomic, index decode, list load per item) of one-tile items.
+      // Batches of 4 (up to 8 items held per CTA) left a longer tail at the end of the queue
+      // than they saved: 98.4 % forward 0.064 -> 0.069 ms, against 0.063 with 2.
+      constexpr int kBatch = 2;
+      const int64_t base = (int64_t)gridDim.x;  // natural order: entry k is item grid + k
+      const int wu = __shfl_sync(0xffffffffu, natural - 1, 0);
+      const int n_ent = __shfl_sync(0xffffffffu, n_entries, 0);
+      int idx = 0;
+      if (lane == 0) idx = atomicAdd(&S.header->counter, kBatch);
+      idx = __shfl_sync(0xffffffffu, idx, 0);
+      while (ok && idx < n_ent) {
+        int idx_nx = 0;
+        if (lane == 0) idx_nx = atomicAdd(&S.header->counter, kBatch);
+        ItemInfo itj{};
+        int kbj = 0;
+        float bbj = 0.f;
+        if (lane < kBatch && idx + lane < n_ent) {
+          itj = item_info(a, base + idx + lane);
+          if (wu > 0) {
+            kbj = a.lists[itj.row_id * a.list_stride];
+            if (a.bias)
+              bbj = load_any_f32(a.bias, a.bias_dtype, itj.z * a.bs[0] + itj.h * a.bs[1] + itj.qb * a.bs[2]) *
+                    kLog2e;
+          }
+        }
+        for (int jj = 0; jj < kBatch && ok && idx + jj < n_ent; ++jj, ++w) {
+          const int z = __shfl_sync(0xffffffffu, (int)itj.z, jj), h = __shfl_sync(0xffffffffu, (int)itj.h, jj);
+          const int hk = __shfl_sync(0xffffffffu, (int)itj.hk, jj);
+          const int q_start = __shfl_sync(0xffffffffu, (int)itj.q_start, jj);
+          const int kb = __shfl_sync(0xffffffffu, kbj, jj);
+          const float b2 = __shfl_sync(0xffffffffu, bbj, jj);
+          if (lane == 0) {
+            const uint32_t slot = w % kRing;
+            ok = mbar_wait(&bars[B_WEMPTY0 + slot], ((w / kRing) & 1) ^ 1, a.status);
+            if (ok) {
+              ring[slot] = WorkEntry{(int)(base + idx + jj), 0, wu, -1};
+              pos[slot] = ItemPos{z, h, hk, q_start};
+              mbar_arrive(&bars[B_WFULL0 + slot]);
+              if (wu > 0)
+                for (int c = 0; c < D / 64; ++c) tma_prefetch_4d(&a.tm_q, c * 64, q_start, h, z);
+            }
+            for (int tt = 0; tt < wu && ok; ++tt, ++kq) {
+              const uint32_t ks_slot = kq % kKeyRing;
+              ok = mbar_wait(&bars[B_KEYEMPTY0 + ks_slot], ((kq / kKeyRing) & 1) ^ 1, a.status);
+              if (ok) {
+                keys[ks_slot] = TileKey{(int)((int64_t)kb * a.RB + (int64_t)tt * kT), b2, hk, z};
+                mbar_arrive(&bars[B_KEYFULL0 + ks_slot]);
+              }
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+        }
+        idx = __shfl_sync(0xffffffffu, idx_nx, 0);
+      }
+      // the terminating entry ends every role's loop
+      if (ok && lane == 0) {
+        const uint32_t slot = w % kRing;
+        if (mbar_wait(&bars[B_WEMPTY0 + slot], ((w / kRing) & 1) ^ 1, a.status)) {
+          ring[slot] = no_work();
+          mbar_arrive(&bars[B_WFULL0 + slot]);
         }
       }
     }

@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
       a.plan.header->counter = 0;
       a.plan.header->n_entries = a.items > a.skip ? a.items - a.skip : 0;
       a.plan.header->n_split = 0;
-      a.plan.header->natural = 1;
+      a.plan.header->natural = 1 + s_wmax;  // nonzero; the forward reads the weight back
     }
     return;
   }

@@ -34,7 +34,8 @@ struct PlanHeader {
   int counter;    // next entry to hand out (atomic)
   int n_entries;
   int n_split;
-  int natural;    // 1: no queue was written, entry k is item skip + k (all weights equal)
+  int natural;    // 0: the queue holds the entries; 1 + w: no queue was written, entry k is
+                  // item skip + k, and every such item weighs w
 };
 
 // Bytes of planner workspace for `items` items and `ctas` persistent CTAs.  Split chunks need
