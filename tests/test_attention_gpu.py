@@ -375,3 +375,32 @@ def test_fused_backward(Z, H, Hkv, N, RB, depth, causal, sink, local, with_bias,
 def _native_status():
     from ultrametric import _native as nat
     return nat.read_device_status()
+
+
+@pytest.mark.parametrize("RB,empty,with_bias", [(128, False, True), (256, False, False), (128, True, False)])
+def test_forward_uniform_one_entry_items(RB, empty, with_bias):
+    """Every query block lists exactly one key block (or none): the forward planner finds every
+    work item of the same weight, and the kernel's scheduler then takes the items two per queue
+    atomic and decodes them on two lanes -- with a soft bias, with two key tiles per list entry
+    (route block 256), and with every item empty.  256 items, so most come from the queue."""
+    Z, H, Hkv, D, N = 1, 16, 4, 128, 2048
+    NB = N // RB
+    gen = torch.Generator().manual_seed(RB + 11)
+    q = randn((Z, H, N, D), gen).to(torch.bfloat16)
+    k = randn((Z, Hkv, N, D), gen).to(torch.bfloat16)
+    v = randn((Z, Hkv, N, D), gen).to(torch.bfloat16)
+    m = torch.zeros(Z, H, NB, NB, dtype=torch.bool)
+    if not empty:
+        cols = torch.randint(0, NB, (H, NB), generator=gen)
+        for h in range(H):
+            m[0, h, torch.arange(NB), cols[h]] = True
+    bl = build_block_lists_from_mask(m.to(DEV))
+    bias = randn(bl.lists.shape, gen).to(DEV) if with_bias else None
+    out, lse = block_list_attention(q.to(DEV), k.to(DEV), v.to(DEV), bl, route_block=RB,
+                                    is_causal=False, return_lse=True, soft_block_bias=bias)
+    if empty:
+        assert (out == 0).all() and torch.isneginf(lse).all()
+        return
+    ref, ref_lse = oracle_fwd(q.float(), k.float(), v.float(), bl, RB, False, bias=bias)
+    assert_half_close(out, ref, "out")
+    lse_close(lse, ref_lse, 2e-2)
