@@ -33,8 +33,9 @@
 //               one-tile item: its owner alone.  O / l is staged (128B swizzle) in the P
 //               buffer and written by TMA tile stores; LSE.
 // Work item = (query tile of 128 rows, z, h).  With a planner workspace the items come
-// heaviest-first from the device-built queue (one atomic per item); without one, round-robin
-// with late (heavier, under causal masking) query tiles first.
+// heaviest-first from the device-built queue (one atomic per item; two per atomic when every
+// item has the same weight of at most one list entry); without one, round-robin with late
+// (heavier, under causal masking) query tiles first.
 #include <string>
 #include <type_traits>
 
