@@ -5,7 +5,8 @@
 // pairs, dS = P * (dP - Delta), dQ = scale * dS K, dK = scale * dS^T Q, dV = P^T dO,
 // d_soft_bias[z,h,qb,t] = sum of the unscaled dS of the block pair.
 //
-// Both kernels are persistent (one CTA per SM, work from the planner's queue), 10 warps:
+// Both kernels are persistent (one CTA per SM, work from the planner's queue), 10 warps (the
+// fused kernel below adds an eleventh, its second MMA issuer):
 //   warp 0      TMA producer (and the queue fetch)
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
 //   warps 2-9   two elementwise groups of 4 warps (a thread owns one TMEM lane = row); the
@@ -819,10 +820,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
 // them, half hc of the 64 query columns holding P^T at [32 hc, 32 hc + 16) and dS^T at
 // [32 hc + 16, 32 hc + 32)), one dP^T buffer at 128, one dQ^T buffer at 192, dV at 256 and dK
 // at 384.  The tensor pipe runs A(j+1) B(j) A(j+2) B(j+1) ..., where A(j) = S^T, dP^T of
-// sub-tile j and B(j) = dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T.  A(j) needs the dP^T
-// buffer read out by sub-tile j-1's group (DPFREE, signalled right after its first TMEM
-// loads) and B(j) needs dQ^T(j-1) read out (DQEMPTY): both happen while the other block
-// runs, so neither waits for a drain.
+// sub-tile j and B(j) = dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T.  A(j)'s S^T MMAs need
+// B(j-2)'s dV / dK MMAs to have read the S^T buffer (SFREE), its dP^T MMAs the dP^T buffer
+// read out by sub-tile j-1's group (DPFREE); B(j) needs dQ^T(j-1) read out (DQEMPTY).
 //
 // The owning group reads dQ^T out of TMEM and stages it as fp32 rows [q][d] in the
 // sub-tile's own Q/dO stage, whose tiles B(j) no longer needs once DQFULL(j) fired; one
@@ -831,9 +831,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_dkdv_sm100_kernel(const __
 // reduction has read it.  dQ's summation order depends on timing, so it is not bitwise
 // reproducible from run to run; the two-kernel path is.
 //
-// The MMA thread polls its barriers (mbarrier.test_wait, never a blocking try_wait) and
-// issues whichever block is ready; the accumulating MMAs stay in sub-tile order, so dV and
-// dK sums are reproducible.
+// Two threads issue the MMAs: warp 1 the A blocks, warp kFuBWarp the B blocks, each in
+// sub-tile order (a thread issuing tcgen05.mma is held at each issue while the tensor pipe is
+// busy, so one thread for both left the pipe idle through its waits and commits).  The
+// accumulating MMAs all come from one thread in sub-tile order, so dV and dK sums are
+// reproducible.
 
 constexpr int kFuStages = 4;
 
